@@ -1,0 +1,204 @@
+/*
+ * w4.h -- C ABI of libw4, the B200 (sm_100a) weight-only quantized linear
+ * library (GPTQ int4 W4A16, NVFP4, epilogue quant).
+ *
+ * Conventions for every entry point:
+ *   - All tensor pointers are DEVICE pointers unless the comment says otherwise.
+ *     Row-major, densely packed, shapes as documented.  fp16 / bf16 values are
+ *     passed as uint16_t bit patterns.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Work is
+ *     enqueued asynchronously; the call returns once it is launched.
+ *   - Nothing is allocated inside a call.  Scratch space, where needed, is the
+ *     caller's `workspace` buffer, sized by the matching *_workspace_bytes().
+ *   - Argument errors are reported synchronously (W4_ERR_INVALID /
+ *     W4_ERR_UNSUPPORTED) before anything is launched; launch failures are
+ *     W4_ERR_CUDA.  w4_last_error() gives a one-line reason (thread-local).
+ *   - Calls are reentrant; concurrent calls on different streams must not
+ *     share a workspace.
+ *
+ * Each entry point names the reference (hotschmoe/xe2x2) interface it replaces,
+ * as file:line within that project.  The reference's kernels are file-local
+ * `sycl::event launch(sycl::queue&, ...)` functions driven by their own
+ * run_shape(); its only operator-level API is the external PyTorch op
+ * `torch.ops._xpu_C.nvfp4_gemm_w4a16[_f8scale]` (kernels/nvfp4/bench_nvfp4_m1.py:67,88).
+ */
+#ifndef W4_H
+#define W4_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define W4_ABI_VERSION 1
+
+/* Status codes.  The reference harness exits 0 ok / 1 numeric fail / 2 bad
+ * shape or usage (kernels/esimd_dpas/dpas_s4_gptq.cpp:171-176,282-289); here a
+ * bad shape is W4_ERR_INVALID and a legal-but-unsupported one W4_ERR_UNSUPPORTED. */
+enum w4_status {
+    W4_OK = 0,
+    W4_ERR_INVALID = 1,
+    W4_ERR_UNSUPPORTED = 2,
+    W4_ERR_CUDA = 3,
+    W4_ERR_TIMEOUT = 4,
+    W4_ERR_NCCL = 5
+};
+
+/* Element types. */
+enum w4_dtype {
+    W4_F16 = 0,
+    W4_BF16 = 1,
+    W4_F32 = 2,
+    W4_E4M3 = 3, /* fp8 e4m3fn (bias 7, max 448, no inf) */
+    W4_S8 = 4
+};
+
+/* NVFP4 packed-weight layouts (two E2M1 nibbles per byte, low nibble = even k). */
+enum w4_nvfp4_layout {
+    W4_NVFP4_KN = 0, /* u8 [K/2, N], N contiguous: kernels/nvfp4/nibble_lut_sc.cpp:77-83 */
+    W4_NVFP4_NK = 1  /* u8 [N, K/2], K contiguous: the external op's w with stride(0)==1,
+                        kernels/nvfp4/bench_nvfp4_m1.py:58-61 */
+};
+
+/* NVFP4 activation handling. */
+enum w4_act_mode {
+    W4_ACT_W4A16 = 0, /* activations stay bf16; weights dequantised on the fly */
+    W4_ACT_NVFP4 = 1  /* activations quantised to NVFP4 per 16-block (w4_nvfp4_quant_act) */
+};
+
+int w4_abi_version(void);
+const char *w4_status_string(int status);
+const char *w4_last_error(void);
+
+/* ===================================================================== */
+/* GPTQ int4                                                              */
+/* ===================================================================== */
+
+/* Dequantise a GPTQ checkpoint matrix to fp32, bit-exact:
+ *   w[k,n] = float(scales[g,n]) * (q[k,n] - zero[g,n]),  g = g_idx ? g_idx[k] : k/group_size
+ * qweight i32 [K/8,N] (8 nibbles LSB-first along K), qzeros i32 [K/gs,N/8]
+ * (LSB-first along N) or NULL (symmetric, zero = 8), scales f16 [K/gs,N],
+ * g_idx i32 [K] or NULL.  zero = stored + zero_offset (1 = GPTQ v1 "+1", 0 = v2).
+ * Replaces the host unpack of kernels/nvfp4/gptq_s4_dump.py:61-73,106-114. */
+int w4_gptq_dequant(const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
+                    const int32_t *g_idx, int K, int N, int group_size, int zero_offset,
+                    float *w, void *stream);
+
+/* act_order load-time repack: perm = stable argsort(g_idx) (i32 [K]) and
+ * qweight_out[K/8,N] whose row j is row perm[j] of qweight, so every group is a
+ * contiguous run of group_size rows.  Requires every group to hold exactly
+ * group_size rows (GPTQ act_order does).  qweight_out must not alias qweight.
+ * Replaces the g_idx check of kernels/nvfp4/gptq_s4_dump.py:119-122. */
+int w4_gptq_repack_act_order(const int32_t *qweight, const int32_t *g_idx, int K, int N,
+                             int group_size, int32_t *qweight_out, int32_t *perm_out,
+                             void *stream);
+
+/* Workspace needed by w4_gptq_gemm for these arguments (0 if none). */
+size_t w4_gptq_workspace_bytes(int M, int N, int K, int group_size, int has_perm, int c_dtype);
+
+/* W4A16 GPTQ GEMM:  C[m,n] = sum_k A[m,k'] * w[k,n]   (fp32 accumulate)
+ * a: [M,K] f16 or bf16 (a_dtype); qweight/qzeros/scales as in w4_gptq_dequant
+ * with groups contiguous (k/group_size); perm: i32 [K] from
+ * w4_gptq_repack_act_order (then k' = perm[k]) or NULL (k' = k).
+ * c: [M,N] of c_dtype W4_F16 / W4_BF16 / W4_F32, or W4_E4M3 with the per-row
+ * scale written to row_scale f32 [M] (c = e4m3(y / row_scale), row_scale =
+ * max|y_row| / 448, the epilogue_quant contract of
+ * kernels/epilogue_quant/rmsnorm_epilogue.cpp:56-69 with qmax 448).
+ * Shapes: K % 32 == 0, N % 32 == 0, group_size % 32 == 0, K % group_size == 0, M >= 1.
+ * Replaces launch() of kernels/esimd_dpas/dpas_s4_gptq_sc.cpp:146-233 (decode)
+ * and kernels/esimd_dpas/dpas_s4_gptq_db48.cpp:148-246 (prefill). */
+int w4_gptq_gemm(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
+                 const uint16_t *scales, const int32_t *perm, void *c, int c_dtype,
+                 float *row_scale, int M, int N, int K, int group_size, int zero_offset,
+                 void *workspace, size_t workspace_bytes, void *stream);
+
+/* The reference kernel's own contract, same arguments in the same order as
+ * launch(q, ad, bd, asd, sd, cd, rows, cols, dk) of
+ * kernels/esimd_dpas/dpas_s4_gptq_sc.cpp:146-149:
+ *   C[r,c] = half( sum_g float(s32_g) * a_scale[r] * float(b_scale[g,c]) ),
+ *   s32_g  = sum_{k in g} A_s4[r,k] * B_s4[k,c]   (group size 128, exact)
+ * a_s4 u8 [rows, dk/2] (pack_a, low nibble = even k), b_s4 u8 [dk/2, cols]
+ * (pack_b), a_scale f32 [rows], b_scale f16 [dk/128, cols], c f16 [rows, cols].
+ * Bit-exact with the reference host oracle (dpas_s4_gptq_sc.cpp:273-288). */
+int w4_gptq_gemm_s4a(const uint8_t *a_s4, const uint8_t *b_s4, const float *a_scale,
+                     const uint16_t *b_scale, uint16_t *c, int rows, int cols, int dk,
+                     void *stream);
+
+/* ===================================================================== */
+/* NVFP4                                                                  */
+/* ===================================================================== */
+
+/* Dequantise to fp32, bit-exact: w[k,n] = (e2m1(nib[k,n]) * s[k/16,n]) * global.
+ * scale: [K/16,N] of scale_dtype W4_E4M3 (then global_scale is an f32[1] device
+ * pointer) or W4_BF16 (folded scale; global_scale must be NULL).
+ * Replaces unpack_host of kernels/nvfp4/nibble_lut_sc.cpp:85-92 with the block
+ * scales of the external op (kernels/nvfp4/bench_nvfp4_m1.py:84-88). */
+int w4_nvfp4_dequant(const uint8_t *w, int layout, const void *scale, int scale_dtype,
+                     const float *global_scale, int K, int N, float *out, void *stream);
+
+/* Quantise bf16 activations to NVFP4, bit-exact with the host definition:
+ *   sf = e4m3(amax16 / (6 * a_global)),  code = e2m1(a / (e4m3(sf) * a_global))
+ * a: bf16 [M,K]; a_global: f32[1] device pointer (the tensor decode scale);
+ * codes u8 [M,K/2] (low nibble = even k); sf u8 [M,K/16]. */
+int w4_nvfp4_quant_act(const uint16_t *a, int M, int K, const float *a_global,
+                       uint8_t *codes, uint8_t *sf, void *stream);
+
+size_t w4_nvfp4_workspace_bytes(int M, int N, int K, int act_mode, int c_dtype);
+
+/* NVFP4 GEMM:  C[m,n] = (sum_k A[m,k] * (e2m1(w[k,n]) * s[k/16,n])) * global
+ * a: bf16 [M,K]; w, layout, scale, scale_dtype, global_scale as in
+ * w4_nvfp4_dequant; act_mode W4_ACT_W4A16 (a used as is) or W4_ACT_NVFP4 (a
+ * quantised per w4_nvfp4_quant_act with a_global first; needs workspace);
+ * c, c_dtype, row_scale as in w4_gptq_gemm.  Weights must be in the W4_NVFP4_NK
+ * layout (w4_nvfp4_repack_kn_to_nk converts the other).  Shapes: K % 128 == 0,
+ * N % 32 == 0, M >= 1.
+ * Replaces the external op nvfp4_gemm_w4a16(x, w, None, scale, 16) /
+ * nvfp4_gemm_w4a16_f8scale(x, w, None, bscale, gscale, 16)
+ * (kernels/nvfp4/bench_nvfp4_m1.py:67,88) and launch() of
+ * kernels/nvfp4/nibble_lut_sc.cpp:198-290. */
+int w4_nvfp4_gemm(const void *a, const uint8_t *w, int layout, const void *scale,
+                  int scale_dtype, const float *global_scale, int act_mode,
+                  const float *a_global, void *c, int c_dtype, float *row_scale, int M, int N,
+                  int K, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Load-time transpose of packed weights from the reference kernel's layout
+ * u8 [K/2, N] (kernels/nvfp4/nibble_lut_sc.cpp:77-83) to the K-contiguous
+ * u8 [N, K/2] that w4_nvfp4_gemm reads.  Block scales keep their [K/16, N]
+ * layout.  w_nk must not alias w_kn. */
+int w4_nvfp4_repack_kn_to_nk(const uint8_t *w_kn, int K, int N, uint8_t *w_nk, void *stream);
+
+/* The reference LUT kernel's own contract, same arguments in the same order as
+ * launch(q, ad, pd, asd, bsd, cd, rows, cols, dk) of
+ * kernels/nvfp4/nibble_lut_sc.cpp:198-201:
+ *   C[r,c] = half( (sum_k A_s8[r,k] * q[k,c]) * a_s[r] * b_s[c] ),  q = 2*e2m1
+ * a s8 [rows, dk], packed u8 [dk/2, cols], a_s f32 [rows], b_s f32 [cols],
+ * c f16 [rows, cols].  Bit-exact with nibble_lut_sc.cpp:319-330. */
+int w4_nvfp4_lut_gemm_s8a(const int8_t *a, const uint8_t *packed, const float *a_s,
+                          const float *b_s, uint16_t *c, int rows, int cols, int dk,
+                          void *stream);
+
+/* ===================================================================== */
+/* epilogue quant                                                         */
+/* ===================================================================== */
+
+/* Fused RMSNorm (gamma = 1) + symmetric per-row s8 quantisation:
+ *   inv = 1/sqrt(mean(x^2) + eps); y = x*inv; s = max|y|/127 (1 if 0);
+ *   q = clamp(rint(y/s), -127, 127)
+ * x f16 [M,K], q s8 [M,K], scale f32 [M].  Same arguments as launch_fused(q, x,
+ * q, s, m, k) of kernels/epilogue_quant/rmsnorm_epilogue.cpp:118-119 plus eps
+ * (the reference fixes 1e-6, :23). */
+int w4_rmsnorm_quant_s8(const uint16_t *x, int8_t *q, float *scale, int M, int K, float eps,
+                        void *stream);
+
+/* Per-row fp8-E4M3 cast of a finished [M,N] tensor (f16 / bf16 / f32):
+ * s = max|y_row|/448 (1 if 0), q = e4m3_rne_satfinite(y/s).  The same cast
+ * the GEMMs apply in their epilogue when c_dtype == W4_E4M3. */
+int w4_rowscale_fp8(const void *y, int y_dtype, uint8_t *q, float *row_scale, int M, int N,
+                    void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* W4_H */

@@ -1,0 +1,47 @@
+"""Generate the golden fixtures in this folder from the reference's own code.
+
+Run in a container where the reference checkout is present (it is not needed at
+test time):
+
+    python tests/golden/make_golden.py /path/to/hotschmoe-xe2x2
+
+It imports kernels/nvfp4/gptq_s4_dump.py (numpy only; its main() is guarded) and
+records, for seeded random packed words, the outputs of the reference's
+checkpoint unpackers unpack_i32_nibbles_first (qweight, :69-73) and
+unpack_i32_nibbles_last (qzeros, :61-66), plus the reference's s4 view u - 8
+(:114).  tests/test_oracle_golden.py replays them against the C oracle.
+"""
+from __future__ import annotations
+
+import importlib.util
+import os
+import sys
+
+import numpy as np
+
+
+def main(ref_root: str) -> None:
+    path = os.path.join(ref_root, "kernels", "nvfp4", "gptq_s4_dump.py")
+    spec = importlib.util.spec_from_file_location("gptq_s4_dump", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+
+    rng = np.random.default_rng(20261201)
+    out = {}
+    for name, (rows, cols) in {"a": (16, 40), "b": (64, 24)}.items():
+        qw = rng.integers(-2**31, 2**31, size=(rows, cols), dtype=np.int64).astype(np.int32)
+        qz = rng.integers(-2**31, 2**31, size=(rows // 8 + 1, cols // 8 + 1), dtype=np.int64).astype(np.int32)
+        out[f"{name}_qweight"] = qw
+        out[f"{name}_unpack_first"] = mod.unpack_i32_nibbles_first(qw).astype(np.int16)
+        out[f"{name}_s4"] = (mod.unpack_i32_nibbles_first(qw).astype(np.int16) - 8).astype(np.int16)
+        out[f"{name}_qzeros"] = qz
+        out[f"{name}_unpack_last"] = mod.unpack_i32_nibbles_last(qz).astype(np.int16)
+    here = os.path.dirname(os.path.abspath(__file__))
+    np.savez_compressed(os.path.join(here, "gptq_unpack.npz"), **out)
+    print("wrote", os.path.join(here, "gptq_unpack.npz"), sorted(out))
+
+
+if __name__ == "__main__":
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <reference checkout root>")
+    main(sys.argv[1])

@@ -1,0 +1,88 @@
+"""C-ABI surface checks that need no GPU: the library loads, exports every
+entry point declared in include/w4.h, and rejects bad arguments synchronously
+(before any CUDA call)."""
+import ctypes
+
+import pytest
+
+from xe2x2_b200 import _lib as L
+
+
+def test_library_exports_every_header_symbol():
+    lib = L.lib()
+    names = L.header_symbols()
+    assert len(names) >= 15
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, f"missing exports: {missing}"
+    # and every header symbol has a ctypes signature in the binding
+    assert set(names) <= set(L._SIGS), set(names) - set(L._SIGS)
+
+
+def test_version_and_status_strings():
+    lib = L.lib()
+    assert lib.w4_abi_version() == 1
+    assert lib.w4_status_string(L.W4_OK) == b"ok"
+    assert lib.w4_status_string(L.W4_ERR_UNSUPPORTED) == b"unsupported shape or option"
+
+
+def _fake(addr=0x10000):
+    return ctypes.c_void_p(addr)
+
+
+def test_gptq_gemm_rejects_bad_arguments_without_gpu():
+    lib = L.lib()
+    # null qweight
+    rc = lib.w4_gptq_gemm(_fake(), L.W4_F16, None, None, _fake(), None, _fake(), L.W4_F16, None,
+                          1, 64, 128, 128, 1, None, 0, None)
+    assert rc == L.W4_ERR_INVALID and b"qweight" in lib.w4_last_error()
+    # K not a multiple of group size
+    rc = lib.w4_gptq_gemm(_fake(), L.W4_F16, _fake(), None, _fake(), None, _fake(), L.W4_F16, None,
+                          1, 64, 200, 128, 1, None, 0, None)
+    assert rc == L.W4_ERR_INVALID
+    # M < 1 (the reference harness rejects m < 1, dpas_s4_gptq_sc.cpp:239)
+    rc = lib.w4_gptq_gemm(_fake(), L.W4_F16, _fake(), None, _fake(), None, _fake(), L.W4_F16, None,
+                          0, 64, 128, 128, 1, None, 0, None)
+    assert rc == L.W4_ERR_INVALID
+    # ragged N (the reference requires n % tile == 0)
+    rc = lib.w4_gptq_gemm(_fake(), L.W4_F16, _fake(), None, _fake(), None, _fake(), L.W4_F16, None,
+                          1, 40, 128, 128, 1, None, 0, None)
+    assert rc == L.W4_ERR_UNSUPPORTED
+    # fp8 output without a row-scale buffer
+    rc = lib.w4_gptq_gemm(_fake(), L.W4_F16, _fake(), None, _fake(), None, _fake(), L.W4_E4M3, None,
+                          1, 64, 128, 128, 1, None, 0, None)
+    assert rc == L.W4_ERR_INVALID
+    # misaligned activation pointer
+    rc = lib.w4_gptq_gemm(_fake(0x10002), L.W4_F16, _fake(), None, _fake(), None, _fake(), L.W4_F16,
+                          None, 1, 64, 128, 128, 1, None, 0, None)
+    assert rc == L.W4_ERR_INVALID
+    # workspace too small for act_order
+    rc = lib.w4_gptq_gemm(_fake(), L.W4_F16, _fake(), None, _fake(), _fake(), _fake(), L.W4_F16, None,
+                          1, 64, 128, 128, 1, None, 0, None)
+    assert rc == L.W4_ERR_INVALID and b"workspace" in lib.w4_last_error()
+
+
+def test_workspace_sizes():
+    lib = L.lib()
+    assert lib.w4_gptq_workspace_bytes(16, 4096, 4096, 128, 0, L.W4_F16) == 0
+    assert lib.w4_gptq_workspace_bytes(16, 4096, 4096, 128, 1, L.W4_F16) >= 16 * 4096 * 2
+    assert lib.w4_gptq_workspace_bytes(16, 4096, 4096, 128, 0, L.W4_E4M3) >= 16 * 4096 * 4
+    assert lib.w4_nvfp4_workspace_bytes(16, 5120, 5120, L.W4_ACT_W4A16, L.W4_BF16) == 0
+
+
+def test_nvfp4_rejects_bad_arguments_without_gpu():
+    lib = L.lib()
+    # e4m3 scales need a tensor scale
+    rc = lib.w4_nvfp4_gemm(_fake(), _fake(), L.W4_NVFP4_NK, _fake(), L.W4_E4M3, None, L.W4_ACT_W4A16, None,
+                           _fake(), L.W4_BF16, None, 1, 64, 128, None, 0, None)
+    assert rc == L.W4_ERR_INVALID
+    # the GEMM reads the NK layout only
+    rc = lib.w4_nvfp4_gemm(_fake(), _fake(), L.W4_NVFP4_KN, _fake(), L.W4_E4M3, _fake(), L.W4_ACT_W4A16,
+                           None, _fake(), L.W4_BF16, None, 1, 64, 128, None, 0, None)
+    assert rc == L.W4_ERR_UNSUPPORTED and b"repack" in lib.w4_last_error()
+    rc = lib.w4_rmsnorm_quant_s8(_fake(), _fake(), _fake(), 1, 12, 1e-6, None)
+    assert rc == L.W4_ERR_INVALID
+
+
+def test_oracle_library_loads():
+    import oracle as O
+    assert O.e2m1_value(7) == 6.0

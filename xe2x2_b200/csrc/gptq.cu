@@ -1,0 +1,426 @@
+// gptq.cu -- GPTQ int4 kernels for sm_100a.
+//
+// Checkpoint layout (kernels/nvfp4/gptq_s4_dump.py:106-114 of the reference):
+//   qweight i32 [K/8, N]   eight 4-bit codes per word, LSB-first along K
+//   qzeros  i32 [K/gs, N/8] eight codes per word, LSB-first along N (or absent)
+//   scales  f16 [K/gs, N]
+// The kernels read this layout as stored; nothing is repacked for the GEMM
+// except the optional act_order row permutation.
+#include <cooperative_groups.h>
+
+#include "w4_common.cuh"
+#include "w4_internal.h"
+
+namespace cg = cooperative_groups;
+
+namespace w4 {
+
+// ---------------------------------------------------------------------------
+// Dequantisation (bit-exact): one thread per qweight word -> 8 fp32 outputs.
+// ---------------------------------------------------------------------------
+__global__ void gptq_dequant_kernel(const int32_t *__restrict__ qweight,
+                                    const int32_t *__restrict__ qzeros,
+                                    const uint16_t *__restrict__ scales,
+                                    const int32_t *__restrict__ g_idx, int K, int N, int gs,
+                                    int zero_offset, float *__restrict__ w) {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    const int kw = blockIdx.y;
+    if (n >= N) return;
+    const uint32_t word = (uint32_t)qweight[(size_t)kw * N + n];
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        const int k = kw * 8 + s;
+        const int g = g_idx ? g_idx[k] : k / gs;
+        int z = 8;
+        if (qzeros) z = (int)(((uint32_t)qzeros[(size_t)g * (N / 8) + (n >> 3)] >> (4 * (n & 7))) & 15u) + zero_offset;
+        const int d = (int)((word >> (4 * s)) & 15u) - z;
+        w[(size_t)k * N + n] = __fmul_rn((float)d, f16_bits_to_f(scales[(size_t)g * N + n]));
+    }
+}
+
+int gptq_dequant(const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
+                 const int32_t *g_idx, int K, int N, int gs, int zero_offset, float *w,
+                 cudaStream_t st) {
+    dim3 block(256), grid((N + 255) / 256, K / 8);
+    gptq_dequant_kernel<<<grid, block, 0, st>>>(qweight, qzeros, scales, g_idx, K, N, gs,
+                                                zero_offset, w);
+    W4_LAUNCH_CHECK();
+    return W4_OK;
+}
+
+// ---------------------------------------------------------------------------
+// act_order repack.  perm = stable argsort(g_idx) by counting sort (one block,
+// one thread per group scanning K in order), then row gather of the codes.
+// ---------------------------------------------------------------------------
+__global__ void act_order_perm_kernel(const int32_t *__restrict__ g_idx, int K, int gs,
+                                      int32_t *__restrict__ perm) {
+    __shared__ int bad;
+    if (threadIdx.x == 0) bad = 0;
+    __syncthreads();
+    const int ngrp = K / gs;
+    for (int g = threadIdx.x; g < ngrp; g += blockDim.x) {
+        int pos = g * gs, cnt = 0;
+        for (int k = 0; k < K; ++k) {
+            if (g_idx[k] == g) {
+                if (cnt < gs) perm[pos + cnt] = k;
+                ++cnt;
+            }
+        }
+        if (cnt != gs) atomicExch(&bad, 1);
+    }
+    __syncthreads();
+    // A valid permutation never starts with -1: it marks an invalid g_idx.
+    if (threadIdx.x == 0 && bad) perm[0] = -1;
+}
+
+__global__ void permute_rows_kernel(const int32_t *__restrict__ qweight,
+                                    const int32_t *__restrict__ perm, int N,
+                                    int32_t *__restrict__ out) {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    const int kw = blockIdx.y;
+    if (n >= N) return;
+    uint32_t word = 0;
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        const int src = perm[kw * 8 + s];
+        const uint32_t v = ((uint32_t)qweight[(size_t)(src >> 3) * N + n] >> (4 * (src & 7))) & 15u;
+        word |= v << (4 * s);
+    }
+    out[(size_t)kw * N + n] = (int32_t)word;
+}
+
+int gptq_repack_act_order(const int32_t *qweight, const int32_t *g_idx, int K, int N, int gs,
+                          int32_t *qweight_out, int32_t *perm_out, cudaStream_t st) {
+    act_order_perm_kernel<<<1, 256, 0, st>>>(g_idx, K, gs, perm_out);
+    W4_LAUNCH_CHECK();
+    // Load-time call: read the validity marker back synchronously.
+    int32_t first = 0;
+    W4_CUDA_TRY(cudaMemcpyAsync(&first, perm_out, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    W4_CUDA_TRY(cudaStreamSynchronize(st));
+    W4_REQUIRE(first >= 0, W4_ERR_UNSUPPORTED,
+               "act_order: every group must hold exactly group_size=%d rows", gs);
+    dim3 block(256), grid((N + 255) / 256, K / 8);
+    permute_rows_kernel<<<grid, block, 0, st>>>(qweight, perm_out, N, qweight_out);
+    W4_LAUNCH_CHECK();
+    return W4_OK;
+}
+
+// A_perm[m, k] = A[m, perm[k]] (16-bit elements)
+__global__ void gather_cols_kernel(const uint16_t *__restrict__ a, const int32_t *__restrict__ perm,
+                                   int K, uint16_t *__restrict__ out) {
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    const int m = blockIdx.y;
+    if (k >= K) return;
+    out[(size_t)m * K + k] = a[(size_t)m * K + perm[k]];
+}
+
+int gather_cols(const uint16_t *a, const int32_t *perm, int M, int K, uint16_t *out,
+                cudaStream_t st) {
+    dim3 block(256), grid((K + 255) / 256, M);
+    gather_cols_kernel<<<grid, block, 0, st>>>(a, perm, K, out);
+    W4_LAUNCH_CHECK();
+    return W4_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Decode GEMM (M small): warp-level, HBM-bound.
+//
+// A warp owns 32 output columns and a range of qweight words (4 words = 32 k
+// per step).  Lane (g = lane/4, t = lane%4) loads 16 B = 4 adjacent columns of
+// word row (kbase + t): for each t the 8 lanes of that t read one contiguous
+// 128-byte line.  The 32 codes in the lane's registers become the A operand of
+// m16n8k16 MMAs with the WEIGHT COLUMNS as MMA rows (swap-AB) and the tokens
+// as MMA columns:
+//   m-tile mt: MMA row g   <- column 4g + 2mt,  MMA row g+8 <- column 4g + 2mt + 1
+//   k-step s : MMA k-slots (2t, 2t+1) <- codes (2s, 2s+4) of word kbase+t,
+//              k-slots (2t+8, 2t+9) <- codes (2s+1, 2s+5)
+// Any consistent relabelling of k is legal for a dot product; this one lets a
+// single lop3 turn code pair (j, j+4) of a word into two 16-bit floats
+// (magic + q) and the activations follow with two byte-permutes per pair.
+// (q - zero) is formed exactly in bf16/f16, products are exact, fp32
+// accumulation runs per group and is scaled by the fp16 group scale when the
+// group ends -- the s32-partial-then-scale structure of the reference kernel
+// (kernels/esimd_dpas/dpas_s4_gptq_sc.cpp:178-218) with real activations.
+//
+// Split-K: the 8 warps of a CTA take consecutive k ranges and reduce through
+// shared memory; when the grid has too few column blocks to fill the GPU, a
+// thread-block cluster of KS CTAs splits K further and the cluster leader sums
+// the partials over distributed shared memory.  No global scratch, one launch.
+// ---------------------------------------------------------------------------
+template <typename T> struct Deq;
+template <> struct Deq<__nv_bfloat16> {
+    static constexpr uint32_t kMagic = 0x43004300u;  // bf16 128.0 | q in mantissa bits 0-3
+    static __device__ __forceinline__ uint32_t zconst(int z) {
+        const uint32_t h = __bfloat16_as_ushort(__float2bfloat16_rn(128.0f + (float)z));
+        return h | (h << 16);
+    }
+    static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
+        __nv_bfloat162 r = __hsub2(*reinterpret_cast<__nv_bfloat162 *>(&a),
+                                   *reinterpret_cast<__nv_bfloat162 *>(&b));
+        return *reinterpret_cast<uint32_t *>(&r);
+    }
+};
+template <> struct Deq<__half> {
+    static constexpr uint32_t kMagic = 0x64006400u;  // f16 1024.0 | q in mantissa bits 0-3
+    static __device__ __forceinline__ uint32_t zconst(int z) {
+        const uint32_t h = __half_as_ushort(__float2half_rn(1024.0f + (float)z));
+        return h | (h << 16);
+    }
+    static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
+        __half2 r = __hsub2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b));
+        return *reinterpret_cast<uint32_t *>(&r);
+    }
+};
+
+constexpr int kGemvWarps = 8;
+
+template <typename T, int NT, int D>
+__global__ void __launch_bounds__(kGemvWarps * 32)
+gptq_gemv_kernel(const T *__restrict__ A, const int32_t *__restrict__ qweight,
+                 const int32_t *__restrict__ qzeros, const uint16_t *__restrict__ scales,
+                 void *__restrict__ C, int c_dtype, int M, int N, int K, int gs, int zero_offset,
+                 int words_per_part, int ks) {
+    constexpr int NE = 2 * NT * 4;  // accumulator floats per lane
+    __shared__ float red[kGemvWarps][NE][32];
+    __shared__ float part[NE * 32];
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int n_base = blockIdx.x * 32 + 4 * g;
+    const int tok0 = blockIdx.z * 8 * NT;
+    const int KW = K / 8, gw = gs / 8;
+    const int p = blockIdx.y * kGemvWarps + warp;
+    const int w_begin = min(p * words_per_part, KW);
+    const int w_end = min(w_begin + words_per_part, KW);
+    const int nsteps = (w_end - w_begin) / 4;
+
+    float facc[2][NT][4], gacc[2][NT][4];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int b = 0; b < NT; ++b)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) facc[a][b][i] = gacc[a][b][i] = 0.f;
+
+    const int32_t *wptr = qweight + (size_t)(w_begin + t) * N + n_base;
+    uint4 wbuf[D];
+#pragma unroll
+    for (int d = 0; d < D; ++d)
+        if (d < nsteps) wbuf[d] = ld_stream_v4(wptr + (size_t)(4 * d) * N);
+
+    int cur_g = -1;
+    uint32_t zc[4];
+    float sc[4];
+    auto load_group = [&](int grp) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            int z = 8;
+            if (qzeros)
+                z = (int)(((uint32_t)__ldg(qzeros + (size_t)grp * (N / 8) + ((n_base + c) >> 3)) >>
+                           (4 * ((n_base + c) & 7))) & 15u) + zero_offset;
+            zc[c] = Deq<T>::zconst(z);
+        }
+        const uint2 s4 = __ldg(reinterpret_cast<const uint2 *>(scales + (size_t)grp * N + n_base));
+        sc[0] = f16_bits_to_f((uint16_t)(s4.x & 0xFFFF));
+        sc[1] = f16_bits_to_f((uint16_t)(s4.x >> 16));
+        sc[2] = f16_bits_to_f((uint16_t)(s4.y & 0xFFFF));
+        sc[3] = f16_bits_to_f((uint16_t)(s4.y >> 16));
+    };
+    auto flush = [&]() {
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                facc[mt][nt][0] += gacc[mt][nt][0] * sc[2 * mt];
+                facc[mt][nt][1] += gacc[mt][nt][1] * sc[2 * mt];
+                facc[mt][nt][2] += gacc[mt][nt][2] * sc[2 * mt + 1];
+                facc[mt][nt][3] += gacc[mt][nt][3] * sc[2 * mt + 1];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) gacc[mt][nt][i] = 0.f;
+            }
+    };
+
+    for (int i0 = 0; i0 < nsteps; i0 += D) {
+#pragma unroll
+        for (int d = 0; d < D; ++d) {
+            const int step = i0 + d;
+            if (step < nsteps) {
+                const uint4 wv = wbuf[d];
+                if (step + D < nsteps) wbuf[d] = ld_stream_v4(wptr + (size_t)(4 * (step + D)) * N);
+                const int kw = w_begin + 4 * step;  // word of lane t is kw + t
+                const int grp = kw / gw;
+                if (grp != cur_g) {
+                    if (cur_g >= 0) flush();
+                    cur_g = grp;
+                    load_group(grp);
+                }
+                // activation fragments: token tok0 + nt*8 + g, elements 8(kw+t)..+7
+                uint32_t bf[NT][2][2];
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    const int tok = tok0 + nt * 8 + g;
+                    uint4 x = make_uint4(0, 0, 0, 0);
+                    if (tok < M) x = ld_nc_v4(A + (size_t)tok * K + (size_t)(kw + t) * 8);
+                    bf[nt][0][0] = __byte_perm(x.x, x.z, 0x5410);
+                    bf[nt][0][1] = __byte_perm(x.x, x.z, 0x7632);
+                    bf[nt][1][0] = __byte_perm(x.y, x.w, 0x5410);
+                    bf[nt][1][1] = __byte_perm(x.y, x.w, 0x7632);
+                }
+                const uint32_t wc[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt) {
+                    const uint32_t lo = wc[2 * mt], hi = wc[2 * mt + 1];
+#pragma unroll
+                    for (int s = 0; s < 2; ++s) {
+                        const uint32_t a0 = Deq<T>::sub(lop3_and_or(lo >> (8 * s), 0x000F000Fu, Deq<T>::kMagic), zc[2 * mt]);
+                        const uint32_t a1 = Deq<T>::sub(lop3_and_or(hi >> (8 * s), 0x000F000Fu, Deq<T>::kMagic), zc[2 * mt + 1]);
+                        const uint32_t a2 = Deq<T>::sub(lop3_and_or(lo >> (8 * s + 4), 0x000F000Fu, Deq<T>::kMagic), zc[2 * mt]);
+                        const uint32_t a3 = Deq<T>::sub(lop3_and_or(hi >> (8 * s + 4), 0x000F000Fu, Deq<T>::kMagic), zc[2 * mt + 1]);
+#pragma unroll
+                        for (int nt = 0; nt < NT; ++nt)
+                            mma_16816<T>(gacc[mt][nt], a0, a1, a2, a3, bf[nt][s][0], bf[nt][s][1]);
+                    }
+                }
+            }
+        }
+    }
+    if (cur_g >= 0) flush();
+
+    // ---- reduce: warps -> CTA (shared) -> cluster leader (distributed shared) ----
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) red[warp][(mt * NT + nt) * 4 + i][lane] = facc[mt][nt][i];
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < NE * 32; idx += blockDim.x) {
+        const int e = idx >> 5, l = idx & 31;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kGemvWarps; ++w) v += red[w][e][l];
+        part[idx] = v;
+    }
+    bool leader = true;
+    if (ks > 1) {
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();
+        leader = cluster.block_rank() == 0;
+        if (leader) {
+            for (int idx = threadIdx.x; idx < NE * 32; idx += blockDim.x) {
+                float v = part[idx];
+                for (int r = 1; r < ks; ++r) v += cluster.map_shared_rank(part, r)[idx];
+                red[0][0][idx] = v;  // red is free again; NE*32 floats fit in red[0..]
+            }
+        }
+        cluster.sync();
+    } else {
+        __syncthreads();
+    }
+    if (!leader) return;
+    if (ks > 1) __syncthreads();
+    const float *src = (ks > 1) ? &red[0][0][0] : part;
+    for (int idx = threadIdx.x; idx < NE * 32; idx += blockDim.x) {
+        const int e = idx >> 5, l = idx & 31;
+        const int mt = e / (NT * 4), nt = (e / 4) % NT, i = e & 3;
+        const int col = blockIdx.x * 32 + 4 * (l >> 2) + 2 * mt + (i >> 1);
+        const int tok = tok0 + nt * 8 + 2 * (l & 3) + (i & 1);
+        if (tok < M && col < N) {
+            const float v = src[idx];
+            const size_t o = (size_t)tok * N + col;
+            if (c_dtype == W4_F32) reinterpret_cast<float *>(C)[o] = v;
+            else if (c_dtype == W4_BF16) reinterpret_cast<__nv_bfloat16 *>(C)[o] = __float2bfloat16_rn(v);
+            else reinterpret_cast<__half *>(C)[o] = __float2half_rn(v);
+        }
+    }
+}
+
+template <typename T, int NT>
+static int launch_gemv_t(const T *a, const int32_t *qweight, const int32_t *qzeros,
+                         const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs,
+                         int zero_offset, cudaStream_t st) {
+    constexpr int D = 4;
+    const int nsm = num_sms();
+    const int ncol = N / 32;
+    const int mblocks = (M + 8 * NT - 1) / (8 * NT);
+    const int KW = K / 8;
+    // Cluster split-K when the column blocks alone cannot fill ~2 CTAs per SM,
+    // keeping at least one step (4 words) of work per warp.
+    int ks = 1;
+    while (ks < 8 && ncol * mblocks * ks < 2 * nsm && KW / (kGemvWarps * ks * 2) >= 4) ks *= 2;
+    int wpp = (KW + kGemvWarps * ks - 1) / (kGemvWarps * ks);
+    wpp = (wpp + 3) & ~3;
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ncol, ks, mblocks);
+    cfg.blockDim = dim3(kGemvWarps * 32);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = ks;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = ks > 1 ? 1 : 0;
+    W4_CUDA_TRY(cudaLaunchKernelEx(&cfg, gptq_gemv_kernel<T, NT, D>, a, qweight, qzeros, scales, c,
+                                   c_dtype, M, N, K, gs, zero_offset, wpp, ks));
+    return W4_OK;
+}
+
+int gptq_gemv(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
+              const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs,
+              int zero_offset, cudaStream_t st) {
+    if (a_dtype == W4_BF16) {
+        const auto *ap = static_cast<const __nv_bfloat16 *>(a);
+        if (M <= 8) return launch_gemv_t<__nv_bfloat16, 1>(ap, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+        if (M <= 16) return launch_gemv_t<__nv_bfloat16, 2>(ap, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+        return launch_gemv_t<__nv_bfloat16, 4>(ap, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    }
+    const auto *ap = static_cast<const __half *>(a);
+    if (M <= 8) return launch_gemv_t<__half, 1>(ap, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    if (M <= 16) return launch_gemv_t<__half, 2>(ap, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    return launch_gemv_t<__half, 4>(ap, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+}
+
+// ---------------------------------------------------------------------------
+// Reference-formula kernel (dpas_s4_gptq_sc.cpp:146-233 contract, host oracle
+// :273-288).  One thread per output; the group partial is an exact s32 and the
+// fp32 epilogue uses the reference's operation order without contraction, so
+// the f16 result is bit-identical to the host oracle.
+// ---------------------------------------------------------------------------
+__global__ void gptq_s4a_kernel(const uint8_t *__restrict__ a, const uint8_t *__restrict__ b,
+                                const float *__restrict__ a_scale,
+                                const uint16_t *__restrict__ s, uint16_t *__restrict__ c,
+                                int rows, int cols, int dk) {
+    const int col = blockIdx.x * blockDim.x + threadIdx.x;
+    const int r = blockIdx.y;
+    if (col >= cols) return;
+    const int ngrp = dk / 128;
+    const uint8_t *arow = a + (size_t)r * (dk / 2);
+    const float as = a_scale[r];
+    float acc = 0.f;
+    for (int g = 0; g < ngrp; ++g) {
+        int32_t s32 = 0;
+        for (int kk = 0; kk < 128; kk += 2) {
+            const int k = g * 128 + kk;
+            const uint32_t ab = arow[k / 2];
+            const uint32_t bb = b[(size_t)(k / 2) * cols + col];
+            const int a0 = ((int)(ab << 28)) >> 28, a1 = ((int)(ab << 24)) >> 28;
+            const int b0 = ((int)(bb << 28)) >> 28, b1 = ((int)(bb << 24)) >> 28;
+            s32 += a0 * b0 + a1 * b1;
+        }
+        acc = __fadd_rn(acc, __fmul_rn(__fmul_rn((float)s32, as), f16_bits_to_f(s[(size_t)g * cols + col])));
+    }
+    c[(size_t)r * cols + col] = __half_as_ushort(__float2half_rn(acc));
+}
+
+int gptq_s4a(const uint8_t *a, const uint8_t *b, const float *a_scale, const uint16_t *s,
+             uint16_t *c, int rows, int cols, int dk, cudaStream_t st) {
+    dim3 block(128), grid((cols + 127) / 128, rows);
+    gptq_s4a_kernel<<<grid, block, 0, st>>>(a, b, a_scale, s, c, rows, cols, dk);
+    W4_LAUNCH_CHECK();
+    return W4_OK;
+}
+
+}  // namespace w4

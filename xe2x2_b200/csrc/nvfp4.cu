@@ -1,0 +1,388 @@
+// nvfp4.cu -- NVFP4 (E2M1 nibbles, one E4M3 scale per 16 K, fp32 tensor scale)
+// kernels for sm_100a.
+//
+// Packing (kernels/nvfp4/nibble_lut_sc.cpp:77-92 of the reference): two codes per
+// byte along K, low nibble = even k.  Two layouts: KN = u8 [K/2, N] (the
+// reference kernel's own) and NK = u8 [N, K/2] (the external operator's w with
+// stride(0)==1, kernels/nvfp4/bench_nvfp4_m1.py:58-61).  Block scales are
+// [K/16, N] in both.
+#include <cooperative_groups.h>
+
+#include "w4_common.cuh"
+#include "w4_internal.h"
+
+namespace cg = cooperative_groups;
+
+namespace w4 {
+
+__device__ __forceinline__ uint32_t nib_at(const uint8_t *w, int layout, int K, int N, int k,
+                                           int n) {
+    const uint8_t p = (layout == W4_NVFP4_KN) ? w[(size_t)(k >> 1) * N + n]
+                                              : w[(size_t)n * (K / 2) + (k >> 1)];
+    return (k & 1) ? (uint32_t)(p >> 4) : (uint32_t)(p & 15);
+}
+
+__device__ __forceinline__ float block_scale_f(const void *scale, int scale_dtype, int N, int k,
+                                               int n) {
+    const size_t i = (size_t)(k >> 4) * N + n;
+    if (scale_dtype == W4_E4M3) return e4m3_to_f(reinterpret_cast<const uint8_t *>(scale)[i]);
+    return __bfloat162float(__ushort_as_bfloat16(reinterpret_cast<const uint16_t *>(scale)[i]));
+}
+
+// ---- dequant (bit-exact): out[k,n] = (e2m1 * s) * global ----
+__global__ void nvfp4_dequant_kernel(const uint8_t *__restrict__ w, int layout,
+                                     const void *__restrict__ scale, int scale_dtype,
+                                     const float *__restrict__ global_scale, int K, int N,
+                                     float *__restrict__ out) {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    const int k = blockIdx.y;
+    if (n >= N) return;
+    const float g = global_scale ? *global_scale : 1.0f;
+    const float v = __fmul_rn(e2m1_to_f(nib_at(w, layout, K, N, k, n)),
+                              block_scale_f(scale, scale_dtype, N, k, n));
+    out[(size_t)k * N + n] = __fmul_rn(v, g);
+}
+
+int nvfp4_dequant(const uint8_t *w, int layout, const void *scale, int scale_dtype,
+                  const float *global_scale, int K, int N, float *out, cudaStream_t st) {
+    dim3 block(256), grid((N + 255) / 256, K);
+    nvfp4_dequant_kernel<<<grid, block, 0, st>>>(w, layout, scale, scale_dtype, global_scale, K,
+                                                 N, out);
+    W4_LAUNCH_CHECK();
+    return W4_OK;
+}
+
+// ---- activation quantiser: one thread per 16-element block ----
+__global__ void nvfp4_quant_act_kernel(const uint16_t *__restrict__ a, int M, int K,
+                                       const float *__restrict__ a_global,
+                                       uint8_t *__restrict__ codes, uint8_t *__restrict__ sf) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    const int nb = K / 16;
+    if (b >= M * nb) return;
+    const int m = b / nb, kb = b % nb;
+    const uint16_t *x = a + (size_t)m * K + (size_t)kb * 16;
+    const uint4 u0 = ld_nc_v4(x), u1 = ld_nc_v4(x + 8);
+    const uint32_t wv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        v[2 * i] = __uint_as_float(wv[i] << 16);
+        v[2 * i + 1] = __uint_as_float(wv[i] & 0xFFFF0000u);
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    const float g = *a_global;
+    const uint32_t s = f_to_e4m3(__fdiv_rn(amax, __fmul_rn(6.0f, g)));
+    const float sdec = __fmul_rn(e4m3_to_f(s), g);
+    sf[(size_t)m * nb + kb] = (uint8_t)s;
+    uint32_t packed[2] = {0, 0};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const uint32_t c = (sdec != 0.f) ? f_to_e2m1(__fdiv_rn(v[i], sdec)) : 0u;
+        packed[i >> 3] |= c << (4 * (i & 7));
+    }
+    *reinterpret_cast<uint2 *>(codes + (size_t)m * (K / 2) + (size_t)kb * 8) =
+        make_uint2(packed[0], packed[1]);
+}
+
+int nvfp4_quant_act(const uint16_t *a, int M, int K, const float *a_global, uint8_t *codes,
+                    uint8_t *sf, cudaStream_t st) {
+    const int nblk = M * (K / 16);
+    nvfp4_quant_act_kernel<<<(nblk + 255) / 256, 256, 0, st>>>(a, M, K, a_global, codes, sf);
+    W4_LAUNCH_CHECK();
+    return W4_OK;
+}
+
+// ---- reference LUT kernel contract (nibble_lut_sc.cpp:198-290, oracle :319-330) ----
+// Integer products summed in fp32 are exact (|acc| < 2^24), and the epilogue
+// keeps the host's operation order, so the f16 result is bit-identical.
+__global__ void nvfp4_lut_s8a_kernel(const int8_t *__restrict__ a, const uint8_t *__restrict__ p,
+                                     const float *__restrict__ a_s, const float *__restrict__ b_s,
+                                     uint16_t *__restrict__ c, int rows, int cols, int dk) {
+    const int col = blockIdx.x * blockDim.x + threadIdx.x;
+    const int r = blockIdx.y;
+    if (col >= cols) return;
+    const int8_t *ar = a + (size_t)r * dk;
+    float acc = 0.f;
+    for (int k = 0; k < dk; k += 2) {
+        const uint32_t byte = p[(size_t)(k / 2) * cols + col];
+        const float q0 = 2.0f * e2m1_to_f(byte & 15), q1 = 2.0f * e2m1_to_f(byte >> 4);
+        acc = __fadd_rn(acc, __fmul_rn((float)ar[k], q0));
+        acc = __fadd_rn(acc, __fmul_rn((float)ar[k + 1], q1));
+    }
+    c[(size_t)r * cols + col] = __half_as_ushort(__float2half_rn(__fmul_rn(__fmul_rn(acc, a_s[r]), b_s[col])));
+}
+
+int nvfp4_lut_s8a(const int8_t *a, const uint8_t *packed, const float *a_s, const float *b_s,
+                  uint16_t *c, int rows, int cols, int dk, cudaStream_t st) {
+    dim3 block(128), grid((cols + 127) / 128, rows);
+    nvfp4_lut_s8a_kernel<<<grid, block, 0, st>>>(a, packed, a_s, b_s, c, rows, cols, dk);
+    W4_LAUNCH_CHECK();
+    return W4_OK;
+}
+
+// ---- load-time layout transpose KN [K/2, N] -> NK [N, K/2] ----
+__global__ void nvfp4_kn_to_nk_kernel(const uint8_t *__restrict__ in, int K, int N,
+                                      uint8_t *__restrict__ out) {
+    __shared__ uint8_t tile[32][33];
+    const int kb0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+    const int tx = threadIdx.x, ty = threadIdx.y;
+    for (int j = ty; j < 32; j += blockDim.y) {
+        const int kb = kb0 + j, n = n0 + tx;
+        tile[j][tx] = (kb < K / 2 && n < N) ? in[(size_t)kb * N + n] : 0;
+    }
+    __syncthreads();
+    for (int j = ty; j < 32; j += blockDim.y) {
+        const int n = n0 + j, kb = kb0 + tx;
+        if (n < N && kb < K / 2) out[(size_t)n * (K / 2) + kb] = tile[tx][j];
+    }
+}
+
+int nvfp4_kn_to_nk(const uint8_t *in, int K, int N, uint8_t *out, cudaStream_t st) {
+    dim3 block(32, 8), grid((N + 31) / 32, (K / 2 + 31) / 32);
+    nvfp4_kn_to_nk_kernel<<<grid, block, 0, st>>>(in, K, N, out);
+    W4_LAUNCH_CHECK();
+    return W4_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Decode GEMM (M small) on the NK layout, bf16 warp MMA, swap-AB.
+//
+// A warp owns 32 output columns; lane (g = lane/4, t = lane%4) streams 16 B of
+// each of the columns n0+g, n0+8+g, n0+16+g, n0+24+g per step of 128 k (lane t
+// holds k 32t..32t+31 of the step, so a quad reads 64 contiguous bytes of a
+// column).  MMA m-tile 0 has rows (g, g+8) = columns (n0+g, n0+8+g), m-tile 1
+// columns (n0+16+g, n0+24+g).  k-step s of lane t covers k = 32t + 4s .. +3:
+// slots (2t, 2t+1) <- k (+0, +1) and (2t+8, 2t+9) <- k (+2, +3), so the
+// activation fragment is 8 contiguous bytes and needs no shuffling.
+//
+// E2M1 -> bf16 is a register lookup: two byte-permutes read the low / high
+// byte of the bf16 pattern of |e2m1| from 8-entry tables held in immediates,
+// a third merges the sign bytes.  The block scale (E4M3 -> bf16, exact) is then
+// applied with one bf16x2 multiply; e2m1 * e4m3 needs at most 6 significant
+// bits, so the weight operand is exact and only the fp32 accumulation rounds.
+// The tensor scale multiplies the fp32 result.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void e2m1x4_to_bf16(uint32_t x, uint32_t &r01, uint32_t &r23) {
+    // |e2m1| in bf16: 0, .5, 1, 1.5 | 2, 3, 4, 6
+    constexpr uint32_t TL0 = 0xC0800000u, TL1 = 0xC0804000u;  // low bytes
+    constexpr uint32_t TH0 = 0x3F3F3F00u, TH1 = 0x40404040u;  // high bytes
+    const uint32_t sel = x & 0x7777u;
+    const uint32_t L = __byte_perm(TL0, TL1, sel);
+    const uint32_t Hp = __byte_perm(TH0, TH1, sel);
+    // sign of nibble i -> bit 7 of byte i: nibbles 1,3 have it at bits 7,15 of x,
+    // nibbles 0,2 at bits 3,11 (bits 7,15 of x << 4)
+    uint32_t sg;
+    asm("prmt.b32 %0, %1, %2, 0x1504;" : "=r"(sg) : "r"(x), "r"(x << 4));
+    const uint32_t H = lop3_and_or(sg, 0x80808080u, Hp);
+    r01 = __byte_perm(L, H, 0x5140);
+    r23 = __byte_perm(L, H, 0x7362);
+}
+
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+    __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162 *>(&a),
+                               *reinterpret_cast<__nv_bfloat162 *>(&b));
+    return *reinterpret_cast<uint32_t *>(&r);
+}
+
+template <int SCALE_DT>
+__device__ __forceinline__ uint32_t load_scale2(const void *scale, size_t i) {
+    uint32_t h;
+    if constexpr (SCALE_DT == W4_E4M3) {
+        const uint32_t b = __ldg(reinterpret_cast<const uint8_t *>(scale) + i);
+        h = __bfloat16_as_ushort(__float2bfloat16_rn(e4m3_to_f(b)));
+    } else {
+        h = __ldg(reinterpret_cast<const uint16_t *>(scale) + i);
+    }
+    return h | (h << 16);
+}
+
+constexpr int kFp4Warps = 8;
+
+template <int NT, int D, int SCALE_DT>
+__global__ void __launch_bounds__(kFp4Warps * 32)
+nvfp4_gemv_nk_kernel(const __nv_bfloat16 *__restrict__ A, const uint8_t *__restrict__ W,
+                     const void *__restrict__ scale, const float *__restrict__ global_scale,
+                     void *__restrict__ C, int c_dtype, int M, int N, int K, int steps_per_part,
+                     int ks) {
+    constexpr int NE = 2 * NT * 4;
+    __shared__ float red[kFp4Warps][NE][32];
+    __shared__ float part[NE * 32];
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int n0 = blockIdx.x * 32;
+    const int tok0 = blockIdx.z * 8 * NT;
+    const int nsteps_total = K / 128;
+    const int p = blockIdx.y * kFp4Warps + warp;
+    const int s_begin = min(p * steps_per_part, nsteps_total);
+    const int s_end = min(s_begin + steps_per_part, nsteps_total);
+    const int nsteps = s_end - s_begin;
+    const size_t kb2 = (size_t)K / 2;
+
+    float acc[2][NT][4];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int b = 0; b < NT; ++b)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[a][b][i] = 0.f;
+
+    // column c in 0..3 of this lane: n0 + g + 8c
+    const uint8_t *wp = W + (size_t)(n0 + g) * kb2 + (size_t)s_begin * 64 + 16 * t;
+    uint4 wbuf[D][4];
+#pragma unroll
+    for (int d = 0; d < D; ++d)
+        if (d < nsteps)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) wbuf[d][c] = ld_stream_v4(wp + (size_t)(8 * c) * kb2 + d * 64);
+
+    for (int i0 = 0; i0 < nsteps; i0 += D) {
+#pragma unroll
+        for (int d = 0; d < D; ++d) {
+            const int step = i0 + d;
+            if (step < nsteps) {
+                uint4 wv[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) wv[c] = wbuf[d][c];
+                if (step + D < nsteps)
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        wbuf[d][c] = ld_stream_v4(wp + (size_t)(8 * c) * kb2 + (size_t)(step + D) * 64);
+                const int kstep = (s_begin + step) * 128;  // first k of this step
+                // block scales: blocks (kstep/16 + 2t + {0,1}) for the 4 columns
+                uint32_t sc[4][2];
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+                        sc[c][h] = load_scale2<SCALE_DT>(scale, (size_t)(kstep / 16 + 2 * t + h) * N + n0 + g + 8 * c);
+                // activations: 32 bf16 per token starting at kstep + 32t
+                uint4 xa[NT][4];
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    const int tok = tok0 + nt * 8 + g;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        xa[nt][q] = (tok < M) ? ld_nc_v4(A + (size_t)tok * K + kstep + 32 * t + 8 * q)
+                                              : make_uint4(0, 0, 0, 0);
+                }
+#pragma unroll
+                for (int s = 0; s < 8; ++s) {
+                    const int q = s >> 1, half = s & 1, h = s >> 2;
+                    uint32_t a01[4], a23[4];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const uint32_t word = (q == 0) ? wv[c].x : (q == 1) ? wv[c].y : (q == 2) ? wv[c].z : wv[c].w;
+                        uint32_t r01, r23;
+                        e2m1x4_to_bf16(half ? (word >> 16) : word, r01, r23);
+                        a01[c] = bf16x2_mul(r01, sc[c][h]);
+                        a23[c] = bf16x2_mul(r23, sc[c][h]);
+                    }
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        const uint4 xv = xa[nt][q];
+                        const uint32_t b0 = half ? xv.z : xv.x, b1 = half ? xv.w : xv.y;
+                        mma_16816<__nv_bfloat16>(acc[0][nt], a01[0], a01[1], a23[0], a23[1], b0, b1);
+                        mma_16816<__nv_bfloat16>(acc[1][nt], a01[2], a01[3], a23[2], a23[3], b0, b1);
+                    }
+                }
+            }
+        }
+    }
+
+    // ---- reduce: warps -> CTA -> cluster leader (distributed shared memory) ----
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) red[warp][(mt * NT + nt) * 4 + i][lane] = acc[mt][nt][i];
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < NE * 32; idx += blockDim.x) {
+        const int e = idx >> 5, l = idx & 31;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kFp4Warps; ++w) v += red[w][e][l];
+        part[idx] = v;
+    }
+    bool leader = true;
+    if (ks > 1) {
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();
+        leader = cluster.block_rank() == 0;
+        if (leader) {
+            for (int idx = threadIdx.x; idx < NE * 32; idx += blockDim.x) {
+                float v = part[idx];
+                for (int r = 1; r < ks; ++r) v += cluster.map_shared_rank(part, r)[idx];
+                red[0][0][idx] = v;
+            }
+        }
+        cluster.sync();
+    } else {
+        __syncthreads();
+    }
+    if (!leader) return;
+    const float gsc = global_scale ? *global_scale : 1.0f;
+    const float *src = (ks > 1) ? &red[0][0][0] : part;
+    for (int idx = threadIdx.x; idx < NE * 32; idx += blockDim.x) {
+        const int e = idx >> 5, l = idx & 31;
+        const int mt = e / (NT * 4), nt = (e / 4) % NT, i = e & 3;
+        const int col = n0 + 16 * mt + 8 * (i >> 1) + (l >> 2);
+        const int tok = tok0 + nt * 8 + 2 * (l & 3) + (i & 1);
+        if (tok < M && col < N) {
+            const float v = src[idx] * gsc;
+            const size_t o = (size_t)tok * N + col;
+            if (c_dtype == W4_F32) reinterpret_cast<float *>(C)[o] = v;
+            else if (c_dtype == W4_BF16) reinterpret_cast<__nv_bfloat16 *>(C)[o] = __float2bfloat16_rn(v);
+            else reinterpret_cast<__half *>(C)[o] = __float2half_rn(v);
+        }
+    }
+}
+
+template <int NT, int SCALE_DT>
+static int launch_nvfp4_gemv_t(const uint16_t *a, const uint8_t *w, const void *scale,
+                               const float *global_scale, void *c, int c_dtype, int M, int N,
+                               int K, cudaStream_t st) {
+    constexpr int D = 2;
+    const int nsm = num_sms();
+    const int ncol = N / 32;
+    const int mblocks = (M + 8 * NT - 1) / (8 * NT);
+    const int nsteps = K / 128;
+    int ks = 1;
+    while (ks < 8 && ncol * mblocks * ks < 2 * nsm && nsteps / (kFp4Warps * ks * 2) >= 1) ks *= 2;
+    const int spp = (nsteps + kFp4Warps * ks - 1) / (kFp4Warps * ks);
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ncol, ks, mblocks);
+    cfg.blockDim = dim3(kFp4Warps * 32);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = ks;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = ks > 1 ? 1 : 0;
+    W4_CUDA_TRY(cudaLaunchKernelEx(&cfg, nvfp4_gemv_nk_kernel<NT, D, SCALE_DT>,
+                                   reinterpret_cast<const __nv_bfloat16 *>(a), w, scale,
+                                   global_scale, c, c_dtype, M, N, K, spp, ks));
+    return W4_OK;
+}
+
+int nvfp4_gemv(const uint16_t *a, const uint8_t *w, int layout, const void *scale,
+               int scale_dtype, const float *global_scale, void *c, int c_dtype, int M, int N,
+               int K, cudaStream_t st) {
+    (void)layout;  // NK only; validated by the caller
+    if (scale_dtype == W4_E4M3) {
+        if (M <= 8) return launch_nvfp4_gemv_t<1, W4_E4M3>(a, w, scale, global_scale, c, c_dtype, M, N, K, st);
+        if (M <= 16) return launch_nvfp4_gemv_t<2, W4_E4M3>(a, w, scale, global_scale, c, c_dtype, M, N, K, st);
+        return launch_nvfp4_gemv_t<4, W4_E4M3>(a, w, scale, global_scale, c, c_dtype, M, N, K, st);
+    }
+    if (M <= 8) return launch_nvfp4_gemv_t<1, W4_BF16>(a, w, scale, global_scale, c, c_dtype, M, N, K, st);
+    if (M <= 16) return launch_nvfp4_gemv_t<2, W4_BF16>(a, w, scale, global_scale, c, c_dtype, M, N, K, st);
+    return launch_nvfp4_gemv_t<4, W4_BF16>(a, w, scale, global_scale, c, c_dtype, M, N, K, st);
+}
+
+}  // namespace w4

@@ -1,0 +1,276 @@
+// w4_api.cu -- the extern "C" boundary of libw4 (include/w4.h).
+//
+// Every entry point validates its arguments on the host, then enqueues on the
+// caller's stream.  Nothing here allocates: scratch comes from the caller's
+// workspace, sized by the *_workspace_bytes() functions.
+#include <mutex>
+#include <vector>
+
+#include "w4_common.cuh"
+#include "w4_internal.h"
+
+namespace w4 {
+
+static thread_local char g_err[512] = "";
+
+void set_error(const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+}
+
+const char *last_error() { return g_err; }
+
+int num_sms() {
+    static std::mutex mu;
+    static std::vector<int> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    std::lock_guard<std::mutex> lk(mu);
+    if ((int)cache.size() <= dev) cache.resize(dev + 1, 0);
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+int nvfp4_kn_to_nk(const uint8_t *in, int K, int N, uint8_t *out, cudaStream_t st);
+
+}  // namespace w4
+
+using w4::aligned;
+
+static inline cudaStream_t S(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+static inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+extern "C" {
+
+int w4_abi_version(void) { return W4_ABI_VERSION; }
+
+const char *w4_status_string(int status) {
+    switch (status) {
+        case W4_OK: return "ok";
+        case W4_ERR_INVALID: return "invalid argument";
+        case W4_ERR_UNSUPPORTED: return "unsupported shape or option";
+        case W4_ERR_CUDA: return "CUDA error";
+        case W4_ERR_TIMEOUT: return "timed out";
+        case W4_ERR_NCCL: return "NCCL error";
+        default: return "unknown status";
+    }
+}
+
+const char *w4_last_error(void) { return w4::last_error(); }
+
+// ------------------------------------------------------------------ GPTQ
+static int check_gptq_common(const int32_t *qweight, const uint16_t *scales, int K, int N,
+                             int group_size) {
+    W4_REQUIRE(qweight && scales, W4_ERR_INVALID, "qweight and scales are required");
+    W4_REQUIRE(K > 0 && N > 0, W4_ERR_INVALID, "K=%d N=%d must be positive", K, N);
+    W4_REQUIRE(group_size > 0 && K % group_size == 0, W4_ERR_INVALID,
+               "K=%d must be a multiple of group_size=%d", K, group_size);
+    W4_REQUIRE(K % 8 == 0 && N % 8 == 0, W4_ERR_INVALID, "K=%d and N=%d must be multiples of 8", K, N);
+    return W4_OK;
+}
+
+int w4_gptq_dequant(const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
+                    const int32_t *g_idx, int K, int N, int group_size, int zero_offset,
+                    float *w, void *stream) {
+    w4::set_error("");
+    int rc = check_gptq_common(qweight, scales, K, N, group_size);
+    if (rc) return rc;
+    W4_REQUIRE(w, W4_ERR_INVALID, "output w is required");
+    return w4::gptq_dequant(qweight, qzeros, scales, g_idx, K, N, group_size, zero_offset, w, S(stream));
+}
+
+int w4_gptq_repack_act_order(const int32_t *qweight, const int32_t *g_idx, int K, int N,
+                             int group_size, int32_t *qweight_out, int32_t *perm_out,
+                             void *stream) {
+    w4::set_error("");
+    W4_REQUIRE(qweight && g_idx && qweight_out && perm_out, W4_ERR_INVALID,
+               "qweight, g_idx, qweight_out and perm_out are required");
+    W4_REQUIRE(qweight != qweight_out, W4_ERR_INVALID, "qweight_out must not alias qweight");
+    W4_REQUIRE(K > 0 && N > 0 && K % 8 == 0 && group_size > 0 && K % group_size == 0,
+               W4_ERR_INVALID, "bad shape K=%d N=%d group_size=%d", K, N, group_size);
+    return w4::gptq_repack_act_order(qweight, g_idx, K, N, group_size, qweight_out, perm_out, S(stream));
+}
+
+size_t w4_gptq_workspace_bytes(int M, int N, int K, int group_size, int has_perm, int c_dtype) {
+    (void)group_size;
+    size_t ws = 0;
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    if (has_perm) ws += align256((size_t)M * K * 2);
+    if (c_dtype == W4_E4M3) ws += align256((size_t)M * N * 4);
+    return ws;
+}
+
+int w4_gptq_gemm(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
+                 const uint16_t *scales, const int32_t *perm, void *c, int c_dtype,
+                 float *row_scale, int M, int N, int K, int group_size, int zero_offset,
+                 void *workspace, size_t workspace_bytes, void *stream) {
+    w4::set_error("");
+    int rc = check_gptq_common(qweight, scales, K, N, group_size);
+    if (rc) return rc;
+    W4_REQUIRE(a && c, W4_ERR_INVALID, "a and c are required");
+    W4_REQUIRE(M >= 1, W4_ERR_INVALID, "M=%d must be >= 1", M);
+    W4_REQUIRE(a_dtype == W4_F16 || a_dtype == W4_BF16, W4_ERR_INVALID, "a_dtype must be f16 or bf16");
+    W4_REQUIRE(c_dtype == W4_F16 || c_dtype == W4_BF16 || c_dtype == W4_F32 || c_dtype == W4_E4M3,
+               W4_ERR_INVALID, "c_dtype must be f16, bf16, f32 or e4m3");
+    W4_REQUIRE(c_dtype != W4_E4M3 || row_scale, W4_ERR_INVALID, "e4m3 output needs row_scale");
+    W4_REQUIRE(K % 32 == 0 && N % 32 == 0 && group_size % 32 == 0, W4_ERR_UNSUPPORTED,
+               "need K %% 32 == 0, N %% 32 == 0, group_size %% 32 == 0 (K=%d N=%d gs=%d)", K, N,
+               group_size);
+    W4_REQUIRE(aligned(a, 16) && aligned(qweight, 16) && aligned(scales, 8), W4_ERR_INVALID,
+               "a and qweight must be 16-byte aligned, scales 8-byte aligned");
+    const size_t need = w4_gptq_workspace_bytes(M, N, K, group_size, perm != nullptr, c_dtype);
+    W4_REQUIRE(workspace_bytes >= need && (need == 0 || workspace), W4_ERR_INVALID,
+               "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+    cudaStream_t st = S(stream);
+    char *ws = static_cast<char *>(workspace);
+    const void *a_eff = a;
+    if (perm) {
+        uint16_t *ap = reinterpret_cast<uint16_t *>(ws);
+        ws += align256((size_t)M * K * 2);
+        rc = w4::gather_cols(static_cast<const uint16_t *>(a), perm, M, K, ap, st);
+        if (rc) return rc;
+        a_eff = ap;
+    }
+    if (c_dtype == W4_E4M3) {
+        float *y = reinterpret_cast<float *>(ws);
+        rc = w4::gptq_gemv(a_eff, a_dtype, qweight, qzeros, scales, y, W4_F32, M, N, K, group_size,
+                           zero_offset, st);
+        if (rc) return rc;
+        return w4::rowscale_fp8(y, W4_F32, static_cast<uint8_t *>(c), row_scale, M, N, st);
+    }
+    return w4::gptq_gemv(a_eff, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, group_size,
+                         zero_offset, st);
+}
+
+int w4_gptq_gemm_s4a(const uint8_t *a_s4, const uint8_t *b_s4, const float *a_scale,
+                     const uint16_t *b_scale, uint16_t *c, int rows, int cols, int dk,
+                     void *stream) {
+    w4::set_error("");
+    W4_REQUIRE(a_s4 && b_s4 && a_scale && b_scale && c, W4_ERR_INVALID, "null pointer argument");
+    W4_REQUIRE(rows >= 1 && cols >= 1 && dk >= 128 && dk % 128 == 0, W4_ERR_INVALID,
+               "shape rows=%d cols=%d dk=%d (dk must be a multiple of 128)", rows, cols, dk);
+    return w4::gptq_s4a(a_s4, b_s4, a_scale, b_scale, c, rows, cols, dk, S(stream));
+}
+
+// ------------------------------------------------------------------ NVFP4
+static int check_nvfp4_w(const uint8_t *w, int layout, const void *scale, int scale_dtype,
+                         const float *global_scale, int K, int N) {
+    W4_REQUIRE(w && scale, W4_ERR_INVALID, "w and scale are required");
+    W4_REQUIRE(layout == W4_NVFP4_KN || layout == W4_NVFP4_NK, W4_ERR_INVALID, "bad layout %d", layout);
+    W4_REQUIRE(scale_dtype == W4_E4M3 || scale_dtype == W4_BF16, W4_ERR_INVALID,
+               "scale_dtype must be e4m3 or bf16");
+    W4_REQUIRE(scale_dtype != W4_E4M3 || global_scale, W4_ERR_INVALID,
+               "e4m3 block scales need the fp32 tensor scale");
+    W4_REQUIRE(scale_dtype != W4_BF16 || !global_scale, W4_ERR_INVALID,
+               "bf16 (folded) block scales take no tensor scale");
+    W4_REQUIRE(K > 0 && N > 0 && K % 16 == 0, W4_ERR_INVALID, "K=%d must be a positive multiple of 16", K);
+    return W4_OK;
+}
+
+int w4_nvfp4_dequant(const uint8_t *w, int layout, const void *scale, int scale_dtype,
+                     const float *global_scale, int K, int N, float *out, void *stream) {
+    w4::set_error("");
+    int rc = check_nvfp4_w(w, layout, scale, scale_dtype, global_scale, K, N);
+    if (rc) return rc;
+    W4_REQUIRE(out, W4_ERR_INVALID, "out is required");
+    return w4::nvfp4_dequant(w, layout, scale, scale_dtype, global_scale, K, N, out, S(stream));
+}
+
+int w4_nvfp4_quant_act(const uint16_t *a, int M, int K, const float *a_global, uint8_t *codes,
+                       uint8_t *sf, void *stream) {
+    w4::set_error("");
+    W4_REQUIRE(a && a_global && codes && sf, W4_ERR_INVALID, "null pointer argument");
+    W4_REQUIRE(M >= 1 && K > 0 && K % 16 == 0, W4_ERR_INVALID, "M=%d K=%d (K %% 16 == 0)", M, K);
+    W4_REQUIRE(aligned(a, 16) && aligned(codes, 8), W4_ERR_INVALID, "a 16-byte, codes 8-byte aligned");
+    return w4::nvfp4_quant_act(a, M, K, a_global, codes, sf, S(stream));
+}
+
+size_t w4_nvfp4_workspace_bytes(int M, int N, int K, int act_mode, int c_dtype) {
+    size_t ws = 0;
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    if (act_mode == W4_ACT_NVFP4) ws += align256((size_t)M * K / 2) + align256((size_t)M * K / 16);
+    if (c_dtype == W4_E4M3) ws += align256((size_t)M * N * 4);
+    return ws;
+}
+
+int w4_nvfp4_gemm(const void *a, const uint8_t *w, int layout, const void *scale,
+                  int scale_dtype, const float *global_scale, int act_mode,
+                  const float *a_global, void *c, int c_dtype, float *row_scale, int M, int N,
+                  int K, void *workspace, size_t workspace_bytes, void *stream) {
+    w4::set_error("");
+    int rc = check_nvfp4_w(w, layout, scale, scale_dtype, global_scale, K, N);
+    if (rc) return rc;
+    W4_REQUIRE(a && c, W4_ERR_INVALID, "a and c are required");
+    W4_REQUIRE(M >= 1, W4_ERR_INVALID, "M=%d must be >= 1", M);
+    W4_REQUIRE(act_mode == W4_ACT_W4A16 || act_mode == W4_ACT_NVFP4, W4_ERR_INVALID, "bad act_mode");
+    W4_REQUIRE(act_mode != W4_ACT_NVFP4 || a_global, W4_ERR_INVALID, "NVFP4 activations need a_global");
+    W4_REQUIRE(c_dtype == W4_F16 || c_dtype == W4_BF16 || c_dtype == W4_F32 || c_dtype == W4_E4M3,
+               W4_ERR_INVALID, "c_dtype must be f16, bf16, f32 or e4m3");
+    W4_REQUIRE(c_dtype != W4_E4M3 || row_scale, W4_ERR_INVALID, "e4m3 output needs row_scale");
+    W4_REQUIRE(layout == W4_NVFP4_NK, W4_ERR_UNSUPPORTED,
+               "the GEMM reads the K-contiguous [N, K/2] layout; transpose [K/2, N] weights once "
+               "with w4_nvfp4_repack_kn_to_nk");
+    W4_REQUIRE(act_mode == W4_ACT_W4A16, W4_ERR_UNSUPPORTED,
+               "NVFP4-activation GEMM is not built yet");
+    W4_REQUIRE(K % 128 == 0 && N % 32 == 0, W4_ERR_UNSUPPORTED,
+               "need K %% 128 == 0 and N %% 32 == 0 (K=%d N=%d)", K, N);
+    W4_REQUIRE(aligned(a, 16) && aligned(w, 16), W4_ERR_INVALID, "a and w must be 16-byte aligned");
+    const size_t need = w4_nvfp4_workspace_bytes(M, N, K, act_mode, c_dtype);
+    W4_REQUIRE(workspace_bytes >= need && (need == 0 || workspace), W4_ERR_INVALID,
+               "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+    cudaStream_t st = S(stream);
+    if (c_dtype == W4_E4M3) {
+        float *y = static_cast<float *>(workspace);
+        rc = w4::nvfp4_gemv(static_cast<const uint16_t *>(a), w, layout, scale, scale_dtype,
+                            global_scale, y, W4_F32, M, N, K, st);
+        if (rc) return rc;
+        return w4::rowscale_fp8(y, W4_F32, static_cast<uint8_t *>(c), row_scale, M, N, st);
+    }
+    return w4::nvfp4_gemv(static_cast<const uint16_t *>(a), w, layout, scale, scale_dtype,
+                          global_scale, c, c_dtype, M, N, K, st);
+}
+
+int w4_nvfp4_repack_kn_to_nk(const uint8_t *w_kn, int K, int N, uint8_t *w_nk, void *stream) {
+    w4::set_error("");
+    W4_REQUIRE(w_kn && w_nk && w_kn != w_nk, W4_ERR_INVALID, "distinct w_kn and w_nk are required");
+    W4_REQUIRE(K > 0 && N > 0 && K % 2 == 0, W4_ERR_INVALID, "K=%d N=%d", K, N);
+    return w4::nvfp4_kn_to_nk(w_kn, K, N, w_nk, S(stream));
+}
+
+int w4_nvfp4_lut_gemm_s8a(const int8_t *a, const uint8_t *packed, const float *a_s,
+                          const float *b_s, uint16_t *c, int rows, int cols, int dk,
+                          void *stream) {
+    w4::set_error("");
+    W4_REQUIRE(a && packed && a_s && b_s && c, W4_ERR_INVALID, "null pointer argument");
+    W4_REQUIRE(rows >= 1 && cols >= 1 && dk >= 2 && dk % 2 == 0, W4_ERR_INVALID,
+               "shape rows=%d cols=%d dk=%d", rows, cols, dk);
+    return w4::nvfp4_lut_s8a(a, packed, a_s, b_s, c, rows, cols, dk, S(stream));
+}
+
+// ------------------------------------------------------------------ epilogue quant
+int w4_rmsnorm_quant_s8(const uint16_t *x, int8_t *q, float *scale, int M, int K, float eps,
+                        void *stream) {
+    w4::set_error("");
+    W4_REQUIRE(x && q && scale, W4_ERR_INVALID, "null pointer argument");
+    W4_REQUIRE(M >= 1 && K >= 8 && K % 8 == 0, W4_ERR_INVALID, "M=%d K=%d (K %% 8 == 0)", M, K);
+    W4_REQUIRE(aligned(x, 16) && aligned(q, 8), W4_ERR_INVALID, "x 16-byte, q 8-byte aligned");
+    return w4::rmsnorm_quant_s8(x, q, scale, M, K, eps, S(stream));
+}
+
+int w4_rowscale_fp8(const void *y, int y_dtype, uint8_t *q, float *row_scale, int M, int N,
+                    void *stream) {
+    w4::set_error("");
+    W4_REQUIRE(y && q && row_scale, W4_ERR_INVALID, "null pointer argument");
+    W4_REQUIRE(M >= 1 && N >= 1, W4_ERR_INVALID, "M=%d N=%d", M, N);
+    W4_REQUIRE(y_dtype == W4_F16 || y_dtype == W4_BF16 || y_dtype == W4_F32, W4_ERR_INVALID,
+               "y_dtype must be f16, bf16 or f32");
+    return w4::rowscale_fp8(y, y_dtype, q, row_scale, M, N, S(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,177 @@
+// w4_common.cuh -- shared helpers for libw4 (sm_100a only).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+
+#include "../../include/w4.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "libw4 targets sm_100a only"
+#endif
+
+namespace w4 {
+
+// ---- error reporting (thread-local one-line reason) ----
+void set_error(const char *fmt, ...);
+const char *last_error();
+
+#define W4_REQUIRE(cond, code, ...)        \
+    do {                                   \
+        if (!(cond)) {                     \
+            ::w4::set_error(__VA_ARGS__);  \
+            return (code);                 \
+        }                                  \
+    } while (0)
+
+#define W4_CUDA_TRY(expr)                                                             \
+    do {                                                                              \
+        cudaError_t _e = (expr);                                                      \
+        if (_e != cudaSuccess) {                                                      \
+            ::w4::set_error("%s: %s (%s:%d)", #expr, cudaGetErrorString(_e), __FILE__, \
+                            __LINE__);                                                \
+            return W4_ERR_CUDA;                                                       \
+        }                                                                             \
+    } while (0)
+
+#define W4_LAUNCH_CHECK()                                                                   \
+    do {                                                                                    \
+        cudaError_t _e = cudaGetLastError();                                                \
+        if (_e != cudaSuccess) {                                                            \
+            ::w4::set_error("kernel launch: %s (%s:%d)", cudaGetErrorString(_e), __FILE__, \
+                            __LINE__);                                                      \
+            return W4_ERR_CUDA;                                                             \
+        }                                                                                   \
+    } while (0)
+
+inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int num_sms();
+
+// ---- device helpers ----
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;  // (a & b) | c
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+__device__ __forceinline__ uint4 ld_stream_v4(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint4 ld_nc_v4(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// D = A(16x16, row) * B(16x8, col) + C, fp32 accumulate.  Legacy warp MMA;
+// used by the decode kernels whose bound is HBM, not the tensor pipe.
+template <typename T>
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1);
+
+template <>
+__device__ __forceinline__ void mma_16816<__nv_bfloat16>(float (&d)[4], uint32_t a0, uint32_t a1,
+                                                         uint32_t a2, uint32_t a3, uint32_t b0,
+                                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <>
+__device__ __forceinline__ void mma_16816<__half>(float (&d)[4], uint32_t a0, uint32_t a1,
+                                                  uint32_t a2, uint32_t a3, uint32_t b0,
+                                                  uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <typename T> struct Conv;
+template <> struct Conv<__half> {
+    static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+    static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+};
+template <> struct Conv<__nv_bfloat16> {
+    static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+    static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+__device__ __forceinline__ float f16_bits_to_f(uint16_t b) {
+    return __half2float(__ushort_as_half(b));
+}
+
+// e4m3fn -> f32 (exact; 0x7F/0xFF decode to NaN).
+__device__ __forceinline__ float e4m3_to_f(uint32_t b) {
+    uint32_t e = (b >> 3) & 0xF, m = b & 7;
+    float v;
+    if (e == 0) {
+        v = __int2float_rn(m) * 0.001953125f;
+    } else {
+        v = __uint_as_float(((e + 120u) << 23) | (m << 20));
+        if (e == 15 && m == 7) v = __int_as_float(0x7fc00000);
+    }
+    return (b & 0x80) ? -v : v;
+}
+
+// f32 -> e4m3fn, round-to-nearest-even, saturating to +-448 (NaN -> 0x7F).
+__device__ __forceinline__ uint32_t f_to_e4m3(float x) {
+    uint32_t u = __float_as_uint(x);
+    uint32_t s = (u >> 24) & 0x80;
+    uint32_t a = u & 0x7FFFFFFFu;
+    if (a > 0x7F800000u) return 0x7F;
+    if (a >= 0x43E00000u) return s | 0x7E;
+    if (a < 0x3C800000u) {
+        float q = rintf(__uint_as_float(a) * 512.0f);
+        return s | (uint32_t)q;
+    }
+    int e = (int)(a >> 23) - 127;
+    uint32_t m = a & 0x7FFFFFu;
+    uint32_t q = m >> 20, rem = m & 0xFFFFFu;
+    if (rem > 0x80000u || (rem == 0x80000u && (q & 1))) q++;
+    uint32_t code = ((uint32_t)(e + 7) << 3) + q;
+    if (code > 0x7E) code = 0x7E;
+    return s | code;
+}
+
+// f32 -> e2m1 code (RNE, saturating to +-6).
+__device__ __forceinline__ uint32_t f_to_e2m1(float x) {
+    uint32_t s = (__float_as_uint(x) >> 31) ? 8u : 0u;
+    float a = fabsf(x);
+    uint32_t c;
+    if (a <= 0.25f) c = 0;
+    else if (a < 0.75f) c = 1;
+    else if (a <= 1.25f) c = 2;
+    else if (a < 1.75f) c = 3;
+    else if (a <= 2.5f) c = 4;
+    else if (a < 3.5f) c = 5;
+    else if (a <= 5.0f) c = 6;
+    else c = 7;
+    return s | c;
+}
+
+__device__ __forceinline__ float e2m1_to_f(uint32_t nib) {
+    // magnitudes {0, .5, 1, 1.5, 2, 3, 4, 6}
+    const uint32_t e = (nib >> 1) & 3, m = nib & 1;
+    float v = (e == 0) ? 0.5f * (float)m : __uint_as_float(((e + 126u) << 23) | (m << 22));
+    return (nib & 8) ? -v : v;
+}
+
+}  // namespace w4

@@ -1,0 +1,39 @@
+// w4_internal.h -- launchers shared between the libw4 translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace w4 {
+
+// gptq.cu
+int gptq_dequant(const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
+                 const int32_t *g_idx, int K, int N, int gs, int zero_offset, float *w,
+                 cudaStream_t st);
+int gptq_repack_act_order(const int32_t *qweight, const int32_t *g_idx, int K, int N, int gs,
+                          int32_t *qweight_out, int32_t *perm_out, cudaStream_t st);
+int gather_cols(const uint16_t *a, const int32_t *perm, int M, int K, uint16_t *out,
+                cudaStream_t st);
+int gptq_gemv(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
+              const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs,
+              int zero_offset, cudaStream_t st);
+int gptq_s4a(const uint8_t *a, const uint8_t *b, const float *a_scale, const uint16_t *s,
+             uint16_t *c, int rows, int cols, int dk, cudaStream_t st);
+
+// nvfp4.cu
+int nvfp4_dequant(const uint8_t *w, int layout, const void *scale, int scale_dtype,
+                  const float *global_scale, int K, int N, float *out, cudaStream_t st);
+int nvfp4_quant_act(const uint16_t *a, int M, int K, const float *a_global, uint8_t *codes,
+                    uint8_t *sf, cudaStream_t st);
+int nvfp4_lut_s8a(const int8_t *a, const uint8_t *packed, const float *a_s, const float *b_s,
+                  uint16_t *c, int rows, int cols, int dk, cudaStream_t st);
+int nvfp4_gemv(const uint16_t *a, const uint8_t *w, int layout, const void *scale,
+               int scale_dtype, const float *global_scale, void *c, int c_dtype, int M, int N,
+               int K, cudaStream_t st);
+
+// epilogue.cu
+int rmsnorm_quant_s8(const uint16_t *x, int8_t *q, float *scale, int M, int K, float eps,
+                     cudaStream_t st);
+int rowscale_fp8(const void *y, int y_dtype, uint8_t *q, float *row_scale, int M, int N,
+                 cudaStream_t st);
+
+}  // namespace w4
