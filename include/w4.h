@@ -114,6 +114,21 @@ int w4_gptq_gemm(const void *a, int a_dtype, const int32_t *qweight, const int32
                  float *row_scale, int M, int N, int K, int group_size, int zero_offset,
                  void *workspace, size_t workspace_bytes, void *stream);
 
+/* w4_gptq_gemm with c_dtype == W4_E4M3 for callers that cannot allocate
+ * device memory (a binding that only forwards pointers it was given, a runtime
+ * that pre-reserved all HBM).  It has no counterpart in the reference.  Same
+ * arguments and results as w4_gptq_gemm(a, a_dtype, qweight, qzeros, scales,
+ * NULL, q_out, W4_E4M3, row_scale, M, N, K, group_size, zero_offset, ...), but
+ * the f32 intermediate lives in a static device array inside the library
+ * (4 MiB per device, held until exit) instead of a workspace: M*N must be
+ * <= 1,048,576 or the call returns W4_ERR_UNSUPPORTED.  The first call on a
+ * device looks the array's address up; make it before any stream capture.
+ * All calls share the array: calls that overlap on the GPU race. */
+int w4_gptq_gemm_fp8_noalloc(const void *a, int a_dtype, const int32_t *qweight,
+                             const int32_t *qzeros, const uint16_t *scales, uint8_t *q_out,
+                             float *row_scale, int M, int N, int K, int group_size,
+                             int zero_offset, void *stream);
+
 /* The reference kernel's own contract, same arguments in the same order as
  * launch(q, ad, bd, asd, sd, cd, rows, cols, dk) of
  * kernels/esimd_dpas/dpas_s4_gptq_sc.cpp:146-149:
