@@ -42,9 +42,9 @@ MS = (1, 4, 8, 16)
 METRIC = json.load(open(os.path.join(ROOT, "BASELINE.json")))["metric"]
 WORKLOAD = ("config2: GPTQ int4 W4A16 decode sweep, M in {1,4,8,16}, K=5120, N=17408, group 128, "
             "asymmetric packed zeros (v1 +1), bf16 activations and output, fp32 accumulate")
-# dram__bytes_read.sum + dram__bytes_write.sum per gptq_gemv launch, from the ncu capture
-# summarised in profiles/ (None until a capture exists).
-TRAFFIC_PER_LAUNCH = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one gptq_gemv launch at M=1 from the ncu
+# capture summarised in profiles/gptq_gemv_config2.md (46.35 MB read + ~0.03 MB written).
+TRAFFIC_PER_LAUNCH = 46_380_000
 
 
 def alg_bytes(M: int, n_cols: int = N) -> int:
@@ -276,16 +276,10 @@ def run_ours(args) -> None:
     value = step_bytes() * args.steps * world / (ms / 1e3) / 1e9
 
     # ---------------- per-launch kernel durations (roofline of the GEMV kernel)
+    from xe2x2_b200.profile_driver import time_launches
     per_m = {}
-    reps = 30
     for M in MS:
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
-        for r in range(reps):
-            evs[r][0].record(st)
-            gemm(M, weights[r % R], outs[M])
-            evs[r][1].record(st)
-        torch.cuda.synchronize()
-        us = statistics.median(a.elapsed_time(b) * 1e3 for a, b in evs)
+        us = statistics.median(time_launches(lambda r, M=M: gemm(M, weights[r % R], outs[M]), 30))
         per_m[str(M)] = {"us": round(us, 3), "GB/s": round(alg_bytes(M) / us / 1e3, 1)}
     tot_b = sum(alg_bytes(M) for M in MS)
     tot_us = sum(per_m[str(M)]["us"] for M in MS)

@@ -8,6 +8,10 @@
 // except the optional act_order row permutation.
 #include <cooperative_groups.h>
 
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "w4_common.cuh"
 #include "w4_internal.h"
 
@@ -125,12 +129,12 @@ int gather_cols(const uint16_t *a, const int32_t *perm, int M, int K, uint16_t *
 // ---------------------------------------------------------------------------
 // Decode GEMM (M small): warp-level, HBM-bound.
 //
-// A warp owns 32 output columns and a range of qweight words (4 words = 32 k
-// per step).  Lane (g = lane/4, t = lane%4) loads 16 B = 4 adjacent columns of
-// word row (kbase + t): for each t the 8 lanes of that t read one contiguous
-// 128-byte line.  The 32 codes in the lane's registers become the A operand of
-// m16n8k16 MMAs with the WEIGHT COLUMNS as MMA rows (swap-AB) and the tokens
-// as MMA columns:
+// A warp owns 32 output columns and a run of qweight words (4 words = 32 k per
+// step).  Lane (g = lane/4, t = lane%4) loads 16 B = 4 adjacent columns of word
+// row (kbase + t): for each t the 8 lanes of that t read one contiguous 128-byte
+// line.  The 32 codes in the lane's registers become the A operand of m16n8k16
+// MMAs with the WEIGHT COLUMNS as MMA rows (swap-AB) and the tokens as MMA
+// columns:
 //   m-tile mt: MMA row g   <- column 4g + 2mt,  MMA row g+8 <- column 4g + 2mt + 1
 //   k-step s : MMA k-slots (2t, 2t+1) <- codes (2s, 2s+4) of word kbase+t,
 //              k-slots (2t+8, 2t+9) <- codes (2s+1, 2s+5)
@@ -141,19 +145,11 @@ int gather_cols(const uint16_t *a, const int32_t *perm, int M, int K, uint16_t *
 // accumulation runs per group and is scaled by the fp16 group scale when the
 // group ends -- the s32-partial-then-scale structure of the reference kernel
 // (kernels/esimd_dpas/dpas_s4_gptq_sc.cpp:178-218) with real activations.
-//
-// Split-K: the 8 warps of a CTA take consecutive k ranges and reduce through
-// shared memory; when the grid has too few column blocks to fill the GPU, a
-// thread-block cluster of KS CTAs splits K further and the cluster leader sums
-// the partials over distributed shared memory.  No global scratch, one launch.
 // ---------------------------------------------------------------------------
 template <typename T> struct Deq;
 template <> struct Deq<__nv_bfloat16> {
-    static constexpr uint32_t kMagic = 0x43004300u;  // bf16 128.0 | q in mantissa bits 0-3
-    static __device__ __forceinline__ uint32_t zconst(int z) {
-        const uint32_t h = __bfloat16_as_ushort(__float2bfloat16_rn(128.0f + (float)z));
-        return h | (h << 16);
-    }
+    // bf16 128.0 with q in mantissa bits 0-3 is 128 + q; (128 + z) is 0x4300 + z
+    static constexpr uint32_t kMagic = 0x43004300u, kMagicHalf = 0x4300u;
     static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
         __nv_bfloat162 r = __hsub2(*reinterpret_cast<__nv_bfloat162 *>(&a),
                                    *reinterpret_cast<__nv_bfloat162 *>(&b));
@@ -161,226 +157,226 @@ template <> struct Deq<__nv_bfloat16> {
     }
 };
 template <> struct Deq<__half> {
-    static constexpr uint32_t kMagic = 0x64006400u;  // f16 1024.0 | q in mantissa bits 0-3
-    static __device__ __forceinline__ uint32_t zconst(int z) {
-        const uint32_t h = __half_as_ushort(__float2half_rn(1024.0f + (float)z));
-        return h | (h << 16);
-    }
+    // f16 1024.0 with q in mantissa bits 0-3 is 1024 + q; (1024 + z) is 0x6400 + z
+    static constexpr uint32_t kMagic = 0x64006400u, kMagicHalf = 0x6400u;
     static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
         __half2 r = __hsub2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b));
         return *reinterpret_cast<uint32_t *>(&r);
     }
 };
 
-constexpr int kGemvWarps = 8;
+// Geometry: a CTA owns 32 output columns; its W warps (blockDim = 32 W, W <= 16)
+// split K into W contiguous runs of whole virtual groups and meet in shared
+// memory at the end.  Token blocks of 8*NT run as grid.x (fastest), so the
+// token blocks of a column chunk re-read its weights from L2.
+//
+// Streaming: HBM on this part needs ~120 KB of reads in flight per SM (loaded
+// latency ~3 us).  Each warp issues a batch of kBatch independent 16-byte
+// weight loads (kBatch steps of 32 k) and then consumes the whole batch, so no
+// outstanding load waits behind a younger one; W is chosen on the host so the
+// whole grid is resident at once (one wave).
+template <int NT> struct GemvCfg;
+template <> struct GemvCfg<1> { static constexpr int kBatch = 16, kMaxRegs = 128; };
+template <> struct GemvCfg<2> { static constexpr int kBatch = 8, kMaxRegs = 128; };
+constexpr int kGemvMaxWarps = 16;
 
-template <typename T, int NT, int D>
-__global__ void __launch_bounds__(kGemvWarps * 32)
+template <typename T, int NT, int GSTEPS>
+__global__ void __launch_bounds__(kGemvMaxWarps * 32)
 gptq_gemv_kernel(const T *__restrict__ A, const int32_t *__restrict__ qweight,
                  const int32_t *__restrict__ qzeros, const uint16_t *__restrict__ scales,
-                 void *__restrict__ C, int c_dtype, int M, int N, int K, int gs, int zero_offset,
-                 int words_per_part, int ks) {
-    constexpr int NE = 2 * NT * 4;  // accumulator floats per lane
-    __shared__ float red[kGemvWarps][NE][32];
-    __shared__ float part[NE * 32];
+                 void *__restrict__ C, int c_dtype, int M, int N, int K, int zero_offset,
+                 int vpg, int vgroups_per_warp) {
+    constexpr int kBatch = GemvCfg<NT>::kBatch;
+    static_assert(kBatch % GSTEPS == 0, "a batch holds whole virtual groups");
+    constexpr int VPB = kBatch / GSTEPS;  // virtual groups per batch
+    constexpr int NE = 2 * NT * 4;
+    extern __shared__ float red[];  // [W][NE][32]
 
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const int n_base = blockIdx.x * 32 + 4 * g;
-    const int tok0 = blockIdx.z * 8 * NT;
-    const int KW = K / 8, gw = gs / 8;
-    const int p = blockIdx.y * kGemvWarps + warp;
-    const int w_begin = min(p * words_per_part, KW);
-    const int w_end = min(w_begin + words_per_part, KW);
-    const int nsteps = (w_end - w_begin) / 4;
+    const int n_base = blockIdx.y * 32 + 4 * g;
+    const int tok0 = blockIdx.x * 8 * NT;
+    const int nvg = K / (32 * GSTEPS);
+    const int vg_begin = min(warp * vgroups_per_warp, nvg);
+    const int vg_end = min(vg_begin + vgroups_per_warp, nvg);
+    const int nsteps = (vg_end - vg_begin) * GSTEPS;
+    const int w0 = vg_begin * GSTEPS * 4;  // first qweight word row of this warp
+    const bool has_z = qzeros != nullptr;
+    const int zshift = 4 * (n_base & 7);
 
-    float facc[2][NT][4], gacc[2][NT][4];
+    const int step_stride = 4 * N;  // int32 elements per step (K/8 * N < 2^31 is validated)
+    int woff = (w0 + t) * N + n_base;
+    const T *ap[NT];
+    bool av[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const int tok = tok0 + nt * 8 + g;
+        av[nt] = tok < M;
+        ap[nt] = A + (size_t)(av[nt] ? tok : 0) * K + (size_t)(w0 + t) * 8;
+    }
+
+    float facc[2][NT][4];
 #pragma unroll
     for (int a = 0; a < 2; ++a)
 #pragma unroll
         for (int b = 0; b < NT; ++b)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) facc[a][b][i] = gacc[a][b][i] = 0.f;
+            for (int i = 0; i < 4; ++i) facc[a][b][i] = 0.f;
 
-    const int32_t *wptr = qweight + (size_t)(w_begin + t) * N + n_base;
-    uint4 wbuf[D];
+    for (int b0 = 0; b0 < nsteps; b0 += kBatch) {
+        // ---- issue the whole batch: weights, then the group constants ----
+        uint4 wv[kBatch];
 #pragma unroll
-    for (int d = 0; d < D; ++d)
-        if (d < nsteps) wbuf[d] = ld_stream_v4(wptr + (size_t)(4 * d) * N);
-
-    int cur_g = -1;
-    uint32_t zc[4];
-    float sc[4];
-    auto load_group = [&](int grp) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            int z = 8;
-            if (qzeros)
-                z = (int)(((uint32_t)__ldg(qzeros + (size_t)grp * (N / 8) + ((n_base + c) >> 3)) >>
-                           (4 * ((n_base + c) & 7))) & 15u) + zero_offset;
-            zc[c] = Deq<T>::zconst(z);
+        for (int u = 0; u < kBatch; ++u) {
+            wv[u] = make_uint4(0, 0, 0, 0);
+            if (b0 + u < nsteps) wv[u] = ld_stream_v4(qweight + woff + u * step_stride);
         }
-        const uint2 s4 = __ldg(reinterpret_cast<const uint2 *>(scales + (size_t)grp * N + n_base));
-        sc[0] = f16_bits_to_f((uint16_t)(s4.x & 0xFFFF));
-        sc[1] = f16_bits_to_f((uint16_t)(s4.x >> 16));
-        sc[2] = f16_bits_to_f((uint16_t)(s4.y & 0xFFFF));
-        sc[3] = f16_bits_to_f((uint16_t)(s4.y >> 16));
-    };
-    auto flush = [&]() {
+        uint32_t zw[VPB];
+        uint2 sw[VPB];
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                facc[mt][nt][0] += gacc[mt][nt][0] * sc[2 * mt];
-                facc[mt][nt][1] += gacc[mt][nt][1] * sc[2 * mt];
-                facc[mt][nt][2] += gacc[mt][nt][2] * sc[2 * mt + 1];
-                facc[mt][nt][3] += gacc[mt][nt][3] * sc[2 * mt + 1];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) gacc[mt][nt][i] = 0.f;
+        for (int v = 0; v < VPB; ++v) {
+            zw[v] = 0;
+            sw[v] = make_uint2(0, 0);
+            if (b0 + v * GSTEPS < nsteps) {
+                const int grp = (vg_begin + b0 / GSTEPS + v) / vpg;
+                if (has_z) zw[v] = (uint32_t)__ldg(qzeros + grp * (N / 8) + (n_base >> 3));
+                sw[v] = __ldg(reinterpret_cast<const uint2 *>(scales + grp * N + n_base));
             }
-    };
-
-    for (int i0 = 0; i0 < nsteps; i0 += D) {
+        }
+        woff += kBatch * step_stride;
+        // ---- consume it ----
 #pragma unroll
-        for (int d = 0; d < D; ++d) {
-            const int step = i0 + d;
-            if (step < nsteps) {
-                const uint4 wv = wbuf[d];
-                if (step + D < nsteps) wbuf[d] = ld_stream_v4(wptr + (size_t)(4 * (step + D)) * N);
-                const int kw = w_begin + 4 * step;  // word of lane t is kw + t
-                const int grp = kw / gw;
-                if (grp != cur_g) {
-                    if (cur_g >= 0) flush();
-                    cur_g = grp;
-                    load_group(grp);
+        for (int v = 0; v < VPB; ++v) {
+            if (b0 + v * GSTEPS < nsteps) {
+                uint32_t zc[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const uint32_t z = has_z ? ((zw[v] >> (zshift + 4 * c)) & 15u) + (uint32_t)zero_offset : 8u;
+                    zc[c] = (Deq<T>::kMagicHalf + z) * 0x00010001u;
                 }
-                // activation fragments: token tok0 + nt*8 + g, elements 8(kw+t)..+7
-                uint32_t bf[NT][2][2];
+                float gacc[2][NT][4];
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    const int tok = tok0 + nt * 8 + g;
-                    uint4 x = make_uint4(0, 0, 0, 0);
-                    if (tok < M) x = ld_nc_v4(A + (size_t)tok * K + (size_t)(kw + t) * 8);
-                    bf[nt][0][0] = __byte_perm(x.x, x.z, 0x5410);
-                    bf[nt][0][1] = __byte_perm(x.x, x.z, 0x7632);
-                    bf[nt][1][0] = __byte_perm(x.y, x.w, 0x5410);
-                    bf[nt][1][1] = __byte_perm(x.y, x.w, 0x7632);
-                }
-                const uint32_t wc[4] = {wv.x, wv.y, wv.z, wv.w};
+                for (int a = 0; a < 2; ++a)
 #pragma unroll
-                for (int mt = 0; mt < 2; ++mt) {
-                    const uint32_t lo = wc[2 * mt], hi = wc[2 * mt + 1];
+                    for (int bb = 0; bb < NT; ++bb)
 #pragma unroll
-                    for (int s = 0; s < 2; ++s) {
-                        const uint32_t a0 = Deq<T>::sub(lop3_and_or(lo >> (8 * s), 0x000F000Fu, Deq<T>::kMagic), zc[2 * mt]);
-                        const uint32_t a1 = Deq<T>::sub(lop3_and_or(hi >> (8 * s), 0x000F000Fu, Deq<T>::kMagic), zc[2 * mt + 1]);
-                        const uint32_t a2 = Deq<T>::sub(lop3_and_or(lo >> (8 * s + 4), 0x000F000Fu, Deq<T>::kMagic), zc[2 * mt]);
-                        const uint32_t a3 = Deq<T>::sub(lop3_and_or(hi >> (8 * s + 4), 0x000F000Fu, Deq<T>::kMagic), zc[2 * mt + 1]);
+                        for (int i = 0; i < 4; ++i) gacc[a][bb][i] = 0.f;
 #pragma unroll
-                        for (int nt = 0; nt < NT; ++nt)
-                            mma_16816<T>(gacc[mt][nt], a0, a1, a2, a3, bf[nt][s][0], bf[nt][s][1]);
+                for (int s = 0; s < GSTEPS; ++s) {
+                    const int u = v * GSTEPS + s;
+                    const int step = b0 + u;
+                    uint32_t bf[NT][2][2];
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        uint4 x = make_uint4(0, 0, 0, 0);
+                        if (av[nt]) x = __ldg(reinterpret_cast<const uint4 *>(ap[nt] + (size_t)step * 32));
+                        bf[nt][0][0] = __byte_perm(x.x, x.z, 0x5410);
+                        bf[nt][0][1] = __byte_perm(x.x, x.z, 0x7632);
+                        bf[nt][1][0] = __byte_perm(x.y, x.w, 0x5410);
+                        bf[nt][1][1] = __byte_perm(x.y, x.w, 0x7632);
+                    }
+                    const uint32_t wc[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
+#pragma unroll
+                    for (int mt = 0; mt < 2; ++mt) {
+                        const uint32_t lo = wc[2 * mt], hi = wc[2 * mt + 1];
+#pragma unroll
+                        for (int q = 0; q < 2; ++q) {
+                            const uint32_t a0 = Deq<T>::sub(lop3_and_or(lo >> (8 * q), 0x000F000Fu, Deq<T>::kMagic), zc[2 * mt]);
+                            const uint32_t a1 = Deq<T>::sub(lop3_and_or(hi >> (8 * q), 0x000F000Fu, Deq<T>::kMagic), zc[2 * mt + 1]);
+                            const uint32_t a2 = Deq<T>::sub(lop3_and_or(lo >> (8 * q + 4), 0x000F000Fu, Deq<T>::kMagic), zc[2 * mt]);
+                            const uint32_t a3 = Deq<T>::sub(lop3_and_or(hi >> (8 * q + 4), 0x000F000Fu, Deq<T>::kMagic), zc[2 * mt + 1]);
+#pragma unroll
+                            for (int nt = 0; nt < NT; ++nt)
+                                mma_16816<T>(gacc[mt][nt], a0, a1, a2, a3, bf[nt][q][0], bf[nt][q][1]);
+                        }
                     }
                 }
+                const float sc[4] = {f16_bits_to_f((uint16_t)(sw[v].x & 0xFFFF)), f16_bits_to_f((uint16_t)(sw[v].x >> 16)),
+                                     f16_bits_to_f((uint16_t)(sw[v].y & 0xFFFF)), f16_bits_to_f((uint16_t)(sw[v].y >> 16))};
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        facc[mt][nt][0] = fmaf(gacc[mt][nt][0], sc[2 * mt], facc[mt][nt][0]);
+                        facc[mt][nt][1] = fmaf(gacc[mt][nt][1], sc[2 * mt], facc[mt][nt][1]);
+                        facc[mt][nt][2] = fmaf(gacc[mt][nt][2], sc[2 * mt + 1], facc[mt][nt][2]);
+                        facc[mt][nt][3] = fmaf(gacc[mt][nt][3], sc[2 * mt + 1], facc[mt][nt][3]);
+                    }
             }
         }
     }
-    if (cur_g >= 0) flush();
 
-    // ---- reduce: warps -> CTA (shared) -> cluster leader (distributed shared) ----
+    // ---- K-split reduction across the W warps ----
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) red[warp][(mt * NT + nt) * 4 + i][lane] = facc[mt][nt][i];
+            for (int i = 0; i < 4; ++i) red[(warp * NE + (mt * NT + nt) * 4 + i) * 32 + lane] = facc[mt][nt][i];
     __syncthreads();
     for (int idx = threadIdx.x; idx < NE * 32; idx += blockDim.x) {
-        const int e = idx >> 5, l = idx & 31;
         float v = 0.f;
-#pragma unroll
-        for (int w = 0; w < kGemvWarps; ++w) v += red[w][e][l];
-        part[idx] = v;
-    }
-    bool leader = true;
-    if (ks > 1) {
-        cg::cluster_group cluster = cg::this_cluster();
-        cluster.sync();
-        leader = cluster.block_rank() == 0;
-        if (leader) {
-            for (int idx = threadIdx.x; idx < NE * 32; idx += blockDim.x) {
-                float v = part[idx];
-                for (int r = 1; r < ks; ++r) v += cluster.map_shared_rank(part, r)[idx];
-                red[0][0][idx] = v;  // red is free again; NE*32 floats fit in red[0..]
-            }
-        }
-        cluster.sync();
-    } else {
-        __syncthreads();
-    }
-    if (!leader) return;
-    if (ks > 1) __syncthreads();
-    const float *src = (ks > 1) ? &red[0][0][0] : part;
-    for (int idx = threadIdx.x; idx < NE * 32; idx += blockDim.x) {
+        for (int w = 0; w < W; ++w) v += red[w * NE * 32 + idx];
         const int e = idx >> 5, l = idx & 31;
         const int mt = e / (NT * 4), nt = (e / 4) % NT, i = e & 3;
-        const int col = blockIdx.x * 32 + 4 * (l >> 2) + 2 * mt + (i >> 1);
+        const int col = blockIdx.y * 32 + 4 * (l >> 2) + 2 * mt + (i >> 1);
         const int tok = tok0 + nt * 8 + 2 * (l & 3) + (i & 1);
-        if (tok < M && col < N) {
-            const float v = src[idx];
-            const size_t o = (size_t)tok * N + col;
-            if (c_dtype == W4_F32) reinterpret_cast<float *>(C)[o] = v;
-            else if (c_dtype == W4_BF16) reinterpret_cast<__nv_bfloat16 *>(C)[o] = __float2bfloat16_rn(v);
-            else reinterpret_cast<__half *>(C)[o] = __float2half_rn(v);
-        }
+        if (tok < M) store_out(C, c_dtype, (size_t)tok * N + col, v);
     }
 }
 
-template <typename T, int NT>
+template <typename T, int NT, int GSTEPS>
 static int launch_gemv_t(const T *a, const int32_t *qweight, const int32_t *qzeros,
                          const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs,
                          int zero_offset, cudaStream_t st) {
-    constexpr int D = 4;
+    constexpr int kBatch = GemvCfg<NT>::kBatch;
     const int nsm = num_sms();
-    const int ncol = N / 32;
+    const int nchunk = N / 32;
     const int mblocks = (M + 8 * NT - 1) / (8 * NT);
-    const int KW = K / 8;
-    // Cluster split-K when the column blocks alone cannot fill ~2 CTAs per SM,
-    // keeping at least one step (4 words) of work per warp.
-    int ks = 1;
-    while (ks < 8 && ncol * mblocks * ks < 2 * nsm && KW / (kGemvWarps * ks * 2) >= 4) ks *= 2;
-    int wpp = (KW + kGemvWarps * ks - 1) / (kGemvWarps * ks);
-    wpp = (wpp + 3) & ~3;
-
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(ncol, ks, mblocks);
-    cfg.blockDim = dim3(kGemvWarps * 32);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = ks;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = ks > 1 ? 1 : 0;
-    W4_CUDA_TRY(cudaLaunchKernelEx(&cfg, gptq_gemv_kernel<T, NT, D>, a, qweight, qzeros, scales, c,
-                                   c_dtype, M, N, K, gs, zero_offset, wpp, ks));
+    const int nvg = K / (32 * GSTEPS);
+    const int vpg = gs / (32 * GSTEPS);
+    // Warps per CTA (the K split): as many as keep the whole grid resident in
+    // one wave at the register budget, with >= 1 batch of work per warp.
+    const long warp_capacity = (long)nsm * (65536 / (GemvCfg<NT>::kMaxRegs * 32));
+    int W = (int)(warp_capacity / ((long)nchunk * mblocks));
+    const int max_by_work = (nvg * GSTEPS + kBatch - 1) / kBatch;  // batches of the whole K
+    W = W < 1 ? 1 : W;
+    W = W > kGemvMaxWarps ? kGemvMaxWarps : W;
+    W = W > max_by_work ? max_by_work : W;
+    const int vpw = (nvg + W - 1) / W;
+    W = (nvg + vpw - 1) / vpw;  // no idle warps
+    const size_t smem = (size_t)W * (2 * NT * 4) * 32 * sizeof(float);
+    dim3 grid(mblocks, nchunk), block(32 * W);
+    gptq_gemv_kernel<T, NT, GSTEPS><<<grid, block, smem, st>>>(a, qweight, qzeros, scales, c, c_dtype, M,
+                                                               N, K, zero_offset, vpg, vpw);
+    W4_LAUNCH_CHECK();
     return W4_OK;
+}
+
+template <typename T, int NT>
+static int launch_gemv_nt(const T *a, const int32_t *qweight, const int32_t *qzeros,
+                          const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs,
+                          int zero_offset, cudaStream_t st) {
+    if (gs % 128 == 0) return launch_gemv_t<T, NT, 4>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    if (gs % 64 == 0) return launch_gemv_t<T, NT, 2>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    return launch_gemv_t<T, NT, 1>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+}
+
+template <typename T>
+static int launch_gemv(const void *a, const int32_t *qweight, const int32_t *qzeros,
+                       const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs,
+                       int zero_offset, cudaStream_t st) {
+    const T *ap = static_cast<const T *>(a);
+    if (M <= 8) return launch_gemv_nt<T, 1>(ap, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    return launch_gemv_nt<T, 2>(ap, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
 }
 
 int gptq_gemv(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
               const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs,
               int zero_offset, cudaStream_t st) {
-    if (a_dtype == W4_BF16) {
-        const auto *ap = static_cast<const __nv_bfloat16 *>(a);
-        if (M <= 8) return launch_gemv_t<__nv_bfloat16, 1>(ap, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
-        if (M <= 16) return launch_gemv_t<__nv_bfloat16, 2>(ap, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
-        return launch_gemv_t<__nv_bfloat16, 4>(ap, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
-    }
-    const auto *ap = static_cast<const __half *>(a);
-    if (M <= 8) return launch_gemv_t<__half, 1>(ap, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
-    if (M <= 16) return launch_gemv_t<__half, 2>(ap, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
-    return launch_gemv_t<__half, 4>(ap, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    if (a_dtype == W4_BF16)
+        return launch_gemv<__nv_bfloat16>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    return launch_gemv<__half>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
 }
 
 // ---------------------------------------------------------------------------

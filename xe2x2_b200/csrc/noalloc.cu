@@ -66,6 +66,8 @@ extern "C" int w4_gptq_gemm_fp8_noalloc(const void *a, int a_dtype, const int32_
                (size_t)M * (size_t)N, w4::kNoAllocMaxElems);
     W4_REQUIRE(w4::aligned(a, 16) && w4::aligned(qweight, 16) && w4::aligned(scales, 8),
                W4_ERR_INVALID, "a and qweight must be 16-byte aligned, scales 8-byte aligned");
+    W4_REQUIRE((size_t)(K / 8) * (size_t)N < (size_t(1) << 31), W4_ERR_UNSUPPORTED,
+               "qweight of %d x %d words exceeds 2^31 elements", K / 8, N);
     float *y = nullptr;
     int rc = w4::noalloc_scratch(&y);
     if (rc) return rc;

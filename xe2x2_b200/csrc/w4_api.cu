@@ -124,6 +124,8 @@ int w4_gptq_gemm(const void *a, int a_dtype, const int32_t *qweight, const int32
                group_size);
     W4_REQUIRE(aligned(a, 16) && aligned(qweight, 16) && aligned(scales, 8), W4_ERR_INVALID,
                "a and qweight must be 16-byte aligned, scales 8-byte aligned");
+    W4_REQUIRE((size_t)(K / 8) * (size_t)N < (size_t(1) << 31), W4_ERR_UNSUPPORTED,
+               "qweight of %d x %d words exceeds 2^31 elements", K / 8, N);
     const size_t need = w4_gptq_workspace_bytes(M, N, K, group_size, perm != nullptr, c_dtype);
     W4_REQUIRE(workspace_bytes >= need && (need == 0 || workspace), W4_ERR_INVALID,
                "workspace of %zu bytes needed, %zu given", need, workspace_bytes);

@@ -9,7 +9,9 @@
 #include <cstdarg>
 #include <cstdio>
 
-#include "../../include/w4.h"
+#include <cooperative_groups.h>
+
+#include "w4.h"  // include/ is on the include path
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
 #error "libw4 targets sm_100a only"
@@ -74,6 +76,26 @@ __device__ __forceinline__ uint4 ld_nc_v4(const void *p) {
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                  : "l"(p));
     return v;
+}
+
+__device__ __forceinline__ void prefetch_l2(const void *p) {
+    asm volatile("prefetch.global.L2::evict_normal [%0];" ::"l"(p));
+}
+
+// 16-byte asynchronous global -> shared copy (L2 only), in commit groups.
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+template <int BYTES>  // 4 or 8 (L1-allocating form; 16 uses cp_async16)
+__device__ __forceinline__ void cp_async_small(void *smem, const void *gmem) {
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(s), "l"(gmem), "n"(BYTES) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // D = A(16x16, row) * B(16x8, col) + C, fp32 accumulate.  Legacy warp MMA;
@@ -172,6 +194,57 @@ __device__ __forceinline__ float e2m1_to_f(uint32_t nib) {
     const uint32_t e = (nib >> 1) & 3, m = nib & 1;
     float v = (e == 0) ? 0.5f * (float)m : __uint_as_float(((e + 126u) << 23) | (m << 22));
     return (nib & 8) ? -v : v;
+}
+
+// ---- split-K reduction of per-lane accumulators ----
+// The WARPS warps of a CTA each hold NE floats per lane for the same output
+// tile (different k ranges).  They are summed through shared memory; when the
+// kernel runs as a thread-block cluster of `ks` CTAs along K, the leader CTA
+// (cluster rank 0) adds the other CTAs' sums over distributed shared memory.
+// Every thread of every CTA must call this exactly once.  Returns the summed
+// tile (index e*32 + lane) in the leader and nullptr elsewhere.
+template <int NE, int WARPS> struct SplitKSmem {
+    float red[WARPS][NE][32];
+    float part[NE * 32];
+};
+
+template <int NE, int WARPS>
+__device__ __forceinline__ const float *splitk_reduce(SplitKSmem<NE, WARPS> &sm,
+                                                      const float (&acc)[NE], int ks) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int e = 0; e < NE; ++e) sm.red[warp][e][lane] = acc[e];
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < NE * 32; idx += blockDim.x) {
+        const int e = idx >> 5, l = idx & 31;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < WARPS; ++w) v += sm.red[w][e][l];
+        sm.part[idx] = v;
+    }
+    if (ks <= 1) {
+        __syncthreads();
+        return sm.part;
+    }
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    const bool leader = cluster.block_rank() == 0;
+    if (leader) {
+        for (int idx = threadIdx.x; idx < NE * 32; idx += blockDim.x) {
+            float v = sm.part[idx];
+            for (int r = 1; r < ks; ++r) v += cluster.map_shared_rank(sm.part, r)[idx];
+            (&sm.red[0][0][0])[idx] = v;
+        }
+    }
+    cluster.sync();  // remote reads done before any CTA of the cluster exits
+    return leader ? &sm.red[0][0][0] : nullptr;
+}
+
+__device__ __forceinline__ void store_out(void *C, int c_dtype, size_t o, float v) {
+    if (c_dtype == W4_F32) reinterpret_cast<float *>(C)[o] = v;
+    else if (c_dtype == W4_BF16) reinterpret_cast<__nv_bfloat16 *>(C)[o] = __float2bfloat16_rn(v);
+    else reinterpret_cast<__half *>(C)[o] = __float2half_rn(v);
 }
 
 }  // namespace w4

@@ -1,0 +1,97 @@
+"""Launch or time one libw4 GEMM shape (for ncu captures and quick per-shape timings).
+
+    python -m xe2x2_b200.profile_driver --kernel gptq --M 16 --K 5120 --N 17408 --iters 4
+    python -m xe2x2_b200.profile_driver --kernel nvfp4 --M 1,16 --K 5120 --N 5120 --time
+
+Without --time it runs ``--iters`` launches back to back (a small, fixed number of
+launches for an ncu capture).  With --time it reports the median per-launch
+CUDA-event time and the algorithmic GB/s (weights rotate over enough copies to
+exceed twice the L2, so each launch reads its weights from HBM).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import statistics
+
+import torch
+
+from . import ops, synth
+
+
+def time_launches(fn, reps: int) -> list[float]:
+    """Per-launch device time (us) of ``fn(i)`` for i in range(reps).
+
+    A GPU sleep kernel is queued first so every launch and event is already
+    enqueued when the GPU reaches them: host launch overhead is excluded and the
+    events measure back-to-back device time.
+    """
+    st = torch.cuda.current_stream()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+    torch.cuda._sleep(int(reps * 80e-6 * 2.0e9))
+    evs[0].record(st)
+    for r in range(reps):
+        fn(r)
+        evs[r + 1].record(st)
+    torch.cuda.synchronize()
+    return [evs[i].elapsed_time(evs[i + 1]) * 1e3 for i in range(reps)]
+
+
+def gptq_bytes(M, K, N, gs, asym=True):
+    return K // 8 * N * 4 + K // gs * N * 2 + (K // gs * N // 8 * 4 if asym else 0) + M * K * 2 + M * N * 2
+
+
+def nvfp4_bytes(M, K, N):
+    return N * K // 2 + K // 16 * N + 4 + M * K * 2 + M * N * 2
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel", choices=["gptq", "nvfp4"], default="gptq")
+    ap.add_argument("--M", default="16", help="comma-separated token counts")
+    ap.add_argument("--K", type=int, default=5120)
+    ap.add_argument("--N", type=int, default=17408)
+    ap.add_argument("--gs", type=int, default=128)
+    ap.add_argument("--dtype", choices=["bf16", "f16"], default="bf16")
+    ap.add_argument("--iters", type=int, default=4)
+    ap.add_argument("--time", action="store_true")
+    args = ap.parse_args(argv)
+    dev = torch.device("cuda:0")
+    dt = torch.bfloat16 if args.dtype == "bf16" else torch.float16
+    K, N = args.K, args.N
+    wbytes = gptq_bytes(0, K, N, args.gs) if args.kernel == "gptq" else nvfp4_bytes(0, K, N)
+    l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 << 20) or (126 << 20)
+    copies = max(1, math.ceil(2 * l2 / wbytes) + 1) if args.time else 1
+    if args.kernel == "gptq":
+        ws = [synth.gptq_weights(K, N, args.gs, asym=True, seed=s, device=dev)[:3] for s in range(copies)]
+    else:
+        ws = [synth.nvfp4_weights(K, N, seed=s, device=dev) for s in range(copies)]
+    results = []
+    for M in [int(m) for m in args.M.split(",")]:
+        a = synth.activations(M, K, dt, seed=M, device=dev)
+
+        def run(i):
+            w = ws[i % copies]
+            if args.kernel == "gptq":
+                return ops.gptq_gemm(a, w[0], w[1], w[2], args.gs, 1)
+            return ops.nvfp4_gemm(a, w[0], w[1], w[2])
+
+        if not args.time:
+            for i in range(args.iters):
+                run(i)
+            torch.cuda.synchronize()
+            continue
+        for i in range(max(3, copies)):
+            run(i)
+        us = statistics.median(time_launches(run, max(args.iters, 20)))
+        nb = gptq_bytes(M, K, N, args.gs) if args.kernel == "gptq" else nvfp4_bytes(M, K, N)
+        results.append({"kernel": args.kernel, "M": M, "K": K, "N": N, "us": round(us, 3),
+                        "GB/s": round(nb / us / 1e3, 1), "TFLOP/s": round(2 * M * N * K / us / 1e6, 2)})
+    for r in results:
+        print(json.dumps(r))
+    print("ok")
+
+
+if __name__ == "__main__":
+    main()
