@@ -72,6 +72,14 @@ int w4_abi_version(void);
 const char *w4_status_string(int status);
 const char *w4_last_error(void);
 
+/* Kernels that wait on asynchronous copies (mbarrier waits) bound every wait;
+ * if one expires the kernel stops that part of its work and sets a device
+ * status word.  This call reads and clears it for the current device:
+ * W4_ERR_TIMEOUT if a wait expired since the last call, else W4_OK.  It
+ * synchronises with the device.  No counterpart in the reference (its kernels
+ * have no device-side waits). */
+int w4_check_device_status(void);
+
 /* ===================================================================== */
 /* GPTQ int4                                                              */
 /* ===================================================================== */

@@ -36,6 +36,7 @@ _SIGS = {
     "w4_abi_version": (_I, []),
     "w4_status_string": (ctypes.c_char_p, [_I]),
     "w4_last_error": (ctypes.c_char_p, []),
+    "w4_check_device_status": (_I, []),
     "w4_gptq_dequant": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "w4_gptq_repack_act_order": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
     "w4_gptq_workspace_bytes": (_Z, [_I, _I, _I, _I, _I, _I]),

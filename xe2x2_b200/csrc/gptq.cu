@@ -374,6 +374,10 @@ static int launch_gemv(const void *a, const int32_t *qweight, const int32_t *qze
 int gptq_gemv(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
               const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs,
               int zero_offset, cudaStream_t st) {
+    // TMA-streamed kernel (gptq_tma.cu) first; the register-batched kernel below
+    // runs only when the tensor maps cannot be encoded.
+    const int rc = gptq_gemv_tma(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    if (rc >= 0) return rc;
     if (a_dtype == W4_BF16)
         return launch_gemv<__nv_bfloat16>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
     return launch_gemv<__half>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);

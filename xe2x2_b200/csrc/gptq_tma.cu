@@ -1,0 +1,428 @@
+// gptq_tma.cu -- GPTQ int4 decode GEMM with TMA-streamed weights (sm_100a).
+//
+// Same math and register mapping as the batched decode kernel in gptq.cu (swap-AB
+// m16n8k16 MMAs, exact (q - zero) in 16-bit floats, per-group fp32 scaling), but
+// the weights reach shared memory through the tensor-memory accelerator.  A CTA
+// owns 32 output columns; its W consumer warps split K evenly and each owns a
+// ring of kTmaStages stages; a stage is kVps groups (qweight rows x 32 columns
+// as a 128-byte-wide, 128-byte-swizzled box) plus those groups' scale rows and
+// zero rows, all completing on one "full" mbarrier.  One extra producer warp
+// issues every copy and refills a stage when its consumer arrives on the
+// stage's "empty" mbarrier, so the consumers' instruction stream is only the
+// dequantisation and the MMAs.  Every wait is bounded: on expiry the waiting
+// warp stops, a device status word is set and w4_check_device_status()
+// reports W4_ERR_TIMEOUT.  No copy uses multicast.
+//
+// Bulk copies move whole tiles per instruction without holding registers, so
+// each SM keeps >100 KB of weight reads in flight while its warps compute.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "w4_common.cuh"
+#include "w4_internal.h"
+
+namespace w4 {
+
+static __device__ unsigned int g_wait_timeout;  // a bounded wait expired (sticky until read)
+
+constexpr int kTmaStages = 3;   // ring depth per consumer warp
+constexpr int kVps = 2;         // virtual groups per stage
+constexpr int kTmaMaxWarps = 8; // consumer warps per CTA (one more warp produces)
+constexpr unsigned long long kWaitLimitNs = 200ull * 1000 * 1000;  // 200 ms
+
+// Per consumer warp: kTmaStages stages of kVps virtual groups.  Every tensor-copy
+// destination is 128-byte aligned (the swizzled tiles 1024).
+struct WarpRing {
+    uint8_t qw[kTmaStages][kVps * 2048];  // swizzled qweight tile (kVps x <= 16 rows x 128 B)
+    uint8_t sc[kTmaStages][128];          // kVps scale rows (32 x f16 each)
+    uint8_t zr[kTmaStages][128];          // kVps zero rows (4 x i32 each)
+    uint64_t full[kTmaStages];            // producer -> consumer (1 arrive + tx bytes)
+    uint64_t empty[kTmaStages];           // consumer -> producer (1 arrive)
+    uint8_t pad[1024 - (kTmaStages * 256 + kTmaStages * 16) % 1024];
+};
+static_assert(sizeof(WarpRing) % 1024 == 0, "rings stay 1024-byte aligned");
+
+// ---- PTX helpers (TMA + mbarrier) ----
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Wait for the phase with the given parity; false if kWaitLimitNs passed first.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+    const uint32_t b = smem_u32(bar);
+    if (mbar_try_wait(b, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    while (!mbar_try_wait(b, parity))
+        if (global_ns() - t0 > kWaitLimitNs) return false;
+    return true;
+}
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+template <typename T> struct DeqT;
+template <> struct DeqT<__nv_bfloat16> {
+    static constexpr uint32_t kMagic = 0x43004300u, kMagicHalf = 0x4300u;  // 128 + q
+    static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
+        __nv_bfloat162 r = __hsub2(*reinterpret_cast<__nv_bfloat162 *>(&a), *reinterpret_cast<__nv_bfloat162 *>(&b));
+        return *reinterpret_cast<uint32_t *>(&r);
+    }
+};
+template <> struct DeqT<__half> {
+    static constexpr uint32_t kMagic = 0x64006400u, kMagicHalf = 0x6400u;  // 1024 + q
+    static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
+        __half2 r = __hsub2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b));
+        return *reinterpret_cast<uint32_t *>(&r);
+    }
+};
+
+// Lane quad g reads 16-byte chunk sigma(g) = (0,4,1,5,2,6,3,7)[g] of each 128-byte
+// row: with the 128-byte swizzle (chunk ^= row % 8) the 8 lanes of every
+// shared-load phase then hit 8 distinct bank groups.
+__device__ __forceinline__ int sigma(int g) { return (g >> 1) | ((g & 1) << 2); }
+
+template <typename T, int NT, int GSTEPS>
+__global__ void __launch_bounds__((kTmaMaxWarps + 1) * 32)
+gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_constant__ CUtensorMap sc_map,
+                     const __grid_constant__ CUtensorMap zr_map, int has_z, const T *__restrict__ A,
+                     void *__restrict__ C, int c_dtype, int M, int N, int K, int zero_offset,
+                     int stages_total) {
+    constexpr int S = kTmaStages;
+    constexpr int NE = 2 * NT * 4;
+    constexpr int ROWS = 4 * GSTEPS;           // qweight rows per virtual group
+    constexpr int SSTEPS = kVps * GSTEPS;      // k steps per stage
+    extern __shared__ uint8_t smem_dyn[];
+    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int W = (blockDim.x >> 5) - 1;        // consumer warps; warp W produces
+    WarpRing *rings = reinterpret_cast<WarpRing *>(base);
+    float *red = reinterpret_cast<float *>(base + (size_t)W * sizeof(WarpRing));
+    const int n0 = blockIdx.y * 32;
+    // Warp w consumes stages [w*stages_total/W, (w+1)*stages_total/W) of this
+    // CTA's K range; a stage is kVps whole groups.
+
+    if (warp == W) {  // ---------------- producer warp ----------------
+        if (lane == 0) {
+            for (int w = 0; w < W; ++w)
+                for (int s = 0; s < S; ++s) {
+                    mbar_init(&rings[w].full[s], 1);
+                    mbar_init(&rings[w].empty[s], 1);
+                }
+            fence_mbar_init();
+        }
+    }
+    __syncthreads();  // barriers initialised before anyone waits on them
+    if (warp == W) {
+        if (lane == 0) {
+            const uint32_t tx = kVps * (ROWS * 128 + 64 + (has_z ? 16 : 0));
+            bool ok = true;
+            const int most = (stages_total + W - 1) / W;
+            for (int it = 0; it < most && ok; ++it) {
+                const int s = it % S;
+                for (int w = 0; w < W && ok; ++w) {
+                    const int sb = w * stages_total / W, se = (w + 1) * stages_total / W;
+                    if (sb + it >= se) continue;
+                    WarpRing &r = rings[w];
+                    if (it >= S && !mbar_wait_bounded(&r.empty[s], (uint32_t)(((it / S) - 1) & 1))) {
+                        atomicExch(&g_wait_timeout, 1u);
+                        ok = false;
+                        break;
+                    }
+                    const int vg = (sb + it) * kVps;  // first group of the stage
+                    mbar_arrive_expect_tx(&r.full[s], tx);
+                    tma_load_2d(r.qw[s], &qw_map, n0, vg * ROWS, &r.full[s]);
+                    tma_load_2d(r.sc[s], &sc_map, n0, vg, &r.full[s]);
+                    if (has_z) tma_load_2d(r.zr[s], &zr_map, n0 / 8, vg, &r.full[s]);
+                }
+            }
+        }
+        return;  // consumers wait for every copy this warp issued
+    }
+
+    // ---------------- consumer warps ----------------
+    WarpRing &ring = rings[warp];
+    const int g = lane >> 2, t = lane & 3, sg = sigma(g);
+    const int tok0 = blockIdx.x * 8 * NT;
+    const int sbeg = warp * stages_total / W;
+    const int nstages = (warp + 1) * stages_total / W - sbeg;
+    const int nsteps = nstages * SSTEPS;
+    const int w0 = sbeg * kVps * ROWS;  // first qweight row of this warp
+    const T *ap[NT];
+    bool av[NT];
+    uint4 xa[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const int tok = tok0 + nt * 8 + g;
+        av[nt] = tok < M;
+        ap[nt] = A + (size_t)(av[nt] ? tok : 0) * K + (size_t)(w0 + t) * 8;
+        xa[nt] = (av[nt] && nsteps > 0) ? __ldg(reinterpret_cast<const uint4 *>(ap[nt])) : make_uint4(0, 0, 0, 0);
+        ap[nt] += 32;
+    }
+    // This lane's 16-byte chunk in row 4i + t of group vv of a stage tile; the
+    // 128-byte swizzle XORs the chunk index with the row index mod 8.
+    uint32_t roff[kVps][GSTEPS];
+#pragma unroll
+    for (int vv = 0; vv < kVps; ++vv)
+#pragma unroll
+        for (int i = 0; i < GSTEPS; ++i) {
+            const int r = vv * ROWS + 4 * i + t;
+            roff[vv][i] = r * 128 + ((sg ^ (r & 7)) << 4);
+        }
+    const uint32_t zsh = 16 * (sg & 1);
+    const uint32_t zbase = DeqT<T>::kMagicHalf + (has_z ? (uint32_t)zero_offset : 0u);
+
+    float facc[2][NT][4];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int b = 0; b < NT; ++b)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) facc[a][b][i] = 0.f;
+
+    uint32_t parity = 0;
+    bool ok = true;
+    for (int it0 = 0; it0 < nstages && ok; it0 += S, parity ^= 1u) {
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+            const int it = it0 + s;
+            if (it < nstages && ok) {
+                if (!__all_sync(0xffffffffu, mbar_wait_bounded(&ring.full[s], parity))) {
+                    if (lane == 0) atomicExch(&g_wait_timeout, 1u);
+                    ok = false;  // stop; this warp still meets the others below
+                } else {
+#pragma unroll
+                    for (int vv = 0; vv < kVps; ++vv) {
+                        const uint2 sw = *reinterpret_cast<const uint2 *>(ring.sc[s] + vv * 64 + 8 * sg);
+                        const uint32_t zw = has_z ? (*reinterpret_cast<const uint32_t *>(ring.zr[s] + vv * 16 + 4 * (sg >> 1)) >> zsh)
+                                                  : 0x8888u;
+                        uint32_t zc[4];
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) zc[c] = (zbase + ((zw >> (4 * c)) & 15u)) * 0x00010001u;
+                        float gacc[2][NT][4];
+#pragma unroll
+                        for (int a = 0; a < 2; ++a)
+#pragma unroll
+                            for (int b = 0; b < NT; ++b)
+#pragma unroll
+                                for (int i = 0; i < 4; ++i) gacc[a][b][i] = 0.f;
+#pragma unroll
+                        for (int i = 0; i < GSTEPS; ++i) {
+                            const int step = it * SSTEPS + vv * GSTEPS + i;
+                            const uint4 wv = *reinterpret_cast<const uint4 *>(ring.qw[s] + roff[vv][i]);
+                            uint32_t bf[NT][2][2];
+#pragma unroll
+                            for (int nt = 0; nt < NT; ++nt) {
+                                const uint4 x = xa[nt];
+                                if (av[nt] && step + 1 < nsteps) xa[nt] = __ldg(reinterpret_cast<const uint4 *>(ap[nt]));
+                                ap[nt] += 32;
+                                bf[nt][0][0] = __byte_perm(x.x, x.z, 0x5410);
+                                bf[nt][0][1] = __byte_perm(x.x, x.z, 0x7632);
+                                bf[nt][1][0] = __byte_perm(x.y, x.w, 0x5410);
+                                bf[nt][1][1] = __byte_perm(x.y, x.w, 0x7632);
+                            }
+                            const uint32_t wc[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                            for (int mt = 0; mt < 2; ++mt) {
+                                const uint32_t lo = wc[2 * mt], hi = wc[2 * mt + 1];
+#pragma unroll
+                                for (int q = 0; q < 2; ++q) {
+                                    const uint32_t a0 = DeqT<T>::sub(lop3_and_or(lo >> (8 * q), 0x000F000Fu, DeqT<T>::kMagic), zc[2 * mt]);
+                                    const uint32_t a1 = DeqT<T>::sub(lop3_and_or(hi >> (8 * q), 0x000F000Fu, DeqT<T>::kMagic), zc[2 * mt + 1]);
+                                    const uint32_t a2 = DeqT<T>::sub(lop3_and_or(lo >> (8 * q + 4), 0x000F000Fu, DeqT<T>::kMagic), zc[2 * mt]);
+                                    const uint32_t a3 = DeqT<T>::sub(lop3_and_or(hi >> (8 * q + 4), 0x000F000Fu, DeqT<T>::kMagic), zc[2 * mt + 1]);
+#pragma unroll
+                                    for (int nt = 0; nt < NT; ++nt)
+                                        mma_16816<T>(gacc[mt][nt], a0, a1, a2, a3, bf[nt][q][0], bf[nt][q][1]);
+                                }
+                            }
+                        }
+                        const float2 s01 = __half22float2(*reinterpret_cast<const __half2 *>(&sw.x));
+                        const float2 s23 = __half22float2(*reinterpret_cast<const __half2 *>(&sw.y));
+                        const float sc[4] = {s01.x, s01.y, s23.x, s23.y};
+#pragma unroll
+                        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                            for (int nt = 0; nt < NT; ++nt) {
+                                facc[mt][nt][0] = fmaf(gacc[mt][nt][0], sc[2 * mt], facc[mt][nt][0]);
+                                facc[mt][nt][1] = fmaf(gacc[mt][nt][1], sc[2 * mt], facc[mt][nt][1]);
+                                facc[mt][nt][2] = fmaf(gacc[mt][nt][2], sc[2 * mt + 1], facc[mt][nt][2]);
+                                facc[mt][nt][3] = fmaf(gacc[mt][nt][3], sc[2 * mt + 1], facc[mt][nt][3]);
+                            }
+                    }
+                    __syncwarp();  // every lane is done with stage s
+                    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&ring.empty[s])) : "memory");
+                }
+            }
+        }
+    }
+
+    // ---- K-split reduction across the W consumer warps ----
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) red[(warp * NE + (mt * NT + nt) * 4 + i) * 32 + lane] = facc[mt][nt][i];
+    asm volatile("bar.sync 1, %0;" ::"r"(W * 32) : "memory");  // consumers only
+    for (int idx = threadIdx.x; idx < NE * 32; idx += W * 32) {
+        float val = 0.f;
+        for (int w = 0; w < W; ++w) val += red[w * NE * 32 + idx];
+        const int e = idx >> 5, l = idx & 31;
+        const int mt = e / (NT * 4), nt = (e / 4) % NT, i = e & 3;
+        const int col = n0 + 4 * sigma(l >> 2) + 2 * mt + (i >> 1);
+        const int tok = tok0 + nt * 8 + 2 * (l & 3) + (i & 1);
+        if (tok < M) store_out(C, c_dtype, (size_t)tok * N + col, val);
+    }
+}
+
+// ---- host side ----
+static PFN_cuTensorMapEncodeTiled encode_fn() {
+    static std::mutex mu;
+    static PFN_cuTensorMapEncodeTiled fn = nullptr;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(p);
+    }
+    return fn;
+}
+
+static bool make_map_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *ptr, uint64_t d0, uint64_t d1,
+                        uint64_t row_bytes, uint32_t b0, uint32_t b1, CUtensorMapSwizzle swz) {
+    PFN_cuTensorMapEncodeTiled fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {d0, d1};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {b0, b1};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, dt, 2, const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename T, int NT, int GSTEPS>
+static int launch_tma_t(const void *a, const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
+                        void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset, cudaStream_t st) {
+    constexpr int NE = 2 * NT * 4;
+    if (gs != 32 * GSTEPS) return -1;  // one real group per virtual group only
+    const int nsm = num_sms();
+    const int nchunk = N / 32;
+    const int mblocks = (M + 8 * NT - 1) / (8 * NT);
+    const int nvg = K / gs;
+    if (nvg % kVps) return -1;  // whole stages only
+    const int stages_total = nvg / kVps;
+    const size_t per_warp = sizeof(WarpRing) + (size_t)NE * 32 * 4;
+    // Consumer warps per CTA (the K split): as many as fit when the whole grid is
+    // resident in one wave (ctas_per_sm CTAs sharing an SM's 224 KB), at most
+    // one per stage.
+    const long ctas = (long)nchunk * mblocks;
+    const long ctas_per_sm = (ctas + nsm - 1) / nsm;
+    long fit = ((224L * 1024) / ctas_per_sm - 1024) / (long)per_warp;
+    int W = (int)(fit < 1 ? 1 : (fit > kTmaMaxWarps ? kTmaMaxWarps : fit));
+    if (W > stages_total) W = stages_total;
+    CUtensorMap qw_map, sc_map, zr_map;
+    if (!make_map_2d(&qw_map, CU_TENSOR_MAP_DATA_TYPE_INT32, qweight, N, K / 8, (uint64_t)N * 4, 32,
+                     kVps * 4 * GSTEPS, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map_2d(&sc_map, CU_TENSOR_MAP_DATA_TYPE_UINT16, scales, N, K / gs, (uint64_t)N * 2, 32, kVps,
+                     CU_TENSOR_MAP_SWIZZLE_NONE))
+        return -1;
+    const int has_z = qzeros != nullptr;
+    if (has_z) {
+        if (!make_map_2d(&zr_map, CU_TENSOR_MAP_DATA_TYPE_INT32, qzeros, N / 8, K / gs, (uint64_t)N / 2, 4, kVps,
+                         CU_TENSOR_MAP_SWIZZLE_NONE))
+            return -1;
+    } else {
+        zr_map = sc_map;  // unused
+    }
+    auto kern = gptq_gemv_tma_kernel<T, NT, GSTEPS>;
+    {
+        static std::mutex mu;
+        static bool set_dev[128] = {};
+        int dev = 0;
+        W4_CUDA_TRY(cudaGetDevice(&dev));
+        std::lock_guard<std::mutex> lk(mu);
+        if (dev < 128 && !set_dev[dev]) {
+            W4_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+            W4_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+            set_dev[dev] = true;
+        }
+    }
+    const size_t smem = 1024 + (size_t)W * per_warp;
+    if (smem > 220 * 1024) return -1;
+    dim3 grid(mblocks, nchunk), block(32 * (W + 1));
+    kern<<<grid, block, smem, st>>>(qw_map, sc_map, zr_map, has_z, static_cast<const T *>(a), c, c_dtype, M, N, K,
+                                    zero_offset, stages_total);
+    W4_LAUNCH_CHECK();
+    return W4_OK;
+}
+
+template <typename T, int NT>
+static int launch_tma_nt(const void *a, const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
+                         void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset, cudaStream_t st) {
+    if (gs == 128) return launch_tma_t<T, NT, 4>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    if (gs == 64) return launch_tma_t<T, NT, 2>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    if (gs == 32) return launch_tma_t<T, NT, 1>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    return -1;
+}
+
+// Returns W4_OK, a W4 error, or -1 when the tensor maps cannot be encoded (the
+// caller then uses the register-batched kernel).
+int gptq_gemv_tma(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
+                  const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
+                  cudaStream_t st) {
+    if (a_dtype == W4_BF16) {
+        if (M <= 8) return launch_tma_nt<__nv_bfloat16, 1>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+        return launch_tma_nt<__nv_bfloat16, 2>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    }
+    if (M <= 8) return launch_tma_nt<__half, 1>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    return launch_tma_nt<__half, 2>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+}
+
+int take_wait_status() {
+    unsigned int v = 0;
+    W4_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_wait_timeout, sizeof(v)));
+    if (v) {
+        const unsigned int zero = 0;
+        W4_CUDA_TRY(cudaMemcpyToSymbol(g_wait_timeout, &zero, sizeof(zero)));
+        set_error("a device-side wait expired (bounded wait in a libw4 kernel)");
+        return W4_ERR_TIMEOUT;
+    }
+    return W4_OK;
+}
+
+}  // namespace w4

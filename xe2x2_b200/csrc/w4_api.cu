@@ -64,6 +64,11 @@ const char *w4_status_string(int status) {
 
 const char *w4_last_error(void) { return w4::last_error(); }
 
+int w4_check_device_status(void) {
+    w4::set_error("");
+    return w4::take_wait_status();
+}
+
 // ------------------------------------------------------------------ GPTQ
 static int check_gptq_common(const int32_t *qweight, const uint16_t *scales, int K, int N,
                              int group_size) {

@@ -16,6 +16,10 @@ int gather_cols(const uint16_t *a, const int32_t *perm, int M, int K, uint16_t *
 int gptq_gemv(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
               const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs,
               int zero_offset, cudaStream_t st);
+int gptq_gemv_tma(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
+                  const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
+                  cudaStream_t st);
+int take_wait_status();
 int gptq_s4a(const uint8_t *a, const uint8_t *b, const float *a_scale, const uint16_t *s,
              uint16_t *c, int rows, int cols, int dk, cudaStream_t st);
 
