@@ -275,11 +275,13 @@ def run_ours(args) -> None:
     ms = max_over_ranks(e0.elapsed_time(e1))
     value = step_bytes() * args.steps * world / (ms / 1e3) / 1e9
 
-    # ---------------- per-launch kernel durations (roofline of the GEMV kernel)
-    from xe2x2_b200.profile_driver import time_launches
+    # ---------------- per-launch kernel durations (roofline of the GEMV kernel):
+    # for each M, launches over the rotating weights captured back to back in one
+    # graph; CUDA events around its replays give the mean launch duration.
+    from xe2x2_b200.profile_driver import time_graph
     per_m = {}
     for M in MS:
-        us = statistics.median(time_launches(lambda r, M=M: gemm(M, weights[r % R], outs[M]), 30))
+        us = time_graph(lambda r, M=M: gemm(M, weights[r % R], outs[M]), max(30, 2 * R))
         per_m[str(M)] = {"us": round(us, 3), "GB/s": round(alg_bytes(M) / us / 1e3, 1)}
     tot_b = sum(alg_bytes(M) for M in MS)
     tot_us = sum(per_m[str(M)]["us"] for M in MS)

@@ -19,6 +19,7 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "w4_common.cuh"
 #include "w4_internal.h"
@@ -30,19 +31,27 @@ static __device__ unsigned int g_wait_timeout;  // a bounded wait expired (stick
 constexpr int kTmaStages = 3;   // ring depth per consumer warp
 constexpr int kVps = 2;         // virtual groups per stage
 constexpr int kTmaMaxWarps = 8; // consumer warps per CTA (one more warp produces)
+// Register cap: 4 CTAs of 4 warps (the usual one-wave shape) must fit an SM's
+// 64K registers, so 128 at most.
+constexpr int kTmaMaxRegs = 128;
 constexpr unsigned long long kWaitLimitNs = 200ull * 1000 * 1000;  // 200 ms
 
-// Per consumer warp: kTmaStages stages of kVps virtual groups.  Every tensor-copy
-// destination is 128-byte aligned (the swizzled tiles 1024).
-struct WarpRing {
-    uint8_t qw[kTmaStages][kVps * 2048];  // swizzled qweight tile (kVps x <= 16 rows x 128 B)
-    uint8_t sc[kTmaStages][128];          // kVps scale rows (32 x f16 each)
-    uint8_t zr[kTmaStages][128];          // kVps zero rows (4 x i32 each)
-    uint64_t full[kTmaStages];            // producer -> consumer (1 arrive + tx bytes)
-    uint64_t empty[kTmaStages];           // consumer -> producer (1 arrive)
-    uint8_t pad[1024 - (kTmaStages * 256 + kTmaStages * 16) % 1024];
+// Shared-memory ring of one consumer warp (byte offsets from its 1024-aligned
+// base; every tensor-copy destination is 128-byte aligned, the swizzled tiles
+// 1024):  S qweight stages | S activation stages | S constant stages (scales at
+// +0, zeros at +128) | S full + S empty mbarriers | the warp's reduction slot.
+struct RingLayout {
+    uint32_t qw_stage, act_stage, act, cst, bars, red, total;
+    __host__ __device__ RingLayout(int qw_bytes, int act_bytes, int red_bytes) {
+        qw_stage = qw_bytes;
+        act_stage = (act_bytes + 1023) & ~1023;
+        act = kTmaStages * qw_stage;
+        cst = act + kTmaStages * act_stage;
+        bars = cst + kTmaStages * 256;
+        red = (bars + 2 * kTmaStages * 8 + 127) & ~127u;
+        total = (red + red_bytes + 1023) & ~1023u;
+    }
 };
-static_assert(sizeof(WarpRing) % 1024 == 0, "rings stay 1024-byte aligned");
 
 // ---- PTX helpers (TMA + mbarrier) ----
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -89,6 +98,14 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
 }
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
 __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -114,40 +131,44 @@ template <> struct DeqT<__half> {
 // shared-load phase then hit 8 distinct bank groups.
 __device__ __forceinline__ int sigma(int g) { return (g >> 1) | ((g & 1) << 2); }
 
-template <typename T, int NT, int GSTEPS>
-__global__ void __launch_bounds__((kTmaMaxWarps + 1) * 32)
+// ACT: activations arrive by TMA with the stage (rows of up to 8*NT tokens x the
+// stage's k range, a 3-D box over [K/64][M][64] so each 64-k row segment is one
+// 128-byte-swizzled line); otherwise each lane loads them from global memory one
+// step ahead.
+template <typename T, int NT, int GSTEPS, bool ACT>
+__global__ void __maxnreg__(kTmaMaxRegs)
 gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_constant__ CUtensorMap sc_map,
-                     const __grid_constant__ CUtensorMap zr_map, int has_z, const T *__restrict__ A,
-                     void *__restrict__ C, int c_dtype, int M, int N, int K, int zero_offset,
-                     int stages_total) {
+                     const __grid_constant__ CUtensorMap zr_map, const __grid_constant__ CUtensorMap act_map,
+                     int has_z, const T *__restrict__ A, void *__restrict__ C, int c_dtype, int M, int N, int K,
+                     int zero_offset, int stages_total, int act_rows) {
     constexpr int S = kTmaStages;
     constexpr int NE = 2 * NT * 4;
-    constexpr int ROWS = 4 * GSTEPS;           // qweight rows per virtual group
-    constexpr int SSTEPS = kVps * GSTEPS;      // k steps per stage
+    constexpr int ROWS = 4 * GSTEPS;           // qweight rows per group
+    constexpr int SSTEPS = kVps * GSTEPS;      // 32-k steps per stage
+    constexpr int KC = SSTEPS / 2;             // 64-k activation lines per token per stage
     extern __shared__ uint8_t smem_dyn[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int W = (blockDim.x >> 5) - 1;        // consumer warps; warp W produces
-    WarpRing *rings = reinterpret_cast<WarpRing *>(base);
-    float *red = reinterpret_cast<float *>(base + (size_t)W * sizeof(WarpRing));
+    const RingLayout L(kVps * ROWS * 128, ACT ? act_rows * SSTEPS * 64 : 0, NE * 32 * 4);
     const int n0 = blockIdx.y * 32;
-    // Warp w consumes stages [w*stages_total/W, (w+1)*stages_total/W) of this
-    // CTA's K range; a stage is kVps whole groups.
+    const int tok0 = blockIdx.x * 8 * NT;
+    // Warp w consumes stages [w*stages_total/W, (w+1)*stages_total/W) of K; a
+    // stage is kVps whole groups.
 
     if (warp == W) {  // ---------------- producer warp ----------------
         if (lane == 0) {
-            for (int w = 0; w < W; ++w)
-                for (int s = 0; s < S; ++s) {
-                    mbar_init(&rings[w].full[s], 1);
-                    mbar_init(&rings[w].empty[s], 1);
-                }
+            for (int w = 0; w < W; ++w) {
+                uint64_t *bars = reinterpret_cast<uint64_t *>(base + (size_t)w * L.total + L.bars);
+                for (int i = 0; i < 2 * S; ++i) mbar_init(&bars[i], 1);
+            }
             fence_mbar_init();
         }
     }
     __syncthreads();  // barriers initialised before anyone waits on them
     if (warp == W) {
         if (lane == 0) {
-            const uint32_t tx = kVps * (ROWS * 128 + 64 + (has_z ? 16 : 0));
+            const uint32_t tx = kVps * (ROWS * 128 + 64 + (has_z ? 16 : 0)) + (ACT ? act_rows * SSTEPS * 64 : 0);
             bool ok = true;
             const int most = (stages_total + W - 1) / W;
             for (int it = 0; it < most && ok; ++it) {
@@ -155,17 +176,20 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
                 for (int w = 0; w < W && ok; ++w) {
                     const int sb = w * stages_total / W, se = (w + 1) * stages_total / W;
                     if (sb + it >= se) continue;
-                    WarpRing &r = rings[w];
-                    if (it >= S && !mbar_wait_bounded(&r.empty[s], (uint32_t)(((it / S) - 1) & 1))) {
+                    uint8_t *r = base + (size_t)w * L.total;
+                    uint64_t *full = reinterpret_cast<uint64_t *>(r + L.bars) + s;
+                    uint64_t *empty = full + S;
+                    if (it >= S && !mbar_wait_bounded(empty, (uint32_t)(((it / S) - 1) & 1))) {
                         atomicExch(&g_wait_timeout, 1u);
                         ok = false;
                         break;
                     }
                     const int vg = (sb + it) * kVps;  // first group of the stage
-                    mbar_arrive_expect_tx(&r.full[s], tx);
-                    tma_load_2d(r.qw[s], &qw_map, n0, vg * ROWS, &r.full[s]);
-                    tma_load_2d(r.sc[s], &sc_map, n0, vg, &r.full[s]);
-                    if (has_z) tma_load_2d(r.zr[s], &zr_map, n0 / 8, vg, &r.full[s]);
+                    mbar_arrive_expect_tx(full, tx);
+                    tma_load_2d(r + s * L.qw_stage, &qw_map, n0, vg * ROWS, full);
+                    if (ACT) tma_load_3d(r + L.act + s * L.act_stage, &act_map, 0, tok0, (vg * ROWS) / 8, full);  // 64-k line of the stage
+                    tma_load_2d(r + L.cst + s * 256, &sc_map, n0, vg, full);
+                    if (has_z) tma_load_2d(r + L.cst + s * 256 + 128, &zr_map, n0 / 8, vg, full);
                 }
             }
         }
@@ -173,25 +197,39 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
     }
 
     // ---------------- consumer warps ----------------
-    WarpRing &ring = rings[warp];
+    uint8_t *ring = base + (size_t)warp * L.total;
+    uint64_t *fullb = reinterpret_cast<uint64_t *>(ring + L.bars);
+    float *red = reinterpret_cast<float *>(ring + L.red);
     const int g = lane >> 2, t = lane & 3, sg = sigma(g);
-    const int tok0 = blockIdx.x * 8 * NT;
     const int sbeg = warp * stages_total / W;
     const int nstages = (warp + 1) * stages_total / W - sbeg;
     const int nsteps = nstages * SSTEPS;
-    const int w0 = sbeg * kVps * ROWS;  // first qweight row of this warp
+    // Register-path activations (ACT == false).
     const T *ap[NT];
     bool av[NT];
     uint4 xa[NT];
+    // TMA-path activations: this lane's 16-byte chunk of step j (line kc = j/2,
+    // chunk 4*(j%2) + t) for token row 8*nt + g; rows past the box read row 0
+    // (their outputs are discarded).
+    uint32_t aoff[ACT ? SSTEPS : 1][NT];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-        const int tok = tok0 + nt * 8 + g;
-        av[nt] = tok < M;
-        ap[nt] = A + (size_t)(av[nt] ? tok : 0) * K + (size_t)(w0 + t) * 8;
-        xa[nt] = (av[nt] && nsteps > 0) ? __ldg(reinterpret_cast<const uint4 *>(ap[nt])) : make_uint4(0, 0, 0, 0);
-        ap[nt] += 32;
+        if constexpr (ACT) {
+            const int row = (nt * 8 + g) < act_rows ? nt * 8 + g : 0;
+#pragma unroll
+            for (int j = 0; j < SSTEPS; ++j) {
+                const int line = (j >> 1) * act_rows + row;
+                aoff[j][nt] = line * 128 + (((4 * (j & 1) + t) ^ (line & 7)) << 4);
+            }
+        } else {
+            const int tok = tok0 + nt * 8 + g;
+            av[nt] = tok < M;
+            ap[nt] = A + (size_t)(av[nt] ? tok : 0) * K + (size_t)(sbeg * kVps * ROWS + t) * 8;
+            xa[nt] = (av[nt] && nsteps > 0) ? __ldg(reinterpret_cast<const uint4 *>(ap[nt])) : make_uint4(0, 0, 0, 0);
+            ap[nt] += 32;
+        }
     }
-    // This lane's 16-byte chunk in row 4i + t of group vv of a stage tile; the
+    // This lane's 16-byte chunk in qweight row 4i + t of group vv of a stage; the
     // 128-byte swizzle XORs the chunk index with the row index mod 8.
     uint32_t roff[kVps][GSTEPS];
 #pragma unroll
@@ -219,14 +257,17 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
         for (int s = 0; s < S; ++s) {
             const int it = it0 + s;
             if (it < nstages && ok) {
-                if (!__all_sync(0xffffffffu, mbar_wait_bounded(&ring.full[s], parity))) {
+                if (!__all_sync(0xffffffffu, mbar_wait_bounded(&fullb[s], parity))) {
                     if (lane == 0) atomicExch(&g_wait_timeout, 1u);
                     ok = false;  // stop; this warp still meets the others below
                 } else {
+                    const uint8_t *qws = ring + s * L.qw_stage;
+                    const uint8_t *acts = ring + L.act + s * L.act_stage;
+                    const uint8_t *cst = ring + L.cst + s * 256;
 #pragma unroll
                     for (int vv = 0; vv < kVps; ++vv) {
-                        const uint2 sw = *reinterpret_cast<const uint2 *>(ring.sc[s] + vv * 64 + 8 * sg);
-                        const uint32_t zw = has_z ? (*reinterpret_cast<const uint32_t *>(ring.zr[s] + vv * 16 + 4 * (sg >> 1)) >> zsh)
+                        const uint2 sw = *reinterpret_cast<const uint2 *>(cst + vv * 64 + 8 * sg);
+                        const uint32_t zw = has_z ? (*reinterpret_cast<const uint32_t *>(cst + 128 + vv * 16 + 4 * (sg >> 1)) >> zsh)
                                                   : 0x8888u;
                         uint32_t zc[4];
 #pragma unroll
@@ -240,14 +281,20 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
                                 for (int i = 0; i < 4; ++i) gacc[a][b][i] = 0.f;
 #pragma unroll
                         for (int i = 0; i < GSTEPS; ++i) {
-                            const int step = it * SSTEPS + vv * GSTEPS + i;
-                            const uint4 wv = *reinterpret_cast<const uint4 *>(ring.qw[s] + roff[vv][i]);
+                            const int j = vv * GSTEPS + i;  // step within the stage
+                            const uint4 wv = *reinterpret_cast<const uint4 *>(qws + roff[vv][i]);
                             uint32_t bf[NT][2][2];
 #pragma unroll
                             for (int nt = 0; nt < NT; ++nt) {
-                                const uint4 x = xa[nt];
-                                if (av[nt] && step + 1 < nsteps) xa[nt] = __ldg(reinterpret_cast<const uint4 *>(ap[nt]));
-                                ap[nt] += 32;
+                                uint4 x;
+                                if constexpr (ACT) {
+                                    x = *reinterpret_cast<const uint4 *>(acts + aoff[j][nt]);
+                                } else {
+                                    x = xa[nt];
+                                    if (av[nt] && it * SSTEPS + j + 1 < nsteps)
+                                        xa[nt] = __ldg(reinterpret_cast<const uint4 *>(ap[nt]));
+                                    ap[nt] += 32;
+                                }
                                 bf[nt][0][0] = __byte_perm(x.x, x.z, 0x5410);
                                 bf[nt][0][1] = __byte_perm(x.x, x.z, 0x7632);
                                 bf[nt][1][0] = __byte_perm(x.y, x.w, 0x5410);
@@ -283,7 +330,7 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
                             }
                     }
                     __syncwarp();  // every lane is done with stage s
-                    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&ring.empty[s])) : "memory");
+                    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&fullb[S + s])) : "memory");
                 }
             }
         }
@@ -295,11 +342,11 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) red[(warp * NE + (mt * NT + nt) * 4 + i) * 32 + lane] = facc[mt][nt][i];
+            for (int i = 0; i < 4; ++i) red[((mt * NT + nt) * 4 + i) * 32 + lane] = facc[mt][nt][i];
     asm volatile("bar.sync 1, %0;" ::"r"(W * 32) : "memory");  // consumers only
     for (int idx = threadIdx.x; idx < NE * 32; idx += W * 32) {
         float val = 0.f;
-        for (int w = 0; w < W; ++w) val += red[w * NE * 32 + idx];
+        for (int w = 0; w < W; ++w) val += reinterpret_cast<const float *>(base + (size_t)w * L.total + L.red)[idx];
         const int e = idx >> 5, l = idx & 31;
         const int mt = e / (NT * 4), nt = (e / 4) % NT, i = e & 3;
         const int col = n0 + 4 * sigma(l >> 2) + 2 * mt + (i >> 1);
@@ -335,10 +382,26 @@ static bool make_map_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *pt
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <typename T, int NT, int GSTEPS>
+// Activations as a 3-D tensor [K/64][M][64] (innermost first: 64 k, M tokens,
+// K/64 line groups), so one box of {64, rows, KC} lands as KC x rows 128-byte
+// lines, each swizzled by its line index.
+static bool make_act_map(CUtensorMap *map, CUtensorMapDataType dt, const void *a, int M, int K, int rows, int kc) {
+    PFN_cuTensorMapEncodeTiled fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[3] = {64, (cuuint64_t)M, (cuuint64_t)(K / 64)};
+    const cuuint64_t strides[2] = {(cuuint64_t)K * 2, 128};
+    const cuuint32_t box[3] = {64, (cuuint32_t)rows, (cuuint32_t)kc};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, dt, 3, const_cast<void *>(a), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
+template <typename T, int NT, int GSTEPS, bool ACT>
 static int launch_tma_t(const void *a, const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
                         void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset, cudaStream_t st) {
     constexpr int NE = 2 * NT * 4;
+    constexpr int SSTEPS = kVps * GSTEPS;
     if (gs != 32 * GSTEPS) return -1;  // one real group per virtual group only
     const int nsm = num_sms();
     const int nchunk = N / 32;
@@ -346,7 +409,9 @@ static int launch_tma_t(const void *a, const int32_t *qweight, const int32_t *qz
     const int nvg = K / gs;
     if (nvg % kVps) return -1;  // whole stages only
     const int stages_total = nvg / kVps;
-    const size_t per_warp = sizeof(WarpRing) + (size_t)NE * 32 * 4;
+    const int act_rows = M < 8 * NT ? M : 8 * NT;
+    const RingLayout lay(kVps * 4 * GSTEPS * 128, ACT ? act_rows * SSTEPS * 64 : 0, NE * 32 * 4);
+    const size_t per_warp = lay.total;
     // Consumer warps per CTA (the K split): as many as fit when the whole grid is
     // resident in one wave (ctas_per_sm CTAs sharing an SM's 224 KB), at most
     // one per stage.
@@ -355,7 +420,9 @@ static int launch_tma_t(const void *a, const int32_t *qweight, const int32_t *qz
     long fit = ((224L * 1024) / ctas_per_sm - 1024) / (long)per_warp;
     int W = (int)(fit < 1 ? 1 : (fit > kTmaMaxWarps ? kTmaMaxWarps : fit));
     if (W > stages_total) W = stages_total;
-    CUtensorMap qw_map, sc_map, zr_map;
+    const CUtensorMapDataType adt =
+        std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    CUtensorMap qw_map, sc_map, zr_map, act_map;
     if (!make_map_2d(&qw_map, CU_TENSOR_MAP_DATA_TYPE_INT32, qweight, N, K / 8, (uint64_t)N * 4, 32,
                      kVps * 4 * GSTEPS, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_map_2d(&sc_map, CU_TENSOR_MAP_DATA_TYPE_UINT16, scales, N, K / gs, (uint64_t)N * 2, 32, kVps,
@@ -369,7 +436,12 @@ static int launch_tma_t(const void *a, const int32_t *qweight, const int32_t *qz
     } else {
         zr_map = sc_map;  // unused
     }
-    auto kern = gptq_gemv_tma_kernel<T, NT, GSTEPS>;
+    if (ACT) {
+        if (K % 64 || !make_act_map(&act_map, adt, a, M, K, act_rows, SSTEPS / 2)) return -1;
+    } else {
+        act_map = sc_map;  // unused
+    }
+    auto kern = gptq_gemv_tma_kernel<T, NT, GSTEPS, ACT>;
     {
         static std::mutex mu;
         static bool set_dev[128] = {};
@@ -385,8 +457,8 @@ static int launch_tma_t(const void *a, const int32_t *qweight, const int32_t *qz
     const size_t smem = 1024 + (size_t)W * per_warp;
     if (smem > 220 * 1024) return -1;
     dim3 grid(mblocks, nchunk), block(32 * (W + 1));
-    kern<<<grid, block, smem, st>>>(qw_map, sc_map, zr_map, has_z, static_cast<const T *>(a), c, c_dtype, M, N, K,
-                                    zero_offset, stages_total);
+    kern<<<grid, block, smem, st>>>(qw_map, sc_map, zr_map, act_map, has_z, static_cast<const T *>(a), c, c_dtype,
+                                    M, N, K, zero_offset, stages_total, act_rows);
     W4_LAUNCH_CHECK();
     return W4_OK;
 }
@@ -394,9 +466,10 @@ static int launch_tma_t(const void *a, const int32_t *qweight, const int32_t *qz
 template <typename T, int NT>
 static int launch_tma_nt(const void *a, const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
                          void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset, cudaStream_t st) {
-    if (gs == 128) return launch_tma_t<T, NT, 4>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
-    if (gs == 64) return launch_tma_t<T, NT, 2>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
-    if (gs == 32) return launch_tma_t<T, NT, 1>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    constexpr bool ACT = NT == 1;  // staged activations fit the ring only for <= 8 tokens
+    if (gs == 128) return launch_tma_t<T, NT, 4, ACT>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    if (gs == 64) return launch_tma_t<T, NT, 2, ACT>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    if (gs == 32) return launch_tma_t<T, NT, 1, ACT>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
     return -1;
 }
 

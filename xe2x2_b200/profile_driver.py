@@ -38,6 +38,31 @@ def time_launches(fn, reps: int) -> list[float]:
     return [evs[i].elapsed_time(evs[i + 1]) * 1e3 for i in range(reps)]
 
 
+def time_graph(fn, reps: int) -> float:
+    """Mean device time (us) of one ``fn(i)`` with ``reps`` calls captured in one
+    CUDA graph and replayed (no host work between launches)."""
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        for r in range(3):
+            fn(r)
+    torch.cuda.current_stream().wait_stream(st)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for r in range(reps):
+            fn(r)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / (5 * reps)
+
+
 def gptq_bytes(M, K, N, gs, asym=True):
     return K // 8 * N * 4 + K // gs * N * 2 + (K // gs * N // 8 * 4 if asym else 0) + M * K * 2 + M * N * 2
 
@@ -85,8 +110,9 @@ def main(argv=None):
         for i in range(max(3, copies)):
             run(i)
         us = statistics.median(time_launches(run, max(args.iters, 20)))
+        gus = time_graph(run, max(args.iters, 20, copies))
         nb = gptq_bytes(M, K, N, args.gs) if args.kernel == "gptq" else nvfp4_bytes(M, K, N)
-        results.append({"kernel": args.kernel, "M": M, "K": K, "N": N, "us": round(us, 3),
+        results.append({"kernel": args.kernel, "M": M, "K": K, "N": N, "us": round(us, 3), "graph_us": round(gus, 3),
                         "GB/s": round(nb / us / 1e3, 1), "TFLOP/s": round(2 * M * N * K / us / 1e6, 2)})
     for r in results:
         print(json.dumps(r))
