@@ -359,6 +359,162 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+# ----------------------------------------------------------------------------- TP layer set
+TP_MS = (1, 32, 256)
+TP_WORKLOAD = ("config5: one 27B-class dense layer's GPTQ g128 projections (QKV N=7168 and gate|up N=34816 "
+               "column-parallel, o 5120x5120 and down K=17408 row-parallel with an NCCL all-reduce of bf16 "
+               "outputs), M in {1,32,256}, tensor-parallel over the ranks, attention math excluded")
+
+
+def run_tp(args) -> None:
+    """Tensor-parallel layer set (config 5) at TP = number of ranks: strong scaling."""
+    import torch
+    import torch.distributed as dist
+
+    from xe2x2_b200 import _lib as L
+    from xe2x2_b200 import tp
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    def trace(msg):
+        if args.trace:
+            print(f"[rank {rank}] {time.strftime('%H:%M:%S')} {msg}", file=sys.stderr, flush=True)
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    L.lib()
+    trace("process group up")
+    comm = tp.TPComm(rank, world, timeout_ms=120000, device=dev)
+    trace("communicator up")
+    props = torch.cuda.get_device_properties(dev)
+    l2 = getattr(props, "L2_cache_size", 126 * 2**20) or 126 * 2**20
+    sets = [tp.TPLayerSet(comm, rank, world, dev, seed=0)]
+    per_rank = sets[0].weight_bytes_per_rank()
+    R = max(2, math.ceil(2 * l2 / per_rank) + 1)
+    sets += [tp.TPLayerSet(comm, rank, world, dev, seed=1000 * r) for r in range(1, R)]
+    xs = {M: sets[0].inputs(M) for M in TP_MS}
+    outs = {M: {p.name: torch.empty((M, p.N // world if p.mode == "column" else p.N), dtype=torch.bfloat16,
+                                     device=dev) for p in sets[0].projs} for M in TP_MS}
+
+    def step(i):
+        for j, M in enumerate(TP_MS):
+            sets[(len(TP_MS) * i + j) % R].step(xs[M], outs[M])
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    period = R // math.gcd(len(TP_MS), R)
+    trace(f"{R} layer sets built")
+    for i in range(3):
+        step(i)
+    comm.wait()
+    barrier()
+    trace("eager warm-up done")
+    cap = torch.cuda.Stream()
+    cap.wait_stream(torch.cuda.current_stream())
+    graphs = []
+    with torch.cuda.stream(cap):
+        for ph in range(period):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                step(ph)
+            graphs.append(g)
+    torch.cuda.current_stream().wait_stream(cap)
+    barrier()
+    trace("graphs captured")
+    for i in range(args.warmup):
+        graphs[i % period].replay()
+    comm.wait()
+    trace("graph warm-up done")
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(args.steps):
+        graphs[i % period].replay()
+    e1.record(st)
+    trace("timed steps enqueued")
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    trace(f"timed region: {ms:.3f} ms")
+
+    # per-M layer time and all-reduce time alone (graphs of one M / of the bare collectives)
+    per_m = {}
+    for M in TP_MS:
+        gm = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(cap):
+            with torch.cuda.graph(gm, stream=cap):
+                for r in range(R):
+                    sets[r].step(xs[M], outs[M])
+        torch.cuda.current_stream().wait_stream(cap)
+        trace(f"M={M}: layer graph captured")
+        ga = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(cap):
+            with torch.cuda.graph(ga, stream=cap):
+                for r in range(R):
+                    comm.allreduce_(outs[M]["o"])
+                    comm.allreduce_(outs[M]["down"])
+        torch.cuda.current_stream().wait_stream(cap)
+        res = []
+        for g in (gm, ga):
+            for _ in range(3):
+                g.replay()
+            barrier()
+            e0.record(st)
+            for _ in range(5):
+                g.replay()
+            e1.record(st)
+            barrier()
+            res.append(max_over_ranks(e0.elapsed_time(e1)) * 1e3 / (5 * R))
+            trace(f"M={M}: {res[-1]:.2f} us")
+        per_m[str(M)] = {"layer_us": round(res[0], 2), "allreduce_us": round(res[1], 2),
+                         "TFLOP/s": round(sets[0].flops(M) / res[0] / 1e6, 2)}
+        del gm, ga, g  # graphs holding NCCL work must be gone before the communicator is
+    graphs.clear()
+    torch.cuda.synchronize()
+    comm.close()
+
+    full_w = sum(p.K // 8 * p.N * 4 + p.K // 128 * p.N * 2 + p.K // 128 * p.N // 8 * 4 for p in sets[0].projs)
+    step_bytes_tp = sum(full_w + sum(M * p.K * 2 + M * p.N * 2 for p in sets[0].projs) for M in TP_MS)
+    value = step_bytes_tp * args.steps / (ms / 1e3) / 1e9
+    peak, peak_src = measured_peak()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": TP_WORKLOAD, "parallelism": f"tp{world}",
+                       "step": "12 GEMMs + 6 all-reduces (4 projections x M=1,32,256) replayed from a CUDA graph",
+                       "l2": f"inputs larger than L2: {R} layer-set copies of {per_rank / 1e6:.1f} MB per rank",
+                       "algorithmic_bytes_per_step": step_bytes_tp,
+                       "flops_per_step": sum(sets[0].flops(M) for M in TP_MS)},
+            "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": round(peak * world, 1),
+                         "unit": "GB/s", "frac": round(value / (peak * world), 4), "traffic": None,
+                         "peak_source": f"{world} x {peak_src}", "per_m": per_m},
+            "gpu_launches": None, "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -366,11 +522,16 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--trace", action="store_true", help="progress lines on stderr")
+    ap.add_argument("--workload", choices=["decode", "tp"], default="decode",
+                    help="decode: config 2 sweep (default); tp: config 5 layer set at TP = --gpus")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "tp":
+        run_tp(args)
     else:
         run_ours(args)
 

@@ -221,6 +221,60 @@ int w4_rmsnorm_quant_s8(const uint16_t *x, int8_t *q, float *scale, int M, int K
 int w4_rowscale_fp8(const void *y, int y_dtype, uint8_t *q, float *row_scale, int M, int N,
                     void *stream);
 
+/* ===================================================================== */
+/* tensor parallelism                                                     */
+/* ===================================================================== */
+
+/* One process per GPU.  Column-parallel layers (QKV, gate|up) hold N/TP output
+ * columns of every sub-matrix and need no exchange; row-parallel layers (o,
+ * down) hold K/TP input rows (whole groups) and sum their partial [M,N]
+ * outputs with an NCCL all-reduce over NVLink.  The reference's counterpart is
+ * the collective alone: an in-place bf16 all_reduce(SUM) over torch's xccl
+ * backend (parallel/tp2/bench_xccl_p2p0.py:235-251). */
+typedef struct w4_tp_comm w4_tp_comm;
+
+enum w4_tp_mode {
+    W4_TP_COLUMN = 0,
+    W4_TP_ROW = 1
+};
+
+#define W4_TP_UNIQUE_ID_BYTES 128
+
+/* Rank 0 creates the id (host buffer of W4_TP_UNIQUE_ID_BYTES) and the host
+ * hands it to every rank by its own means (a store, MPI, a file). */
+int w4_tp_get_unique_id(uint8_t *id);
+
+/* Join the communicator of `nranks` ranks as `rank`, on the current CUDA
+ * device.  Returns W4_ERR_TIMEOUT (and creates nothing) when the other ranks
+ * have not joined within timeout_ms. */
+int w4_tp_comm_init(w4_tp_comm **comm, int nranks, int rank, const uint8_t *id, int timeout_ms);
+int w4_tp_comm_destroy(w4_tp_comm *comm);
+/* Tear down without waiting for the other ranks (after a failure on any rank). */
+int w4_tp_comm_abort(w4_tp_comm *comm);
+
+/* In-place sum over all ranks of buf[count] (f16 / bf16 / f32), enqueued on stream. */
+int w4_tp_allreduce(w4_tp_comm *comm, void *buf, size_t count, int dtype, void *stream);
+
+/* Wait (host side) until everything enqueued on stream is done.  If it is not
+ * done within timeout_ms (a peer never reached the collective) or NCCL reports
+ * an error, the communicator is aborted and W4_ERR_TIMEOUT / W4_ERR_NCCL is
+ * returned; an aborted communicator refuses further calls. */
+int w4_tp_wait(w4_tp_comm *comm, void *stream, int timeout_ms);
+
+size_t w4_tp_linear_workspace_bytes(int mode, int M, int N, int K, int group_size, int has_perm,
+                                    int c_dtype);
+
+/* One GPTQ linear shard.  Arguments as w4_gptq_gemm on this rank's shard:
+ *   W4_TP_COLUMN: qweight [K/8, N_rank] etc.; c [M, N_rank]; comm may be NULL.
+ *   W4_TP_ROW:    a [M, K_rank], qweight [K_rank/8, N], K_rank a multiple of
+ *                 group_size; c [M, N] receives the sum over ranks.  With
+ *                 c_dtype W4_E4M3 the sum is taken in f32 (workspace) and then
+ *                 cast with its per-row scale. */
+int w4_tp_linear(w4_tp_comm *comm, int mode, const void *a, int a_dtype, const int32_t *qweight,
+                 const int32_t *qzeros, const uint16_t *scales, const int32_t *perm, void *c,
+                 int c_dtype, float *row_scale, int M, int N, int K, int group_size,
+                 int zero_offset, void *workspace, size_t workspace_bytes, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,180 @@
+"""Tensor-parallel layers on 2 GPUs: w4_tp_linear (column / row) through libw4's
+NCCL communicator against the unsharded single-GPU GEMM, the collective's
+identity check (parallel/tp2/bench_xccl_p2p0.py:235-245: ranks add r+1), and
+the bounded waits: a rank that never joins the communicator, or never reaches
+a collective, makes the other rank's call return W4_ERR_TIMEOUT.
+
+Each case runs as child processes (one per GPU) bootstrapped over gloo, with
+NVLS off (NCCL_NVLS_ENABLE=0).  A rank leaves only between steps, with
+nothing of its own in flight.  Skipped with fewer than 2 GPUs.
+"""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rel(x, y):
+    x, y = x.float(), y.float()
+    return float((x - y).norm() / y.norm())
+
+
+def _case_layers(rank, world):
+    from xe2x2_b200 import _lib as L, ops, synth, tp
+
+    dev = torch.device("cuda", rank)
+    comm = tp.TPComm(rank, world, timeout_ms=60000, device=dev)
+    try:
+        # identity check of the collective
+        t = torch.full((4096,), float(rank + 1), dtype=torch.bfloat16, device=dev)
+        comm.allreduce_(t)
+        comm.wait()
+        assert torch.all(t == float(sum(r + 1 for r in range(world))))
+
+        gs = 128
+        for M in (1, 32, 256):
+            # column-parallel QKV-like matrix with head-aligned splits
+            K, splits = 1024, (512, 256, 256)
+            N = sum(splits)
+            qw, qz, sc, _ = synth.gptq_weights(K, N, gs, asym=True, seed=11, device=dev)
+            a = synth.activations(M, K, torch.bfloat16, seed=M, device=dev)
+            full = ops.gptq_gemm(a, qw, qz, sc, gs, 1, out_dtype=torch.float32)
+            lay = tp.TPLinear(comm, "column", *tp.shard_columns(qw, qz, sc, rank, world, splits), group_size=gs)
+            got = lay(a, out_dtype=torch.float32)
+            want = torch.cat([full[:, s] for s in tp.column_slices(splits, rank, world)], dim=1)
+            assert _rel(got, want) < 1e-6
+
+            # row-parallel: f32, bf16 and fp8 row-scaled outputs
+            K, N = 2048, 512
+            qw, qz, sc, _ = synth.gptq_weights(K, N, gs, asym=True, seed=12, device=dev)
+            a = synth.activations(M, K, torch.bfloat16, seed=100 + M, device=dev)
+            full = ops.gptq_gemm(a, qw, qz, sc, gs, 1, out_dtype=torch.float32)
+            lay = tp.TPLinear(comm, "row", *tp.shard_rows(qw, qz, sc, rank, world, gs), group_size=gs)
+            xs = a[:, tp.row_input_slice(K, rank, world)].contiguous()
+            got32 = lay(xs, out_dtype=torch.float32)
+            got16 = lay(xs, out_dtype=torch.bfloat16)
+            q8, rs = lay(xs, out_dtype=torch.float8_e4m3fn)
+            comm.wait()
+            assert _rel(got32, full) < 1e-5
+            assert _rel(got16, full) < 1e-2
+            deq = q8.float() * rs[:, None]
+            assert _rel(deq, full) < 4e-2
+            ref_rs = full.abs().amax(dim=1) / 448.0
+            assert torch.allclose(rs, ref_rs, rtol=1e-5)
+        assert L.lib().w4_check_device_status() == L.W4_OK
+    finally:
+        comm.close()
+
+
+def _case_init_timeout(rank, world):
+    """Rank 1 never joins: rank 0's communicator init gives up with W4_ERR_TIMEOUT."""
+    import ctypes
+
+    import torch.distributed as dist
+
+    from xe2x2_b200 import _lib as L
+
+    buf = (ctypes.c_uint8 * L.W4_TP_UNIQUE_ID_BYTES)()
+    if rank == 0:
+        L.call("w4_tp_get_unique_id", ctypes.cast(buf, ctypes.c_void_p))
+    dist.barrier()
+    if rank == 0:
+        torch.cuda.set_device(0)
+        h = ctypes.c_void_p()
+        rc = L.lib().w4_tp_comm_init(ctypes.byref(h), world, 0, ctypes.cast(buf, ctypes.c_void_p), 2000)
+        assert rc == L.W4_ERR_TIMEOUT, (rc, L.lib().w4_last_error())
+        assert not h.value
+    dist.barrier()
+
+
+def _case_collective_timeout(rank, world):
+    """Rank 1 skips one all-reduce (it enqueues nothing): rank 0's bounded wait
+    aborts its communicator and reports W4_ERR_TIMEOUT; both ranks then tear
+    down without waiting for each other."""
+    import torch.distributed as dist
+
+    from xe2x2_b200 import _lib as L, tp
+
+    dev = torch.device("cuda", rank)
+    comm = tp.TPComm(rank, world, timeout_ms=60000, device=dev)
+    t = torch.ones(1024, dtype=torch.float32, device=dev)
+    comm.allreduce_(t)
+    comm.wait()
+    assert torch.all(t == world)
+    dist.barrier()  # every rank is between steps
+    if rank == 0:
+        comm.allreduce_(t)
+        with pytest.raises(L.W4Error) as ei:
+            comm.wait(timeout_ms=1500)
+        assert ei.value.status == L.W4_ERR_TIMEOUT
+        comm.abort()
+        torch.cuda.synchronize(dev)  # the aborted collective has left the GPU
+    dist.barrier()
+    if rank != 0:
+        comm.abort()
+
+
+def _child(rank, world, port, case, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    try:
+        globals()[case](rank, world)
+        q.put((rank, "ok"))
+    except BaseException as e:  # report to the parent rather than hang it
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(case):
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip(f"needs {WORLD} GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_child, args=(r, WORLD, port, case, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(WORLD):
+            r, v = q.get(timeout=300)
+            res[r] = v
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert res == {r: "ok" for r in range(WORLD)}, res
+
+
+def test_tp_layers_match_unsharded():
+    _run("_case_layers")
+
+
+def test_tp_init_timeout_when_a_rank_never_joins():
+    _run("_case_init_timeout")
+
+
+def test_tp_collective_timeout_when_a_rank_skips():
+    _run("_case_collective_timeout")

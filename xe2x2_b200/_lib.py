@@ -17,6 +17,8 @@ W4_OK, W4_ERR_INVALID, W4_ERR_UNSUPPORTED, W4_ERR_CUDA, W4_ERR_TIMEOUT, W4_ERR_N
 W4_F16, W4_BF16, W4_F32, W4_E4M3, W4_S8 = range(5)
 W4_NVFP4_KN, W4_NVFP4_NK = 0, 1
 W4_ACT_W4A16, W4_ACT_NVFP4 = 0, 1
+W4_TP_COLUMN, W4_TP_ROW = 0, 1
+W4_TP_UNIQUE_ID_BYTES = 128
 
 HEADER = os.path.join(os.path.dirname(_build.HERE), "include", "w4.h")
 
@@ -51,6 +53,14 @@ _SIGS = {
     "w4_nvfp4_lut_gemm_s8a": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),
     "w4_rmsnorm_quant_s8": (_I, [_P, _P, _P, _I, _I, _F, _P]),
     "w4_rowscale_fp8": (_I, [_P, _I, _P, _P, _I, _I, _P]),
+    "w4_tp_get_unique_id": (_I, [_P]),
+    "w4_tp_comm_init": (_I, [ctypes.POINTER(_P), _I, _I, _P, _I]),
+    "w4_tp_comm_destroy": (_I, [_P]),
+    "w4_tp_comm_abort": (_I, [_P]),
+    "w4_tp_allreduce": (_I, [_P, _P, _Z, _I, _P]),
+    "w4_tp_wait": (_I, [_P, _P, _I]),
+    "w4_tp_linear_workspace_bytes": (_Z, [_I, _I, _I, _I, _I, _I, _I]),
+    "w4_tp_linear": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _P, _Z, _P]),
 }
 
 

@@ -145,7 +145,6 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
     constexpr int NE = 2 * NT * 4;
     constexpr int ROWS = 4 * GSTEPS;           // qweight rows per group
     constexpr int SSTEPS = kVps * GSTEPS;      // 32-k steps per stage
-    constexpr int KC = SSTEPS / 2;             // 64-k activation lines per token per stage
     extern __shared__ uint8_t smem_dyn[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;

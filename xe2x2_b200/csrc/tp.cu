@@ -1,0 +1,285 @@
+// tp.cu -- tensor-parallel GPTQ linear layers: column / row sharding with an
+// NCCL all-reduce of the row-parallel partial outputs.
+//
+// The reference's only tensor-parallel piece is the collective itself: an
+// in-place bf16 all_reduce(SUM) between two ranks through torch's xccl backend
+// (parallel/tp2/bench_xccl_p2p0.py:235-251, parallel/tp2/bench_host_ar.py:91-105).
+// Here one process drives one GPU; its communicator is an NCCL communicator
+// over NVLink/NVSwitch created from a 128-byte unique id that the ranks
+// exchange through whatever bootstrap the host has (torch.distributed's store
+// in the Python layer).
+//
+// NCCL is resolved at run time (dlopen of libnccl.so.2: the copy the process
+// already loaded, else the system one), so libw4 loads and its single-GPU
+// entry points work on hosts without NCCL; the w4_tp_* calls then return
+// W4_ERR_UNSUPPORTED.
+//
+// Failure handling: the communicator is created non-blocking, and
+// w4_tp_comm_init / w4_tp_wait poll with a time limit.  When a peer never
+// joins or never reaches the collective, the wait expires, the communicator
+// is aborted (NCCL stops its in-flight kernels) and W4_ERR_TIMEOUT is
+// returned; the communicator is unusable afterwards.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <chrono>
+#include <mutex>
+#include <thread>
+
+#include "w4_common.cuh"
+#include "w4_internal.h"
+
+struct w4_tp_comm {
+    ncclComm_t comm;
+    int nranks, rank;
+    int timeout_ms;  // bound on every host-side wait for this communicator
+    bool dead;
+};
+
+namespace w4 {
+namespace {
+
+struct NcclApi {
+    ncclResult_t (*get_unique_id)(ncclUniqueId *);
+    ncclResult_t (*comm_init_rank_config)(ncclComm_t *, int, ncclUniqueId, int, ncclConfig_t *);
+    ncclResult_t (*comm_get_async_error)(ncclComm_t, ncclResult_t *);
+    ncclResult_t (*comm_abort)(ncclComm_t);
+    ncclResult_t (*comm_finalize)(ncclComm_t);
+    ncclResult_t (*comm_destroy)(ncclComm_t);
+    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                               cudaStream_t);
+    const char *(*error_string)(ncclResult_t);
+    bool ok;
+};
+
+const NcclApi &nccl() {
+    static NcclApi api{};
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        auto sym = [&](const char *n) { return dlsym(h, n); };
+        api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(sym("ncclGetUniqueId"));
+        api.comm_init_rank_config =
+            reinterpret_cast<decltype(api.comm_init_rank_config)>(sym("ncclCommInitRankConfig"));
+        api.comm_get_async_error =
+            reinterpret_cast<decltype(api.comm_get_async_error)>(sym("ncclCommGetAsyncError"));
+        api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(sym("ncclCommAbort"));
+        api.comm_finalize = reinterpret_cast<decltype(api.comm_finalize)>(sym("ncclCommFinalize"));
+        api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(sym("ncclCommDestroy"));
+        api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(sym("ncclAllReduce"));
+        api.error_string = reinterpret_cast<decltype(api.error_string)>(sym("ncclGetErrorString"));
+        api.ok = api.get_unique_id && api.comm_init_rank_config && api.comm_get_async_error &&
+                 api.comm_abort && api.comm_finalize && api.comm_destroy && api.all_reduce && api.error_string;
+    });
+    return api;
+}
+
+#define W4_NCCL_API()                                                                                     \
+    const NcclApi &api = nccl();                                                                          \
+    W4_REQUIRE(api.ok, W4_ERR_UNSUPPORTED, "NCCL (libnccl.so.2) could not be loaded")
+
+int nccl_fail(const NcclApi &api, ncclResult_t r, const char *what) {
+    set_error("%s: NCCL error %d (%s)", what, (int)r, api.error_string(r));
+    return W4_ERR_NCCL;
+}
+
+using Clock = std::chrono::steady_clock;
+
+// Poll a non-blocking communicator until its pending operation (init) is done.
+int wait_comm_ready(const NcclApi &api, w4_tp_comm *c, int timeout_ms) {
+    const auto t0 = Clock::now();
+    for (;;) {
+        ncclResult_t st = ncclSuccess;
+        ncclResult_t r = api.comm_get_async_error(c->comm, &st);
+        if (r != ncclSuccess) return nccl_fail(api, r, "ncclCommGetAsyncError");
+        if (st == ncclSuccess) return W4_OK;
+        if (st != ncclInProgress) {
+            api.comm_abort(c->comm);
+            c->dead = true;
+            return nccl_fail(api, st, "communicator");
+        }
+        if (std::chrono::duration_cast<std::chrono::milliseconds>(Clock::now() - t0).count() > timeout_ms) {
+            api.comm_abort(c->comm);
+            c->dead = true;
+            set_error("NCCL communicator not ready after %d ms (a peer did not join); aborted", timeout_ms);
+            return W4_ERR_TIMEOUT;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(200));
+    }
+}
+
+ncclDataType_t nccl_dtype(int dt) {
+    switch (dt) {
+    case W4_F16: return ncclFloat16;
+    case W4_BF16: return ncclBfloat16;
+    default: return ncclFloat32;
+    }
+}
+
+}  // namespace
+}  // namespace w4
+
+using namespace w4;
+
+extern "C" int w4_tp_get_unique_id(uint8_t *id) {
+    set_error("");
+    W4_REQUIRE(id, W4_ERR_INVALID, "id buffer is required");
+    W4_NCCL_API();
+    static_assert(sizeof(ncclUniqueId) == W4_TP_UNIQUE_ID_BYTES, "unique id size");
+    ncclUniqueId uid;
+    ncclResult_t r = api.get_unique_id(&uid);
+    if (r != ncclSuccess) return nccl_fail(api, r, "ncclGetUniqueId");
+    memcpy(id, &uid, sizeof(uid));
+    return W4_OK;
+}
+
+extern "C" int w4_tp_comm_init(w4_tp_comm **out, int nranks, int rank, const uint8_t *id, int timeout_ms) {
+    set_error("");
+    W4_REQUIRE(out && id, W4_ERR_INVALID, "out and id are required");
+    W4_REQUIRE(nranks >= 1 && rank >= 0 && rank < nranks, W4_ERR_INVALID, "rank %d of %d", rank, nranks);
+    W4_REQUIRE(timeout_ms > 0, W4_ERR_INVALID, "timeout_ms must be positive");
+    *out = nullptr;
+    W4_NCCL_API();
+    ncclUniqueId uid;
+    memcpy(&uid, id, sizeof(uid));
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    w4_tp_comm *c = new w4_tp_comm{nullptr, nranks, rank, timeout_ms, false};
+    ncclResult_t r = api.comm_init_rank_config(&c->comm, nranks, uid, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        delete c;
+        return nccl_fail(api, r, "ncclCommInitRankConfig");
+    }
+    int rc = wait_comm_ready(api, c, timeout_ms);
+    if (rc) {
+        if (!c->dead) api.comm_abort(c->comm);
+        delete c;
+        return rc;
+    }
+    *out = c;
+    return W4_OK;
+}
+
+extern "C" int w4_tp_comm_destroy(w4_tp_comm *c) {
+    set_error("");
+    if (!c) return W4_OK;
+    W4_NCCL_API();
+    int rc = W4_OK;
+    if (c->dead) {
+        // already aborted: nothing left to release on the NCCL side
+    } else {
+        rc = wait_comm_ready(api, c, c->timeout_ms);  // no operation of ours still being enqueued
+        if (rc) {
+            delete c;
+            return rc;
+        }
+        ncclResult_t r = api.comm_finalize(c->comm);
+        if (r == ncclSuccess || r == ncclInProgress) rc = wait_comm_ready(api, c, c->timeout_ms);
+        else rc = nccl_fail(api, r, "ncclCommFinalize");
+        if (!c->dead) api.comm_destroy(c->comm);
+    }
+    delete c;
+    return rc;
+}
+
+extern "C" int w4_tp_comm_abort(w4_tp_comm *c) {
+    set_error("");
+    if (!c) return W4_OK;
+    W4_NCCL_API();
+    if (!c->dead) api.comm_abort(c->comm);
+    delete c;
+    return W4_OK;
+}
+
+extern "C" int w4_tp_allreduce(w4_tp_comm *c, void *buf, size_t count, int dtype, void *stream) {
+    set_error("");
+    W4_REQUIRE(c && buf, W4_ERR_INVALID, "comm and buf are required");
+    W4_REQUIRE(!c->dead, W4_ERR_INVALID, "communicator was aborted");
+    W4_REQUIRE(dtype == W4_F16 || dtype == W4_BF16 || dtype == W4_F32, W4_ERR_INVALID,
+               "dtype must be f16, bf16 or f32");
+    W4_NCCL_API();
+    if (count == 0 || c->nranks == 1) return W4_OK;
+    ncclResult_t r = api.all_reduce(buf, buf, count, nccl_dtype(dtype), ncclSum, c->comm,
+                                    reinterpret_cast<cudaStream_t>(stream));
+    if (r == ncclInProgress)  // a non-blocking communicator finishing the enqueue (e.g. first-use connections)
+        return wait_comm_ready(api, c, c->timeout_ms);
+    if (r != ncclSuccess) return nccl_fail(api, r, "ncclAllReduce");
+    return W4_OK;
+}
+
+extern "C" int w4_tp_wait(w4_tp_comm *c, void *stream, int timeout_ms) {
+    set_error("");
+    W4_REQUIRE(c, W4_ERR_INVALID, "comm is required");
+    W4_REQUIRE(!c->dead, W4_ERR_INVALID, "communicator was aborted");
+    W4_REQUIRE(timeout_ms > 0, W4_ERR_INVALID, "timeout_ms must be positive");
+    W4_NCCL_API();
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const auto t0 = Clock::now();
+    for (;;) {
+        cudaError_t q = cudaStreamQuery(st);
+        if (q == cudaSuccess) return W4_OK;
+        if (q != cudaErrorNotReady) {
+            set_error("stream error: %s", cudaGetErrorString(q));
+            return W4_ERR_CUDA;
+        }
+        ncclResult_t st_async = ncclSuccess;
+        api.comm_get_async_error(c->comm, &st_async);
+        if (st_async != ncclSuccess && st_async != ncclInProgress) {
+            api.comm_abort(c->comm);
+            c->dead = true;
+            return nccl_fail(api, st_async, "collective");
+        }
+        if (std::chrono::duration_cast<std::chrono::milliseconds>(Clock::now() - t0).count() > timeout_ms) {
+            api.comm_abort(c->comm);
+            c->dead = true;
+            set_error("stream not done after %d ms (a peer did not reach the collective); communicator aborted",
+                      timeout_ms);
+            return W4_ERR_TIMEOUT;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+extern "C" size_t w4_tp_linear_workspace_bytes(int mode, int M, int N, int K, int group_size, int has_perm,
+                                               int c_dtype) {
+    size_t ws = w4_gptq_workspace_bytes(M, N, K, group_size, has_perm, c_dtype == W4_E4M3 ? W4_F32 : c_dtype);
+    if (c_dtype == W4_E4M3) ws = (ws + 255) / 256 * 256 + (size_t)M * N * 4;  // f32 partial, reduced in place
+    (void)mode;
+    return ws;
+}
+
+extern "C" int w4_tp_linear(w4_tp_comm *c, int mode, const void *a, int a_dtype, const int32_t *qweight,
+                            const int32_t *qzeros, const uint16_t *scales, const int32_t *perm, void *out,
+                            int c_dtype, float *row_scale, int M, int N, int K, int group_size,
+                            int zero_offset, void *workspace, size_t workspace_bytes, void *stream) {
+    set_error("");
+    W4_REQUIRE(mode == W4_TP_COLUMN || mode == W4_TP_ROW, W4_ERR_INVALID, "mode must be column or row");
+    if (mode == W4_TP_COLUMN)  // this rank's N columns; no exchange
+        return w4_gptq_gemm(a, a_dtype, qweight, qzeros, scales, perm, out, c_dtype, row_scale, M, N, K,
+                            group_size, zero_offset, workspace, workspace_bytes, stream);
+    W4_REQUIRE(c, W4_ERR_INVALID, "row-parallel needs a communicator");
+    W4_REQUIRE(!c->dead, W4_ERR_INVALID, "communicator was aborted");
+    const size_t need = w4_tp_linear_workspace_bytes(mode, M, N, K, group_size, perm != nullptr, c_dtype);
+    W4_REQUIRE(workspace_bytes >= need && (need == 0 || workspace), W4_ERR_INVALID,
+               "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+    if (c_dtype != W4_E4M3) {
+        // partial product over this rank's K rows, then the in-place sum
+        int rc = w4_gptq_gemm(a, a_dtype, qweight, qzeros, scales, perm, out, c_dtype, nullptr, M, N, K,
+                              group_size, zero_offset, workspace, workspace_bytes, stream);
+        if (rc) return rc;
+        return w4_tp_allreduce(c, out, (size_t)M * N, c_dtype, stream);
+    }
+    // fp8 row-scaled output: the scale needs the full sum, so reduce in f32 first
+    const size_t gws = w4_gptq_workspace_bytes(M, N, K, group_size, perm != nullptr, W4_F32);
+    char *wsb = static_cast<char *>(workspace);
+    float *part = reinterpret_cast<float *>(wsb + (gws + 255) / 256 * 256);
+    int rc = w4_gptq_gemm(a, a_dtype, qweight, qzeros, scales, perm, part, W4_F32, nullptr, M, N, K, group_size,
+                          zero_offset, workspace, gws, stream);
+    if (rc) return rc;
+    rc = w4_tp_allreduce(c, part, (size_t)M * N, W4_F32, stream);
+    if (rc) return rc;
+    W4_REQUIRE(row_scale, W4_ERR_INVALID, "e4m3 output needs row_scale");
+    return w4_rowscale_fp8(part, W4_F32, static_cast<uint8_t *>(out), row_scale, M, N, stream);
+}
