@@ -1,0 +1,397 @@
+// gptq_prefill.cu -- GPTQ int4 W4A16 prefill GEMM on the 5th-generation tensor
+// cores (tcgen05, sm_100a).
+//
+// Contract: the W4A16 GEMM of w4_gptq_gemm, C[m,n] = sum_k A[m,k] * w[k,n] with
+// w = s[g,n] * (q[k,n] - zero[g,n]); the reference's prefill kernel is launch()
+// of kernels/esimd_dpas/dpas_s4_gptq_db48.cpp:148-246 (same formula, s32
+// groups there, W4A16 here per the checkpoint layout).
+//
+// One CTA computes a 128 x BN tile of C (BN = 256, or 128 when N is not a
+// multiple of 256) with the fp32 accumulator in tensor memory (TMEM, BN
+// columns x 128 lanes).  Ten warps, specialised:
+//   warp 0     TMA producer: per 64-deep k-block, the A tile (128 x 64 bf16,
+//              128-byte swizzled) and the raw weight pieces (qweight 8 x BN
+//              int32, the group's scale row and packed zero row) into ring
+//              stage s, all completing on full[s].
+//   warp 1     MMA issuer: allocates TMEM; per k-block one elected thread
+//              issues four tcgen05.mma kind::f16 (M=128, N=BN, K=16) from
+//              shared-memory descriptors, then tcgen05.commit frees the A/raw
+//              stage (empty[s]) and the B stage (bempty[j]).
+//   warps 2-9  dequantisers: each thread owns one column n; it turns the k-block's
+//              eight int32 words of column n into 64 bf16 (or f16) weights
+//              bf16((q - z) * s), written as eight 16-byte chunks of row n of the
+//              K-major, 128-byte-swizzled B tile, then fences the writes to the
+//              async proxy and arrives on bfull[j].  Warps 2-5 then read the
+//              accumulator out of TMEM (32 lanes each) and store C.
+// (q - z) is exact in bf16; the product is rounded once to the MMA input type.
+// Every mbarrier wait is bounded (tma_util.cuh): on expiry the CTA stops its
+// loops, the MMA thread still signals completion, TMEM is freed, and
+// w4_check_device_status() reports W4_ERR_TIMEOUT.  No copy uses multicast.
+#include <type_traits>
+
+#include "tma_util.cuh"
+#include "w4_common.cuh"
+#include "w4_internal.h"
+
+namespace w4 {
+
+static __device__ unsigned int g_prefill_timeout;  // a bounded wait expired (sticky until read)
+
+namespace pf {
+
+constexpr int BM = 128, BK = 64;
+constexpr int S = 4;          // A + raw-weight ring depth
+constexpr int SB = 3;         // dequantised-B ring depth
+constexpr int kDeqWarps = 8;  // one thread per column of a 256-wide tile
+constexpr int kThreads = (2 + kDeqWarps) * 32;
+
+template <int BN> struct Layout {
+    static constexpr uint32_t A_BYTES = BM * BK * 2;         // 16 KB
+    static constexpr uint32_t B_BYTES = BN * BK * 2;         // 32 KB at BN = 256
+    static constexpr uint32_t QW_BYTES = (BK / 8) * BN * 4;  // 8 KB
+    static constexpr uint32_t SC_BYTES = BN * 2;             // one f16 scale row
+    static constexpr uint32_t ZR_SLOT = 128;                 // one packed zero row (BN/2 bytes), 128-aligned
+    static constexpr uint32_t A_OFF = 0;
+    static constexpr uint32_t B_OFF = A_OFF + S * A_BYTES;
+    static constexpr uint32_t QW_OFF = B_OFF + SB * B_BYTES;
+    static constexpr uint32_t SC_OFF = QW_OFF + S * QW_BYTES;
+    static constexpr uint32_t ZR_OFF = SC_OFF + S * SC_BYTES;
+    static constexpr uint32_t BAR_OFF = ZR_OFF + S * ZR_SLOT;  // full[S] empty[S] bfull[SB] bempty[SB] done
+    static constexpr uint32_t MISC_OFF = BAR_OFF + (2 * S + 2 * SB + 1) * 8;
+    static constexpr uint32_t TOTAL = MISC_OFF + 16;
+    static_assert(B_OFF % 1024 == 0 && QW_OFF % 128 == 0 && SC_OFF % 128 == 0 && ZR_OFF % 128 == 0,
+                  "TMA destinations: swizzled tiles 1024-aligned, others 128-aligned");
+    static_assert(BN / 2 <= ZR_SLOT, "zero row fits its slot");
+};
+
+// ---- tcgen05 helpers (cta_group::1) ----
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16, both operands K-major.
+__device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive once on the mbarrier when every tcgen05 operation this thread issued so far is done.
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// 32 lanes x 32 consecutive 32-bit TMEM columns into 32 registers per thread.
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row
+// groups 1024 bytes apart (SBO), version 1 (sm_100), base offset 0 (tiles are
+// 1024-aligned; a K step inside the swizzle atom moves the start address).
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: D f32, A/B f16 (0) or bf16 (1), both K-major, N>>3, M>>4.
+template <typename T, int BN> __host__ __device__ constexpr uint32_t idesc_f16() {
+    return (1u << 4) | ((std::is_same<T, __nv_bfloat16>::value ? 1u : 0u) << 7) |
+           ((std::is_same<T, __nv_bfloat16>::value ? 1u : 0u) << 10) | ((uint32_t)(BN >> 3) << 17) |
+           ((uint32_t)(BM >> 4) << 24);
+}
+
+template <typename T> struct Deq;
+template <> struct Deq<__nv_bfloat16> {
+    static constexpr uint32_t kMagic = 0x43004300u, kMagicHalf = 0x4300u;  // bf16 128 + q
+    static __device__ __forceinline__ uint32_t scale2(uint16_t s_f16) {
+        const __nv_bfloat16 b = __float2bfloat16_rn(__half2float(__ushort_as_half(s_f16)));
+        const uint32_t u = __bfloat16_as_ushort(b);
+        return u | (u << 16);
+    }
+    static __device__ __forceinline__ uint32_t sub_mul(uint32_t q, uint32_t z, uint32_t s) {
+        __nv_bfloat162 d = __hsub2(*reinterpret_cast<__nv_bfloat162 *>(&q), *reinterpret_cast<__nv_bfloat162 *>(&z));
+        d = __hmul2(d, *reinterpret_cast<__nv_bfloat162 *>(&s));
+        return *reinterpret_cast<uint32_t *>(&d);
+    }
+};
+template <> struct Deq<__half> {
+    static constexpr uint32_t kMagic = 0x64006400u, kMagicHalf = 0x6400u;  // f16 1024 + q
+    static __device__ __forceinline__ uint32_t scale2(uint16_t s_f16) { return (uint32_t)s_f16 | ((uint32_t)s_f16 << 16); }
+    static __device__ __forceinline__ uint32_t sub_mul(uint32_t q, uint32_t z, uint32_t s) {
+        __half2 d = __hsub2(*reinterpret_cast<__half2 *>(&q), *reinterpret_cast<__half2 *>(&z));
+        d = __hmul2(d, *reinterpret_cast<__half2 *>(&s));
+        return *reinterpret_cast<uint32_t *>(&d);
+    }
+};
+
+// Bounded wait that also gives up at once when another role already failed.
+__device__ __forceinline__ bool pf_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+    const uint32_t b = smem_u32(bar);
+    if (mbar_try_wait(b, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    while (!mbar_try_wait(b, parity)) {
+        if (*abort_flag) return false;
+        if (global_ns() - t0 > kWaitLimitNs) {
+            *abort_flag = 1;
+            atomicExch(&g_prefill_timeout, 1u);
+            return false;
+        }
+    }
+    return true;
+}
+
+template <typename T, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap qw_map,
+                    const __grid_constant__ CUtensorMap sc_map, const __grid_constant__ CUtensorMap zr_map,
+                    int has_z, void *__restrict__ C, int c_dtype, int M, int N, int K, int gs, int zero_offset) {
+    using Lay = Layout<BN>;
+    extern __shared__ uint8_t smem_dyn[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + Lay::BAR_OFF);
+    uint64_t *empty = full + S;
+    uint64_t *bfull = empty + S;
+    uint64_t *bempty = bfull + SB;
+    uint64_t *done = bempty + SB;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + Lay::MISC_OFF);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + Lay::MISC_OFF + 4);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+    const int nk = K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int j = 0; j < SB; ++j) {
+            mbar_init(&bfull[j], kDeqWarps);
+            mbar_init(&bempty[j], 1);
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, BN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            const uint32_t tx = Lay::A_BYTES + Lay::QW_BYTES + Lay::SC_BYTES + (has_z ? BN / 2 : 0);
+            for (int i = 0; i < nk; ++i) {
+                const int s = i % S;
+                if (i >= S && !pf_wait(&empty[s], (uint32_t)(((i / S) - 1) & 1), abort_flag)) break;
+                const int g = (i * BK) / gs;
+                mbar_arrive_expect_tx(&full[s], tx);
+                tma_load_2d(sm + Lay::A_OFF + s * Lay::A_BYTES, &a_map, i * BK, m0, &full[s]);
+                tma_load_2d(sm + Lay::QW_OFF + s * Lay::QW_BYTES, &qw_map, n0, i * (BK / 8), &full[s]);
+                tma_load_2d(sm + Lay::SC_OFF + s * Lay::SC_BYTES, &sc_map, n0, g, &full[s]);
+                if (has_z) tma_load_2d(sm + Lay::ZR_OFF + s * Lay::ZR_SLOT, &zr_map, n0 / 8, g, &full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16<T, BN>();
+            for (int i = 0; i < nk; ++i) {
+                const int s = i % S, j = i % SB;
+                if (!pf_wait(&full[s], (uint32_t)((i / S) & 1), abort_flag)) break;
+                if (!pf_wait(&bfull[j], (uint32_t)((i / SB) & 1), abort_flag)) break;
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(sm + Lay::A_OFF + s * Lay::A_BYTES);
+                const uint32_t b_addr = smem_u32(sm + Lay::B_OFF + j * Lay::B_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; ++kk)
+                    mma_f16_ss(tmem, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32), idesc,
+                               (i | kk) != 0);
+                tc_commit(&empty[s]);
+                tc_commit(&bempty[j]);
+            }
+            tc_commit(done);  // also on failure: nothing in flight, the epilogue still ends
+        }
+    } else {
+        // ---------------- dequantisers ----------------
+        constexpr int TPC = 256 / BN;  // threads per column
+        const int dt = threadIdx.x - 64;
+        const int n = dt % BN, r0 = dt / BN;
+        const uint32_t zsh = 4 * (n & 7);
+        const uint32_t zbase = Deq<T>::kMagicHalf + (has_z ? (uint32_t)zero_offset : 8u);
+        for (int i = 0; i < nk; ++i) {
+            const int s = i % S, j = i % SB;
+            bool ok = pf_wait(&full[s], (uint32_t)((i / S) & 1), abort_flag);
+            if (ok && i >= SB) ok = pf_wait(&bempty[j], (uint32_t)(((i / SB) - 1) & 1), abort_flag);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            const uint16_t sbits = reinterpret_cast<const uint16_t *>(sm + Lay::SC_OFF + s * Lay::SC_BYTES)[n];
+            const uint32_t zq =
+                has_z ? (reinterpret_cast<const uint32_t *>(sm + Lay::ZR_OFF + s * Lay::ZR_SLOT)[n >> 3] >> zsh) & 15u
+                      : 0u;
+            const uint32_t zc = (zbase + zq) * 0x00010001u;
+            const uint32_t sc = Deq<T>::scale2(sbits);
+            const uint32_t *qw = reinterpret_cast<const uint32_t *>(sm + Lay::QW_OFF + s * Lay::QW_BYTES);
+            uint8_t *brow = sm + Lay::B_OFF + j * Lay::B_BYTES + n * 128;
+#pragma unroll
+            for (int kr = r0; kr < 8; kr += TPC) {
+                const uint32_t w = qw[kr * BN + n];
+                const uint32_t d0 = Deq<T>::sub_mul(lop3_and_or(w, 0x000F000Fu, Deq<T>::kMagic), zc, sc);
+                const uint32_t d1 = Deq<T>::sub_mul(lop3_and_or(w >> 4, 0x000F000Fu, Deq<T>::kMagic), zc, sc);
+                const uint32_t d2 = Deq<T>::sub_mul(lop3_and_or(w >> 8, 0x000F000Fu, Deq<T>::kMagic), zc, sc);
+                const uint32_t d3 = Deq<T>::sub_mul(lop3_and_or(w >> 12, 0x000F000Fu, Deq<T>::kMagic), zc, sc);
+                uint4 o;  // k0..k7 in order: d_q holds (k_q, k_q+4)
+                o.x = __byte_perm(d0, d1, 0x5410);
+                o.y = __byte_perm(d2, d3, 0x5410);
+                o.z = __byte_perm(d0, d1, 0x7632);
+                o.w = __byte_perm(d2, d3, 0x7632);
+                *reinterpret_cast<uint4 *>(brow + ((kr ^ (n & 7)) << 4)) = o;
+            }
+            fence_proxy_async();  // make the generic-proxy writes visible to the tensor core
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bfull[j]);
+        }
+        // ---------------- epilogue (warps 2-5: TMEM lanes 32*(warp%4) ...) ----------------
+        if (warp < 6) {
+            const bool ok = pf_wait(done, 0u, abort_flag);
+            (void)ok;
+            tc_fence_after();
+            const int q = warp & 3;
+            const int row = m0 + 32 * q + lane;
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+                if (row < M) {
+                    const size_t base = (size_t)row * N + n0 + c0;
+                    if (c_dtype == W4_F32) {
+                        float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(C) + base);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            dst[e] = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
+                                                 __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
+                    } else {
+                        uint32_t p[16];
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) {
+                            const float x0 = __uint_as_float(v[2 * e]), x1 = __uint_as_float(v[2 * e + 1]);
+                            if (c_dtype == W4_BF16) {
+                                __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+                                p[e] = *reinterpret_cast<uint32_t *>(&h);
+                            } else {
+                                __half2 h = __floats2half2_rn(x0, x1);
+                                p[e] = *reinterpret_cast<uint32_t *>(&h);
+                            }
+                        }
+                        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(C) + base);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) dst[e] = make_uint4(p[4 * e], p[4 * e + 1], p[4 * e + 2], p[4 * e + 3]);
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, BN);
+    }
+}
+
+template <typename T, int BN>
+static int launch(const void *a, const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales, void *c,
+                  int c_dtype, int M, int N, int K, int gs, int zero_offset, cudaStream_t st) {
+    using Lay = Layout<BN>;
+    const CUtensorMapDataType adt =
+        std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    CUtensorMap a_map, qw_map, sc_map, zr_map;
+    if (!make_map_2d(&a_map, adt, a, K, M, (uint64_t)K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map_2d(&qw_map, CU_TENSOR_MAP_DATA_TYPE_INT32, qweight, N, K / 8, (uint64_t)N * 4, BN, BK / 8,
+                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map_2d(&sc_map, CU_TENSOR_MAP_DATA_TYPE_UINT16, scales, N, K / gs, (uint64_t)N * 2, BN, 1,
+                     CU_TENSOR_MAP_SWIZZLE_NONE))
+        return -1;
+    const int has_z = qzeros != nullptr;
+    if (has_z) {
+        if (!make_map_2d(&zr_map, CU_TENSOR_MAP_DATA_TYPE_INT32, qzeros, N / 8, K / gs, (uint64_t)N / 2, BN / 8, 1,
+                         CU_TENSOR_MAP_SWIZZLE_NONE))
+            return -1;
+    } else {
+        zr_map = sc_map;  // unused
+    }
+    auto kern = gptq_prefill_kernel<T, BN>;
+    const size_t smem = Lay::TOTAL + 1024;
+    {
+        static std::mutex mu;
+        static bool set_dev[128] = {};
+        int dev = 0;
+        W4_CUDA_TRY(cudaGetDevice(&dev));
+        std::lock_guard<std::mutex> lk(mu);
+        if (dev < 128 && !set_dev[dev]) {
+            W4_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            set_dev[dev] = true;
+        }
+    }
+    dim3 grid((M + BM - 1) / BM, N / BN), block(kThreads);
+    kern<<<grid, block, smem, st>>>(a_map, qw_map, sc_map, zr_map, has_z, c, c_dtype, M, N, K, gs, zero_offset);
+    W4_LAUNCH_CHECK();
+    return W4_OK;
+}
+
+}  // namespace pf
+
+// W4_OK / a W4 error, or -1 when this shape is not handled here (the caller
+// then runs the decode kernels).
+int gptq_prefill(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
+                 void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset, cudaStream_t st) {
+    if (K % pf::BK || gs % pf::BK || N % 128 || c_dtype == W4_E4M3) return -1;
+    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(qweight) |
+         reinterpret_cast<uintptr_t>(scales) | reinterpret_cast<uintptr_t>(qzeros)) & 15)
+        return -1;
+    const bool wide = N % 256 == 0;
+    if (a_dtype == W4_BF16)
+        return wide ? pf::launch<__nv_bfloat16, 256>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st)
+                    : pf::launch<__nv_bfloat16, 128>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    return wide ? pf::launch<__half, 256>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st)
+                : pf::launch<__half, 128>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+}
+
+int take_prefill_wait_status() {
+    unsigned int v = 0;
+    W4_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_prefill_timeout, sizeof(v)));
+    if (v) {
+        const unsigned int zero = 0;
+        W4_CUDA_TRY(cudaMemcpyToSymbol(g_prefill_timeout, &zero, sizeof(zero)));
+        set_error("a device-side wait expired in the GPTQ prefill GEMM");
+        return W4_ERR_TIMEOUT;
+    }
+    return W4_OK;
+}
+
+}  // namespace w4

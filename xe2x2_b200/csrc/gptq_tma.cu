@@ -15,12 +15,11 @@
 //
 // Bulk copies move whole tiles per instruction without holding registers, so
 // each SM keeps >100 KB of weight reads in flight while its warps compute.
-#include <cuda.h>
-#include <cudaTypedefs.h>
 
 #include <mutex>
 #include <type_traits>
 
+#include "tma_util.cuh"
 #include "w4_common.cuh"
 #include "w4_internal.h"
 
@@ -34,7 +33,6 @@ constexpr int kTmaMaxWarps = 8; // consumer warps per CTA (one more warp produce
 // Register cap: 4 CTAs of 4 warps (the usual one-wave shape) must fit an SM's
 // 64K registers, so 128 at most.
 constexpr int kTmaMaxRegs = 128;
-constexpr unsigned long long kWaitLimitNs = 200ull * 1000 * 1000;  // 200 ms
 
 // Shared-memory ring of one consumer warp (byte offsets from its 1024-aligned
 // base; every tensor-copy destination is 128-byte aligned, the swizzled tiles
@@ -52,63 +50,6 @@ struct RingLayout {
         total = (red + red_bytes + 1023) & ~1023u;
     }
 };
-
-// ---- PTX helpers (TMA + mbarrier) ----
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void fence_mbar_init() {
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t done;
-    asm volatile(
-        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}"
-        : "=r"(done)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return done != 0;
-}
-__device__ __forceinline__ unsigned long long global_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-// Wait for the phase with the given parity; false if kWaitLimitNs passed first.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
-    const uint32_t b = smem_u32(bar);
-    if (mbar_try_wait(b, parity)) return true;
-    const unsigned long long t0 = global_ns();
-    while (!mbar_try_wait(b, parity))
-        if (global_ns() - t0 > kWaitLimitNs) return false;
-    return true;
-}
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
-                                            uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z,
-                                            uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
-            smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
 template <typename T> struct DeqT;
 template <> struct DeqT<__nv_bfloat16> {
@@ -355,32 +296,6 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
 }
 
 // ---- host side ----
-static PFN_cuTensorMapEncodeTiled encode_fn() {
-    static std::mutex mu;
-    static PFN_cuTensorMapEncodeTiled fn = nullptr;
-    std::lock_guard<std::mutex> lk(mu);
-    if (!fn) {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(p);
-    }
-    return fn;
-}
-
-static bool make_map_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *ptr, uint64_t d0, uint64_t d1,
-                        uint64_t row_bytes, uint32_t b0, uint32_t b1, CUtensorMapSwizzle swz) {
-    PFN_cuTensorMapEncodeTiled fn = encode_fn();
-    if (!fn) return false;
-    const cuuint64_t dims[2] = {d0, d1};
-    const cuuint64_t strides[1] = {row_bytes};
-    const cuuint32_t box[2] = {b0, b1};
-    const cuuint32_t estr[2] = {1, 1};
-    return fn(map, dt, 2, const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 // Activations as a 3-D tensor [K/64][M][64] (innermost first: 64 k, M tokens,
 // K/64 line groups), so one box of {64, rows, KC} lands as KC x rows 128-byte
 // lines, each swizzled by its line index.

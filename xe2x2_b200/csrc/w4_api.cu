@@ -66,7 +66,9 @@ const char *w4_last_error(void) { return w4::last_error(); }
 
 int w4_check_device_status(void) {
     w4::set_error("");
-    return w4::take_wait_status();
+    const int r1 = w4::take_wait_status();
+    const int r2 = w4::take_prefill_wait_status();
+    return r1 ? r1 : r2;
 }
 
 // ------------------------------------------------------------------ GPTQ

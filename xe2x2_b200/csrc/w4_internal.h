@@ -20,6 +20,11 @@ int gptq_gemv_tma(const void *a, int a_dtype, const int32_t *qweight, const int3
                   const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
                   cudaStream_t st);
 int take_wait_status();
+// gptq_prefill.cu (tcgen05); -1 = shape not handled there
+int gptq_prefill(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
+                 void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset, cudaStream_t st);
+int take_prefill_wait_status();
+constexpr int kPrefillMinM = 17;  // token counts from here on run the tensor-core prefill GEMM
 int gptq_s4a(const uint8_t *a, const uint8_t *b, const float *a_scale, const uint16_t *s,
              uint16_t *c, int rows, int cols, int dk, cudaStream_t st);
 
