@@ -8,7 +8,7 @@
 //
 // One CTA computes a 128 x BN tile of C (BN = 256, or 128 when N is not a
 // multiple of 256) with the fp32 accumulator in tensor memory (TMEM, BN
-// columns x 128 lanes).  Ten warps, specialised:
+// columns x 128 lanes).  Eighteen warps, specialised:
 //   warp 0     TMA producer: per 64-deep k-block, the A tile (128 x 64 bf16,
 //              128-byte swizzled) and the raw weight pieces (qweight 8 x BN
 //              int32, the group's scale row and packed zero row) into ring
@@ -17,12 +17,12 @@
 //              issues four tcgen05.mma kind::f16 (M=128, N=BN, K=16) from
 //              shared-memory descriptors, then tcgen05.commit frees the A/raw
 //              stage (empty[s]) and the B stage (bempty[j]).
-//   warps 2-9  dequantisers: each thread owns one column n; it turns the k-block's
-//              eight int32 words of column n into 64 bf16 (or f16) weights
-//              bf16((q - z) * s), written as eight 16-byte chunks of row n of the
-//              K-major, 128-byte-swizzled B tile, then fences the writes to the
-//              async proxy and arrives on bfull[j].  Warps 2-5 then read the
-//              accumulator out of TMEM (32 lanes each) and store C.
+//   warps 2-17 dequantisers: TPC threads share column n; each turns 8/TPC of the
+//              k-block's eight int32 words of column n into 8 bf16 (or f16)
+//              weights bf16((q - z) * s) apiece, written as 16-byte chunks of row
+//              n of the K-major, 128-byte-swizzled B tile, then fences the writes
+//              to the async proxy and arrives on bfull[j].  Warps 2-5 then read
+//              the accumulator out of TMEM (32 lanes each) and store C.
 // (q - z) is exact in bf16; the product is rounded once to the MMA input type.
 // Every mbarrier wait is bounded (tma_util.cuh): on expiry the CTA stops its
 // loops, the MMA thread still signals completion, TMEM is freed, and
@@ -42,7 +42,7 @@ namespace pf {
 constexpr int BM = 128, BK = 64;
 constexpr int S = 4;          // A + raw-weight ring depth
 constexpr int SB = 3;         // dequantised-B ring depth
-constexpr int kDeqWarps = 8;  // one thread per column of a 256-wide tile
+constexpr int kDeqWarps = 16;  // two threads per column of a 256-wide tile
 constexpr int kThreads = (2 + kDeqWarps) * 32;
 
 template <int BN> struct Layout {
@@ -240,7 +240,7 @@ gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
         }
     } else {
         // ---------------- dequantisers ----------------
-        constexpr int TPC = 256 / BN;  // threads per column
+        constexpr int TPC = kDeqWarps * 32 / BN;  // threads per column
         const int dt = threadIdx.x - 64;
         const int n = dt % BN, r0 = dt / BN;
         const uint32_t zsh = 4 * (n & 7);
@@ -259,7 +259,8 @@ gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
             const uint32_t *qw = reinterpret_cast<const uint32_t *>(sm + Lay::QW_OFF + s * Lay::QW_BYTES);
             uint8_t *brow = sm + Lay::B_OFF + j * Lay::B_BYTES + n * 128;
 #pragma unroll
-            for (int kr = r0; kr < 8; kr += TPC) {
+            for (int t = 0; t < 8 / TPC; ++t) {  // compile-time trip count: the words interleave
+                const int kr = r0 + t * TPC;
                 const uint32_t w = qw[kr * BN + n];
                 const uint32_t d0 = Deq<T>::sub_mul(lop3_and_or(w, 0x000F000Fu, Deq<T>::kMagic), zc, sc);
                 const uint32_t d1 = Deq<T>::sub_mul(lop3_and_or(w >> 4, 0x000F000Fu, Deq<T>::kMagic), zc, sc);
@@ -374,7 +375,14 @@ int gptq_prefill(const void *a, int a_dtype, const int32_t *qweight, const int32
     if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(qweight) |
          reinterpret_cast<uintptr_t>(scales) | reinterpret_cast<uintptr_t>(qzeros)) & 15)
         return -1;
-    const bool wide = N % 256 == 0;
+    // 256-wide tiles unless 128-wide ones need fewer waves (a 128-wide tile takes
+    // about half as long): small M leaves SMs idle otherwise.
+    bool wide = N % 256 == 0;
+    if (wide) {
+        const long nsm = num_sms(), t256 = (long)((M + pf::BM - 1) / pf::BM) * (N / 256);
+        const long w256 = 2 * ((t256 + nsm - 1) / nsm), w128 = (2 * t256 + nsm - 1) / nsm;
+        if (w128 < w256) wide = false;
+    }
     if (a_dtype == W4_BF16)
         return wide ? pf::launch<__nv_bfloat16, 256>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st)
                     : pf::launch<__nv_bfloat16, 128>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
