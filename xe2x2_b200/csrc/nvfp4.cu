@@ -8,6 +8,7 @@
 // [K/16, N] in both.
 #include <cooperative_groups.h>
 
+#include "nvfp4_util.cuh"
 #include "w4_common.cuh"
 #include "w4_internal.h"
 
@@ -164,28 +165,6 @@ int nvfp4_kn_to_nk(const uint8_t *in, int K, int N, uint8_t *out, cudaStream_t s
 // bits, so the weight operand is exact and only the fp32 accumulation rounds.
 // The tensor scale multiplies the fp32 result.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void e2m1x4_to_bf16(uint32_t x, uint32_t &r01, uint32_t &r23) {
-    // |e2m1| in bf16: 0, .5, 1, 1.5 | 2, 3, 4, 6
-    constexpr uint32_t TL0 = 0xC0800000u, TL1 = 0xC0804000u;  // low bytes
-    constexpr uint32_t TH0 = 0x3F3F3F00u, TH1 = 0x40404040u;  // high bytes
-    const uint32_t sel = x & 0x7777u;
-    const uint32_t L = __byte_perm(TL0, TL1, sel);
-    const uint32_t Hp = __byte_perm(TH0, TH1, sel);
-    // sign of nibble i -> bit 7 of byte i: nibbles 1,3 have it at bits 7,15 of x,
-    // nibbles 0,2 at bits 3,11 (bits 7,15 of x << 4)
-    uint32_t sg;
-    asm("prmt.b32 %0, %1, %2, 0x1504;" : "=r"(sg) : "r"(x), "r"(x << 4));
-    const uint32_t H = lop3_and_or(sg, 0x80808080u, Hp);
-    r01 = __byte_perm(L, H, 0x5140);
-    r23 = __byte_perm(L, H, 0x7362);
-}
-
-__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
-    __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162 *>(&a),
-                               *reinterpret_cast<__nv_bfloat162 *>(&b));
-    return *reinterpret_cast<uint32_t *>(&r);
-}
-
 template <int SCALE_DT>
 __device__ __forceinline__ uint32_t load_scale2(const void *scale, size_t i) {
     uint32_t h;
@@ -375,6 +354,10 @@ int nvfp4_gemv(const uint16_t *a, const uint8_t *w, int layout, const void *scal
                int scale_dtype, const float *global_scale, void *c, int c_dtype, int M, int N,
                int K, cudaStream_t st) {
     (void)layout;  // NK only; validated by the caller
+    // TMA-streamed kernel (nvfp4_tma.cu) first; the register-streamed one below
+    // covers shapes it does not take.
+    const int rc = nvfp4_gemv_tma(a, w, scale, scale_dtype, global_scale, c, c_dtype, M, N, K, st);
+    if (rc >= 0) return rc;
     if (scale_dtype == W4_E4M3) {
         if (M <= 8) return launch_nvfp4_gemv_t<1, W4_E4M3>(a, w, scale, global_scale, c, c_dtype, M, N, K, st);
         if (M <= 16) return launch_nvfp4_gemv_t<2, W4_E4M3>(a, w, scale, global_scale, c, c_dtype, M, N, K, st);

@@ -100,4 +100,19 @@ inline bool make_map_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *pt
 }
 
 
+// Activations as a 3-D tensor [K/64][M][64] (innermost first: 64 k, M tokens,
+// K/64 line groups), so one box of {64, rows, KC} lands as KC x rows 128-byte
+// lines, each swizzled by its line index.
+inline bool make_act_map(CUtensorMap *map, CUtensorMapDataType dt, const void *a, int M, int K, int rows, int kc) {
+    PFN_cuTensorMapEncodeTiled fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[3] = {64, (cuuint64_t)M, (cuuint64_t)(K / 64)};
+    const cuuint64_t strides[2] = {(cuuint64_t)K * 2, 128};
+    const cuuint32_t box[3] = {64, (cuuint32_t)rows, (cuuint32_t)kc};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, dt, 3, const_cast<void *>(a), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
 }  // namespace w4

@@ -68,7 +68,8 @@ int w4_check_device_status(void) {
     w4::set_error("");
     const int r1 = w4::take_wait_status();
     const int r2 = w4::take_prefill_wait_status();
-    return r1 ? r1 : r2;
+    const int r3 = w4::take_fp4_wait_status();
+    return r1 ? r1 : r2 ? r2 : r3;
 }
 
 // ------------------------------------------------------------------ GPTQ

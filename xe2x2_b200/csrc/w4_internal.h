@@ -35,6 +35,9 @@ int nvfp4_quant_act(const uint16_t *a, int M, int K, const float *a_global, uint
                     uint8_t *sf, cudaStream_t st);
 int nvfp4_lut_s8a(const int8_t *a, const uint8_t *packed, const float *a_s, const float *b_s,
                   uint16_t *c, int rows, int cols, int dk, cudaStream_t st);
+int nvfp4_gemv_tma(const uint16_t *a, const uint8_t *w, const void *scale, int scale_dtype,
+                   const float *global_scale, void *c, int c_dtype, int M, int N, int K, cudaStream_t st);
+int take_fp4_wait_status();
 int nvfp4_gemv(const uint16_t *a, const uint8_t *w, int layout, const void *scale,
                int scale_dtype, const float *global_scale, void *c, int c_dtype, int M, int N,
                int K, cudaStream_t st);
