@@ -52,7 +52,8 @@ enum w4_dtype {
     W4_BF16 = 1,
     W4_F32 = 2,
     W4_E4M3 = 3, /* fp8 e4m3fn (bias 7, max 448, no inf) */
-    W4_S8 = 4
+    W4_S8 = 4,
+    W4_E4M3_ATOMS = 5 /* NVFP4 block scales already rearranged by w4_nvfp4_repack_scales */
 };
 
 /* NVFP4 packed-weight layouts (two E2M1 nibbles per byte, low nibble = even k). */
@@ -162,7 +163,8 @@ int w4_nvfp4_dequant(const uint8_t *w, int layout, const void *scale, int scale_
                      const float *global_scale, int K, int N, float *out, void *stream);
 
 /* Quantise bf16 activations to NVFP4, bit-exact with the host definition:
- *   sf = e4m3(amax16 / (6 * a_global)),  code = e2m1(a / (e4m3(sf) * a_global))
+ *   sf = e4m3(amax16 / (6 * a_global)),  d = e4m3(sf) * a_global,
+ *   code = e2m1(a * (1 / d))   (one correctly rounded reciprocal per block)
  * a: bf16 [M,K]; a_global: f32[1] device pointer (the tensor decode scale);
  * codes u8 [M,K/2] (low nibble = even k); sf u8 [M,K/16]. */
 int w4_nvfp4_quant_act(const uint16_t *a, int M, int K, const float *a_global,
@@ -191,6 +193,16 @@ int w4_nvfp4_gemm(const void *a, const uint8_t *w, int layout, const void *scale
  * u8 [N, K/2] that w4_nvfp4_gemm reads.  Block scales keep their [K/16, N]
  * layout.  w_nk must not alias w_kn. */
 int w4_nvfp4_repack_kn_to_nk(const uint8_t *w_kn, int K, int N, uint8_t *w_nk, void *stream);
+
+/* Load-time rearrangement of E4M3 block scales [K/16, N] into the layout the
+ * block-scaled tensor-core GEMM reads (act_mode W4_ACT_NVFP4): 512-byte atoms of
+ * 128 columns x 4 blocks, byte (n % 32) * 16 + (n / 32 % 4) * 4 + (kb % 4), atoms
+ * ordered [n / 128][kb / 4]; N rounded up to 128 with zero scales.  Size
+ * w4_nvfp4_scale_atoms_bytes(N, K).  Pass the result to w4_nvfp4_gemm with
+ * scale_dtype W4_E4M3_ATOMS (the per-call rearrangement is then skipped).
+ * No counterpart in the reference (its NVFP4 operator is external). */
+size_t w4_nvfp4_scale_atoms_bytes(int N, int K);
+int w4_nvfp4_repack_scales(const uint8_t *scale, int K, int N, uint8_t *atoms, void *stream);
 
 /* The reference LUT kernel's own contract, same arguments in the same order as
  * launch(q, ad, pd, asd, bsd, cd, rows, cols, dk) of

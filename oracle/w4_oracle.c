@@ -424,10 +424,12 @@ void orc_nvfp4_quant_act(const float *a, int M, int K, float global_dec, uint8_t
             for (int i = 0; i < 16; ++i) { float v = fabsf(x[i]); if (v > amax) amax = v; }
             uint8_t s = orc_e4m3_from_f32(amax / denom6);
             float sdec = orc_e4m3_value(s) * global_dec;
+            /* one correctly rounded reciprocal per block, then a product per element */
+            float inv = sdec != 0.f ? 1.0f / sdec : 0.f;
             sf[(size_t)m * (K / 16) + b] = s;
             for (int i = 0; i < 16; i += 2) {
-                uint8_t lo = sdec != 0.f ? orc_e2m1_from_f32(x[i] / sdec) : 0;
-                uint8_t hi = sdec != 0.f ? orc_e2m1_from_f32(x[i + 1] / sdec) : 0;
+                uint8_t lo = sdec != 0.f ? orc_e2m1_from_f32(x[i] * inv) : 0;
+                uint8_t hi = sdec != 0.f ? orc_e2m1_from_f32(x[i + 1] * inv) : 0;
                 codes[(size_t)m * (K / 2) + (size_t)b * 8 + i / 2] = (uint8_t)(lo | (hi << 4));
             }
         }

@@ -14,7 +14,7 @@ _lib = None
 
 # status codes / enums (include/w4.h)
 W4_OK, W4_ERR_INVALID, W4_ERR_UNSUPPORTED, W4_ERR_CUDA, W4_ERR_TIMEOUT, W4_ERR_NCCL = range(6)
-W4_F16, W4_BF16, W4_F32, W4_E4M3, W4_S8 = range(5)
+W4_F16, W4_BF16, W4_F32, W4_E4M3, W4_S8, W4_E4M3_ATOMS = range(6)
 W4_NVFP4_KN, W4_NVFP4_NK = 0, 1
 W4_ACT_W4A16, W4_ACT_NVFP4 = 0, 1
 W4_TP_COLUMN, W4_TP_ROW = 0, 1
@@ -50,6 +50,8 @@ _SIGS = {
     "w4_nvfp4_workspace_bytes": (_Z, [_I, _I, _I, _I, _I]),
     "w4_nvfp4_gemm": (_I, [_P, _P, _I, _P, _I, _P, _I, _P, _P, _I, _P, _I, _I, _I, _P, _Z, _P]),
     "w4_nvfp4_repack_kn_to_nk": (_I, [_P, _I, _I, _P, _P]),
+    "w4_nvfp4_scale_atoms_bytes": (_Z, [_I, _I]),
+    "w4_nvfp4_repack_scales": (_I, [_P, _I, _I, _P, _P]),
     "w4_nvfp4_lut_gemm_s8a": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),
     "w4_rmsnorm_quant_s8": (_I, [_P, _P, _P, _I, _I, _F, _P]),
     "w4_rowscale_fp8": (_I, [_P, _I, _P, _P, _I, _I, _P]),

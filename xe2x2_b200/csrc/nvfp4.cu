@@ -54,13 +54,25 @@ int nvfp4_dequant(const uint8_t *w, int layout, const void *scale, int scale_dty
 }
 
 // ---- activation quantiser: one thread per 16-element block ----
+// sf = e4m3(amax / (6 g)), d = e4m3(sf) * g, code = e2m1(a * (1/d)) with one
+// correctly rounded reciprocal per block.  ATOMS: the scales go straight into
+// the 512-byte atom layout of the block-scaled GEMM (rows padded to 128 with
+// zero scales), else row-major [M, K/16].
+template <bool ATOMS>
 __global__ void nvfp4_quant_act_kernel(const uint16_t *__restrict__ a, int M, int K,
                                        const float *__restrict__ a_global,
-                                       uint8_t *__restrict__ codes, uint8_t *__restrict__ sf) {
-    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+                                       uint8_t *__restrict__ codes, uint8_t *__restrict__ sf, int rows) {
+    const long b = (long)blockIdx.x * blockDim.x + threadIdx.x;
     const int nb = K / 16;
-    if (b >= M * nb) return;
-    const int m = b / nb, kb = b % nb;
+    if (b >= (long)rows * nb) return;
+    const int m = (int)(b / nb), kb = (int)(b % nb);
+    size_t si = (size_t)m * nb + kb;
+    if constexpr (ATOMS)
+        si = ((size_t)(m >> 7) * (nb >> 2) + (kb >> 2)) * 512 + (m & 31) * 16 + ((m >> 5) & 3) * 4 + (kb & 3);
+    if (m >= M) {  // padding row of the last tile
+        sf[si] = 0;
+        return;
+    }
     const uint16_t *x = a + (size_t)m * K + (size_t)kb * 16;
     const uint4 u0 = ld_nc_v4(x), u1 = ld_nc_v4(x + 8);
     const uint32_t wv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
@@ -76,11 +88,12 @@ __global__ void nvfp4_quant_act_kernel(const uint16_t *__restrict__ a, int M, in
     const float g = *a_global;
     const uint32_t s = f_to_e4m3(__fdiv_rn(amax, __fmul_rn(6.0f, g)));
     const float sdec = __fmul_rn(e4m3_to_f(s), g);
-    sf[(size_t)m * nb + kb] = (uint8_t)s;
+    const float inv = sdec != 0.f ? __frcp_rn(sdec) : 0.f;
+    sf[si] = (uint8_t)s;
     uint32_t packed[2] = {0, 0};
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-        const uint32_t c = (sdec != 0.f) ? f_to_e2m1(__fdiv_rn(v[i], sdec)) : 0u;
+        const uint32_t c = (sdec != 0.f) ? f_to_e2m1(__fmul_rn(v[i], inv)) : 0u;
         packed[i >> 3] |= c << (4 * (i & 7));
     }
     *reinterpret_cast<uint2 *>(codes + (size_t)m * (K / 2) + (size_t)kb * 8) =
@@ -89,8 +102,18 @@ __global__ void nvfp4_quant_act_kernel(const uint16_t *__restrict__ a, int M, in
 
 int nvfp4_quant_act(const uint16_t *a, int M, int K, const float *a_global, uint8_t *codes,
                     uint8_t *sf, cudaStream_t st) {
-    const int nblk = M * (K / 16);
-    nvfp4_quant_act_kernel<<<(nblk + 255) / 256, 256, 0, st>>>(a, M, K, a_global, codes, sf);
+    const long nblk = (long)M * (K / 16);
+    nvfp4_quant_act_kernel<false><<<(unsigned)((nblk + 255) / 256), 256, 0, st>>>(a, M, K, a_global, codes, sf, M);
+    W4_LAUNCH_CHECK();
+    return W4_OK;
+}
+
+int nvfp4_quant_act_atoms(const uint16_t *a, int M, int K, const float *a_global, uint8_t *codes,
+                          uint8_t *sf_atoms, cudaStream_t st) {
+    const int rows = (M + 127) / 128 * 128;
+    const long nblk = (long)rows * (K / 16);
+    nvfp4_quant_act_kernel<true><<<(unsigned)((nblk + 255) / 256), 256, 0, st>>>(a, M, K, a_global, codes, sf_atoms,
+                                                                                  rows);
     W4_LAUNCH_CHECK();
     return W4_OK;
 }

@@ -1,0 +1,332 @@
+// nvfp4_prefill.cu -- NVFP4 x NVFP4 block-scaled GEMM on the 5th-generation
+// tensor cores (tcgen05.mma kind::mxf4nvf4, sm_100a).
+//
+// Contract: w4_nvfp4_gemm with act_mode W4_ACT_NVFP4.  The activations are
+// quantised per 16-block exactly as w4_nvfp4_quant_act does (sf_a = e4m3(amax /
+// (6 a_global)), code = e2m1(a / (sf_a a_global))), then
+//   C[m,n] = a_global * w_global * sum_k (e2m1_a * sf_a)[m,k] * (e2m1_w * sf_w)[n,k]
+// with the fp32 sum taken by the tensor core from the block-scaled operands
+// (the MMA applies one UE4M3 scale per 16 elements of each operand).  The
+// reference's NVFP4 GEMM is the external operator of
+// kernels/nvfp4/bench_nvfp4_m1.py:67,88 (oneDNN), W4A16 only; its LUT kernel
+// (kernels/nvfp4/nibble_lut_sc.cpp:198-290) quantises activations to s8.
+//
+// Operands:
+//   A codes  u8 [M, K/2]  (2 E2M1 per byte, low nibble = even k), TMA box
+//            128 rows x 128 bytes (256 k), 128-byte swizzle, K-major.
+//   W codes  u8 [N, K/2]  same.
+//   scales   UE4M3, rearranged once per call into 512-byte atoms of 128 rows x
+//            4 blocks (64 k): byte (r % 32) * 16 + (r / 32 % 4) * 4 + (kb % 4),
+//            atoms ordered [row tile][k / 64], so a stage's four atoms are one
+//            2 KB bulk copy.  tcgen05.cp (32x128b, replicated to the four lane
+//            quarters) moves an atom into 4 TMEM columns for the MMA.
+// Tile 128 x 128 per CTA, 256 k per pipeline stage (four K=64 MMAs).  Warp 0
+// produces (TMA + bulk copies), warp 1 allocates TMEM and issues the scale
+// copies and MMAs, warps 2-5 read the fp32 accumulator out of TMEM, apply the
+// tensor scales and store C.  Every wait is bounded; no copy uses multicast.
+#include <mutex>
+
+#include "tma_util.cuh"
+#include "w4_common.cuh"
+#include "w4_internal.h"
+
+namespace w4 {
+
+static __device__ unsigned int g_fp4pf_timeout;  // a bounded wait expired (sticky until read)
+
+static inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// ---- scale rearrangement: [rows][K/16] (row stride rs, block stride ks) -> atoms ----
+__global__ void nvfp4_sf_atoms_kernel(const uint8_t *__restrict__ src, int rows, int nkb, long rs, long ks,
+                                      int rows_pad, uint8_t *__restrict__ dst) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long total = (long)rows_pad * nkb;
+    if (i >= total) return;
+    // i enumerates destination bytes in order
+    const long atom = i >> 9;
+    const int within = (int)(i & 511);
+    const int kchunks = nkb / 4;
+    const int tile = (int)(atom / kchunks), kc = (int)(atom % kchunks);
+    const int r = tile * 128 + (within >> 4) + 32 * ((within >> 2) & 3);
+    const int kb = kc * 4 + (within & 3);
+    dst[i] = r < rows ? src[r * rs + (long)kb * ks] : (uint8_t)0;
+}
+
+int nvfp4_sf_atoms(const uint8_t *src, int rows, int nkb, long rs, long ks, uint8_t *dst, cudaStream_t st) {
+    const int rows_pad = (rows + 127) / 128 * 128;
+    const long total = (long)rows_pad * nkb;
+    nvfp4_sf_atoms_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, rows, nkb, rs, ks, rows_pad, dst);
+    W4_LAUNCH_CHECK();
+    return W4_OK;
+}
+
+namespace fp4pf {
+
+constexpr int BM = 128, BN = 128, BK = 256;  // BK in elements (128 bytes of codes)
+constexpr int S = 5;
+constexpr int kThreads = 6 * 32;
+constexpr uint32_t A_BYTES = BM * BK / 2, B_BYTES = BN * BK / 2, SF_BYTES = 2048;
+constexpr uint32_t A_OFF = 0, B_OFF = A_OFF + S * A_BYTES, SFA_OFF = B_OFF + S * B_BYTES,
+                   SFB_OFF = SFA_OFF + S * SF_BYTES, BAR_OFF = SFB_OFF + S * SF_BYTES,
+                   MISC_OFF = BAR_OFF + (2 * S + 1) * 8, SMEM = MISC_OFF + 16;
+// TMEM: accumulator columns [0, 128); stage s scale columns at 128 + 32 s (A: 16, B: 16).
+constexpr uint32_t TMEM_COLS = 512, SF_COL0 = 128;
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+// 512-byte scale atom (32 rows x 16 bytes) -> TMEM lanes 0-31, 4 columns, replicated to all four lane quarters.
+__device__ __forceinline__ void tc_cp_sf(uint32_t taddr, uint64_t sdesc) {
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+__device__ __forceinline__ void mma_fp4(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t sfa,
+                                        uint32_t sfb, uint32_t acc) {
+    asm volatile(
+        "{\n.reg .pred p;\nsetp.ne.b32 p, %6, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%4], [%5], p;\n}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(sfa), "r"(sfb), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// K-major operand tile, 128-byte swizzle, 8-row groups 1024 bytes apart, version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Scale atom: 32 rows of 16 bytes, no swizzle, 8-row core matrices 128 bytes apart.
+__device__ __forceinline__ uint64_t sf_desc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(128 >> 4) << 32) |
+           ((uint64_t)1 << 46);
+}
+// Instruction descriptor, block-scaled kind::mxf4nvf4: A/B E2M1 (1), K-major,
+// N>>3 at bit 17, scale format UE4M3 (bit 23 = 0), M>>4 at bit 24, scale ids 0.
+constexpr uint32_t kIdesc = (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ bool wait_pf(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+    const uint32_t b = smem_u32(bar);
+    if (mbar_try_wait(b, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    while (!mbar_try_wait(b, parity)) {
+        if (*abort_flag) return false;
+        if (global_ns() - t0 > kWaitLimitNs) {
+            *abort_flag = 1;
+            atomicExch(&g_fp4pf_timeout, 1u);
+            return false;
+        }
+    }
+    return true;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+nvfp4_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap w_map,
+                     const uint8_t *__restrict__ sfa, const uint8_t *__restrict__ sfb,
+                     const float *__restrict__ a_global, const float *__restrict__ w_global, void *__restrict__ C,
+                     int c_dtype, int M, int N, int K) {
+    extern __shared__ uint8_t smem_dyn[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + BAR_OFF);
+    uint64_t *empty = full + S;
+    uint64_t *done = empty + S;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + MISC_OFF);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + MISC_OFF + 4);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int mt = blockIdx.x, nt = blockIdx.y;
+    const int m0 = mt * BM, n0 = nt * BN;
+    const int nk = K / BK;
+    const int kchunks = K / 64;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint32_t tx = A_BYTES + B_BYTES + 2 * SF_BYTES;
+            for (int i = 0; i < nk; ++i) {
+                const int s = i % S;
+                if (i >= S && !wait_pf(&empty[s], (uint32_t)(((i / S) - 1) & 1), abort_flag)) break;
+                mbar_arrive_expect_tx(&full[s], tx);
+                tma_load_2d(sm + A_OFF + s * A_BYTES, &a_map, i * (BK / 2), m0, &full[s]);
+                tma_load_2d(sm + B_OFF + s * B_BYTES, &w_map, i * (BK / 2), n0, &full[s]);
+                bulk_load(sm + SFA_OFF + s * SF_BYTES, sfa + ((size_t)mt * kchunks + 4 * i) * 512, SF_BYTES, &full[s]);
+                bulk_load(sm + SFB_OFF + s * SF_BYTES, sfb + ((size_t)nt * kchunks + 4 * i) * 512, SF_BYTES, &full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            for (int i = 0; i < nk; ++i) {
+                const int s = i % S;
+                if (!wait_pf(&full[s], (uint32_t)((i / S) & 1), abort_flag)) break;
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(sm + A_OFF + s * A_BYTES);
+                const uint32_t b_addr = smem_u32(sm + B_OFF + s * B_BYTES);
+                const uint32_t sfa_addr = smem_u32(sm + SFA_OFF + s * SF_BYTES);
+                const uint32_t sfb_addr = smem_u32(sm + SFB_OFF + s * SF_BYTES);
+                const uint32_t col_a = tmem + SF_COL0 + 32 * s, col_b = col_a + 16;
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    tc_cp_sf(col_a + 4 * kk, sf_desc(sfa_addr + 512 * kk));
+                    tc_cp_sf(col_b + 4 * kk, sf_desc(sfb_addr + 512 * kk));
+                }
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_fp4(tmem, sw128_desc(a_addr + 32 * kk), sw128_desc(b_addr + 32 * kk), kIdesc, col_a + 4 * kk,
+                            col_b + 4 * kk, (i | kk) != 0);
+                tc_commit(&empty[s]);
+            }
+            tc_commit(done);
+        }
+    } else {
+        const bool ok = wait_pf(done, 0u, abort_flag);
+        (void)ok;
+        tc_fence_after();
+        const int q = warp & 3;
+        const int row = m0 + 32 * q + lane;
+        const float gs = (a_global ? *a_global : 1.0f) * (w_global ? *w_global : 1.0f);
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+            if (row < M) {
+                const size_t base = (size_t)row * N + n0 + c0;
+                if (c_dtype == W4_F32) {
+                    float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(C) + base);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        dst[e] = make_float4(__uint_as_float(v[4 * e]) * gs, __uint_as_float(v[4 * e + 1]) * gs,
+                                             __uint_as_float(v[4 * e + 2]) * gs, __uint_as_float(v[4 * e + 3]) * gs);
+                } else {
+                    uint32_t p[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        const float x0 = __uint_as_float(v[2 * e]) * gs, x1 = __uint_as_float(v[2 * e + 1]) * gs;
+                        if (c_dtype == W4_BF16) {
+                            __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+                            p[e] = *reinterpret_cast<uint32_t *>(&h);
+                        } else {
+                            __half2 h = __floats2half2_rn(x0, x1);
+                            p[e] = *reinterpret_cast<uint32_t *>(&h);
+                        }
+                    }
+                    uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(C) + base);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) dst[e] = make_uint4(p[4 * e], p[4 * e + 1], p[4 * e + 2], p[4 * e + 3]);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+}  // namespace fp4pf
+
+size_t nvfp4_prefill_workspace(int M, int N, int K) {
+    const size_t mp = (size_t)(M + 127) / 128 * 128, np = (size_t)(N + 127) / 128 * 128;
+    return align256(mp * K / 2) + align256(mp * (K / 16)) + align256(np * (K / 16));
+}
+
+// A bf16 [M,K] -> NVFP4 codes + scale atoms in the workspace, weight scales ->
+// atoms, then the block-scaled GEMM.  -1: shape not handled (caller falls back).
+int nvfp4_prefill(const uint16_t *a, const float *a_global, const uint8_t *w_nk, const uint8_t *w_sf,
+                  bool w_sf_atoms, const float *w_global, void *c, int c_dtype, int M, int N, int K,
+                  void *workspace, cudaStream_t st) {
+    using namespace fp4pf;
+    if (K % BK || N % BN || c_dtype == W4_E4M3) return -1;
+    char *ws = static_cast<char *>(workspace);
+    const size_t mp = (size_t)(M + 127) / 128 * 128;
+    uint8_t *codes = reinterpret_cast<uint8_t *>(ws);  // rows padded to the 128-row tile; the pad
+    ws += align256(mp * K / 2);                         // rows' scales are 0
+    uint8_t *sfa = reinterpret_cast<uint8_t *>(ws);
+    ws += align256(mp * (K / 16));
+    int rc = nvfp4_quant_act_atoms(a, M, K, a_global, codes, sfa, st);
+    if (rc) return rc;
+    const uint8_t *sfb = w_sf;
+    if (!w_sf_atoms) {
+        uint8_t *t = reinterpret_cast<uint8_t *>(ws);
+        rc = nvfp4_sf_atoms(w_sf, N, K / 16, 1, N, t, st);
+        if (rc) return rc;
+        sfb = t;
+    }
+    CUtensorMap a_map, w_map;
+    if (!make_map_2d(&a_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, codes, (uint64_t)K / 2, mp, (uint64_t)K / 2, BK / 2, BM,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map_2d(&w_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_nk, (uint64_t)K / 2, N, (uint64_t)K / 2, BK / 2, BN,
+                     CU_TENSOR_MAP_SWIZZLE_128B))
+        return -1;
+    const size_t smem = SMEM + 1024;
+    {
+        static std::mutex mu;
+        static bool set_dev[128] = {};
+        int dev = 0;
+        W4_CUDA_TRY(cudaGetDevice(&dev));
+        std::lock_guard<std::mutex> lk(mu);
+        if (dev < 128 && !set_dev[dev]) {
+            W4_CUDA_TRY(cudaFuncSetAttribute(nvfp4_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem));
+            set_dev[dev] = true;
+        }
+    }
+    dim3 grid((M + BM - 1) / BM, N / BN), block(kThreads);
+    nvfp4_prefill_kernel<<<grid, block, smem, st>>>(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K);
+    W4_LAUNCH_CHECK();
+    return W4_OK;
+}
+
+int take_fp4_prefill_wait_status() {
+    unsigned int v = 0;
+    W4_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_fp4pf_timeout, sizeof(v)));
+    if (v) {
+        const unsigned int zero = 0;
+        W4_CUDA_TRY(cudaMemcpyToSymbol(g_fp4pf_timeout, &zero, sizeof(zero)));
+        set_error("a device-side wait expired in the NVFP4 prefill GEMM");
+        return W4_ERR_TIMEOUT;
+    }
+    return W4_OK;
+}
+
+}  // namespace w4

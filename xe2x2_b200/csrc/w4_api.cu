@@ -69,7 +69,8 @@ int w4_check_device_status(void) {
     const int r1 = w4::take_wait_status();
     const int r2 = w4::take_prefill_wait_status();
     const int r3 = w4::take_fp4_wait_status();
-    return r1 ? r1 : r2 ? r2 : r3;
+    const int r4 = w4::take_fp4_prefill_wait_status();
+    return r1 ? r1 : r2 ? r2 : r3 ? r3 : r4;
 }
 
 // ------------------------------------------------------------------ GPTQ
@@ -173,9 +174,9 @@ static int check_nvfp4_w(const uint8_t *w, int layout, const void *scale, int sc
                          const float *global_scale, int K, int N) {
     W4_REQUIRE(w && scale, W4_ERR_INVALID, "w and scale are required");
     W4_REQUIRE(layout == W4_NVFP4_KN || layout == W4_NVFP4_NK, W4_ERR_INVALID, "bad layout %d", layout);
-    W4_REQUIRE(scale_dtype == W4_E4M3 || scale_dtype == W4_BF16, W4_ERR_INVALID,
-               "scale_dtype must be e4m3 or bf16");
-    W4_REQUIRE(scale_dtype != W4_E4M3 || global_scale, W4_ERR_INVALID,
+    W4_REQUIRE(scale_dtype == W4_E4M3 || scale_dtype == W4_BF16 || scale_dtype == W4_E4M3_ATOMS, W4_ERR_INVALID,
+               "scale_dtype must be e4m3, e4m3 atoms or bf16");
+    W4_REQUIRE(scale_dtype == W4_BF16 || global_scale, W4_ERR_INVALID,
                "e4m3 block scales need the fp32 tensor scale");
     W4_REQUIRE(scale_dtype != W4_BF16 || !global_scale, W4_ERR_INVALID,
                "bf16 (folded) block scales take no tensor scale");
@@ -188,6 +189,7 @@ int w4_nvfp4_dequant(const uint8_t *w, int layout, const void *scale, int scale_
     w4::set_error("");
     int rc = check_nvfp4_w(w, layout, scale, scale_dtype, global_scale, K, N);
     if (rc) return rc;
+    W4_REQUIRE(scale_dtype != W4_E4M3_ATOMS, W4_ERR_UNSUPPORTED, "dequant reads [K/16, N] block scales");
     W4_REQUIRE(out, W4_ERR_INVALID, "out is required");
     return w4::nvfp4_dequant(w, layout, scale, scale_dtype, global_scale, K, N, out, S(stream));
 }
@@ -204,7 +206,7 @@ int w4_nvfp4_quant_act(const uint16_t *a, int M, int K, const float *a_global, u
 size_t w4_nvfp4_workspace_bytes(int M, int N, int K, int act_mode, int c_dtype) {
     size_t ws = 0;
     if (M <= 0 || N <= 0 || K <= 0) return 0;
-    if (act_mode == W4_ACT_NVFP4) ws += align256((size_t)M * K / 2) + align256((size_t)M * K / 16);
+    if (act_mode == W4_ACT_NVFP4) ws += w4::nvfp4_prefill_workspace(M, N, K);
     if (c_dtype == W4_E4M3) ws += align256((size_t)M * N * 4);
     return ws;
 }
@@ -226,15 +228,38 @@ int w4_nvfp4_gemm(const void *a, const uint8_t *w, int layout, const void *scale
     W4_REQUIRE(layout == W4_NVFP4_NK, W4_ERR_UNSUPPORTED,
                "the GEMM reads the K-contiguous [N, K/2] layout; transpose [K/2, N] weights once "
                "with w4_nvfp4_repack_kn_to_nk");
-    W4_REQUIRE(act_mode == W4_ACT_W4A16, W4_ERR_UNSUPPORTED,
-               "NVFP4-activation GEMM is not built yet");
     W4_REQUIRE(K % 128 == 0 && N % 32 == 0, W4_ERR_UNSUPPORTED,
                "need K %% 128 == 0 and N %% 32 == 0 (K=%d N=%d)", K, N);
+    W4_REQUIRE(scale_dtype != W4_E4M3_ATOMS || act_mode == W4_ACT_NVFP4, W4_ERR_UNSUPPORTED,
+               "rearranged scale atoms are read by the NVFP4-activation GEMM only");
     W4_REQUIRE(aligned(a, 16) && aligned(w, 16), W4_ERR_INVALID, "a and w must be 16-byte aligned");
     const size_t need = w4_nvfp4_workspace_bytes(M, N, K, act_mode, c_dtype);
     W4_REQUIRE(workspace_bytes >= need && (need == 0 || workspace), W4_ERR_INVALID,
                "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
     cudaStream_t st = S(stream);
+    if (act_mode == W4_ACT_NVFP4) {
+        // block-scaled tensor-core GEMM on NVFP4 activations (nvfp4_prefill.cu)
+        W4_REQUIRE(scale_dtype == W4_E4M3 || scale_dtype == W4_E4M3_ATOMS, W4_ERR_UNSUPPORTED,
+                   "NVFP4 activations need E4M3 weight block scales (the MMA scales are UE4M3)");
+        W4_REQUIRE(K % 256 == 0 && N % 128 == 0, W4_ERR_UNSUPPORTED,
+                   "NVFP4 activations need K %% 256 == 0 and N %% 128 == 0 (K=%d N=%d)", K, N);
+        char *wsb = static_cast<char *>(workspace);
+        void *out = c;
+        int odt = c_dtype;
+        if (c_dtype == W4_E4M3) {
+            out = wsb;
+            odt = W4_F32;
+            wsb += align256((size_t)M * N * 4);
+        }
+        rc = w4::nvfp4_prefill(static_cast<const uint16_t *>(a), a_global, w, static_cast<const uint8_t *>(scale),
+                               scale_dtype == W4_E4M3_ATOMS, global_scale, out, odt, M, N, K, wsb, st);
+        if (rc < 0) {
+            w4::set_error("NVFP4-activation GEMM: tensor maps could not be encoded for this shape");
+            return W4_ERR_UNSUPPORTED;
+        }
+        if (rc || c_dtype != W4_E4M3) return rc;
+        return w4::rowscale_fp8(out, W4_F32, static_cast<uint8_t *>(c), row_scale, M, N, st);
+    }
     if (c_dtype == W4_E4M3) {
         float *y = static_cast<float *>(workspace);
         rc = w4::nvfp4_gemv(static_cast<const uint16_t *>(a), w, layout, scale, scale_dtype,
@@ -251,6 +276,19 @@ int w4_nvfp4_repack_kn_to_nk(const uint8_t *w_kn, int K, int N, uint8_t *w_nk, v
     W4_REQUIRE(w_kn && w_nk && w_kn != w_nk, W4_ERR_INVALID, "distinct w_kn and w_nk are required");
     W4_REQUIRE(K > 0 && N > 0 && K % 2 == 0, W4_ERR_INVALID, "K=%d N=%d", K, N);
     return w4::nvfp4_kn_to_nk(w_kn, K, N, w_nk, S(stream));
+}
+
+size_t w4_nvfp4_scale_atoms_bytes(int N, int K) {
+    if (N <= 0 || K <= 0 || K % 64) return 0;
+    return (size_t)(N + 127) / 128 * 128 * (size_t)(K / 16);
+}
+
+int w4_nvfp4_repack_scales(const uint8_t *scale, int K, int N, uint8_t *atoms, void *stream) {
+    w4::set_error("");
+    W4_REQUIRE(scale && atoms && (const void *)scale != (const void *)atoms, W4_ERR_INVALID,
+               "distinct scale and atoms buffers are required");
+    W4_REQUIRE(K > 0 && N > 0 && K % 64 == 0, W4_ERR_INVALID, "K=%d must be a positive multiple of 64", K);
+    return w4::nvfp4_sf_atoms(scale, N, K / 16, 1, N, atoms, S(stream));
 }
 
 int w4_nvfp4_lut_gemm_s8a(const int8_t *a, const uint8_t *packed, const float *a_s,

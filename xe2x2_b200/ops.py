@@ -24,6 +24,7 @@ from __future__ import annotations
 
 import ctypes
 import threading
+import weakref
 
 import torch
 
@@ -195,6 +196,40 @@ def nvfp4_quant_act(a, a_global):
     return codes, sf
 
 
+# id(scale tensor) -> (weak reference, tensor version, rearranged atoms); an entry
+# goes away with its tensor (tensors compare elementwise, so they cannot be
+# dictionary keys themselves).
+_SCALE_ATOMS = {}
+
+
+def nvfp4_repack_scales(scale):
+    """E4M3 block scales [K/16, N] -> the atom layout of the block-scaled GEMM (u8, flat)."""
+    _need_cuda(scale)
+    _contig(scale, "scale")
+    K, N = scale.shape[0] * 16, scale.shape[1]
+    nbytes = L.lib().w4_nvfp4_scale_atoms_bytes(N, K)
+    atoms = torch.empty(nbytes, dtype=torch.uint8, device=scale.device)
+    L.call("w4_nvfp4_repack_scales", _p(scale), K, N, _p(atoms), _stream(scale.device))
+    return atoms
+
+
+def _scale_atoms(scale):
+    """Rearranged scales for this tensor, made once and reused while the tensor is unchanged."""
+    hit = _SCALE_ATOMS.get(id(scale))
+    if hit is not None and hit[0]() is scale and hit[1] == scale._version:
+        return hit[2]
+    atoms = nvfp4_repack_scales(scale)
+    key = id(scale)
+    _SCALE_ATOMS[key] = (weakref.ref(scale), scale._version, atoms)
+    weakref.finalize(scale, _SCALE_ATOMS.pop, key, None)
+    return atoms
+
+
+def scale_atoms_cached(scale) -> bool:
+    hit = _SCALE_ATOMS.get(id(scale))
+    return hit is not None and hit[0]() is scale and hit[1] == scale._version
+
+
 def nvfp4_gemm(x, w, scale, global_scale=None, out_dtype=torch.bfloat16, act_mode=L.W4_ACT_W4A16,
                a_global=None):
     _need_cuda(x, w, scale, global_scale, a_global)
@@ -205,6 +240,8 @@ def nvfp4_gemm(x, w, scale, global_scale=None, out_dtype=torch.bfloat16, act_mod
         w = nvfp4_repack_kn_to_nk(w)
         layout = L.W4_NVFP4_NK
     sdt = L.W4_E4M3 if scale.dtype in (torch.float8_e4m3fn, torch.uint8) else L.W4_BF16
+    if act_mode == L.W4_ACT_NVFP4 and sdt == L.W4_E4M3 and K % 64 == 0:
+        scale, sdt = _scale_atoms(scale), L.W4_E4M3_ATOMS
     c = torch.empty((M, N), dtype=out_dtype, device=x.device)
     rs = torch.empty(M, dtype=torch.float32, device=x.device) if out_dtype == torch.float8_e4m3fn else None
     need = L.lib().w4_nvfp4_workspace_bytes(M, N, K, act_mode, _DT[out_dtype])

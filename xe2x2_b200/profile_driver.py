@@ -17,6 +17,7 @@ import statistics
 
 import torch
 
+from . import _lib as L
 from . import ops, synth
 
 
@@ -81,6 +82,8 @@ def main(argv=None):
     ap.add_argument("--dtype", choices=["bf16", "f16"], default="bf16")
     ap.add_argument("--iters", type=int, default=4)
     ap.add_argument("--time", action="store_true")
+    ap.add_argument("--act", choices=["w4a16", "nvfp4"], default="w4a16",
+                    help="NVFP4 kernel: bf16 activations (w4a16) or activations quantised to NVFP4")
     args = ap.parse_args(argv)
     dev = torch.device("cuda:0")
     dt = torch.bfloat16 if args.dtype == "bf16" else torch.float16
@@ -95,12 +98,14 @@ def main(argv=None):
     results = []
     for M in [int(m) for m in args.M.split(",")]:
         a = synth.activations(M, K, dt, seed=M, device=dev)
+        ag = torch.tensor([float(a.float().abs().max()) / (448.0 * 6.0)], dtype=torch.float32, device=dev)
+        act_mode = L.W4_ACT_NVFP4 if args.act == "nvfp4" else L.W4_ACT_W4A16
 
         def run(i):
             w = ws[i % copies]
             if args.kernel == "gptq":
                 return ops.gptq_gemm(a, w[0], w[1], w[2], args.gs, 1)
-            return ops.nvfp4_gemm(a, w[0], w[1], w[2])
+            return ops.nvfp4_gemm(a, w[0], w[1], w[2], act_mode=act_mode, a_global=ag)
 
         if not args.time:
             for i in range(args.iters):
