@@ -74,6 +74,23 @@ def test_quant_act_bit_exact(cuda):
     assert np.array_equal(np_(sf), rs)
 
 
+def test_quant_act_rounding_ties_bit_exact(cuda):
+    """Values that land exactly on E2M1 midpoints (ties to even), negative values
+    that round to zero, and saturation: with a_global = 1 and a block maximum of 6
+    the block scale decodes to 1, so every element is quantised as is."""
+    K = 64
+    row = [6.0, 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, -0.25, -0.75, -1.25, -1.75, -2.5, -3.5, -5.0, -0.1,
+           6.0, 0.2, 0.3, 0.74, 0.76, 1.24, 1.26, 2.49, 2.51, 3.49, 3.51, 4.99, 5.01, -0.0, 0.0, -6.0,
+           6.0, 7.0, -7.0, 1e-3, -1e-3, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, -0.5, -1.0, -1.5, -2.0, -3.0,
+           6.0, -4.0, 0.125, 0.375, 0.625, 0.875, 1.125, 1.375, 2.25, 2.75, 3.25, 3.75, 4.5, 5.5, 5.75, 0.0]
+    x = torch.tensor([row, [v * 0.5 for v in row]], dtype=torch.float32).to(torch.bfloat16).to(cuda)
+    a_global = torch.ones(1, dtype=torch.float32, device=cuda)
+    codes, sf = ops.nvfp4_quant_act(x, a_global)
+    rc, rs = O.nvfp4_quant_act(f32(x), 1.0)
+    assert np.array_equal(np_(sf), rs)
+    assert np.array_equal(np_(codes), rc)
+
+
 @pytest.mark.parametrize("M", [1, 2, 5, 8, 16, 17, 32, 40])
 def test_gemm_w4a16_small(cuda, M):
     K, N = 1024, 256

@@ -7,6 +7,7 @@
 // stride(0)==1, kernels/nvfp4/bench_nvfp4_m1.py:58-61).  Block scales are
 // [K/16, N] in both.
 #include <cooperative_groups.h>
+#include <cuda_fp4.h>
 
 #include "nvfp4_util.cuh"
 #include "w4_common.cuh"
@@ -90,11 +91,16 @@ __global__ void nvfp4_quant_act_kernel(const uint16_t *__restrict__ a, int M, in
     const float sdec = __fmul_rn(e4m3_to_f(s), g);
     const float inv = sdec != 0.f ? __frcp_rn(sdec) : 0.f;
     sf[si] = (uint8_t)s;
+    // hardware E2M1 conversion: round to nearest even, saturating at +-6 (the
+    // rounding rule of f_to_e2m1 / the host quantiser)
     uint32_t packed[2] = {0, 0};
+    if (sdec != 0.f) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        const uint32_t c = (sdec != 0.f) ? f_to_e2m1(__fmul_rn(v[i], inv)) : 0u;
-        packed[i >> 3] |= c << (4 * (i & 7));
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t c2 = __nv_cvt_float2_to_fp4x2(make_float2(__fmul_rn(v[2 * i], inv), __fmul_rn(v[2 * i + 1], inv)),
+                                                         __NV_E2M1, cudaRoundNearest);
+            packed[i >> 2] |= (c2 & 0xFFu) << (8 * (i & 3));
+        }
     }
     *reinterpret_cast<uint2 *>(codes + (size_t)m * (K / 2) + (size_t)kb * 8) =
         make_uint2(packed[0], packed[1]);
