@@ -62,15 +62,26 @@ int nvfp4_sf_atoms(const uint8_t *src, int rows, int nkb, long rs, long ks, uint
 
 namespace fp4pf {
 
-constexpr int BM = 128, BN = 128, BK = 256;  // BK in elements (128 bytes of codes)
-constexpr int S = 5;
+constexpr int BM = 128, BK = 256;  // BK in elements (128 bytes of codes)
 constexpr int kThreads = 6 * 32;
-constexpr uint32_t A_BYTES = BM * BK / 2, B_BYTES = BN * BK / 2, SF_BYTES = 2048;
-constexpr uint32_t A_OFF = 0, B_OFF = A_OFF + S * A_BYTES, SFA_OFF = B_OFF + S * B_BYTES,
-                   SFB_OFF = SFA_OFF + S * SF_BYTES, BAR_OFF = SFB_OFF + S * SF_BYTES,
-                   MISC_OFF = BAR_OFF + (2 * S + 1) * 8, SMEM = MISC_OFF + 16;
-// TMEM: accumulator columns [0, 128); stage s scale columns at 128 + 32 s (A: 16, B: 16).
-constexpr uint32_t TMEM_COLS = 512, SF_COL0 = 128;
+constexpr uint32_t SF_ATOM = 512;
+
+// Shared memory and TMEM plan for a 128 x BN tile.
+template <int BN> struct Cfg {
+    static constexpr int S = BN == 256 ? 4 : 5;                  // pipeline stages
+    static constexpr int NH = BN / 128;                          // 128-row halves of the W tile
+    static constexpr uint32_t A_BYTES = BM * BK / 2, B_BYTES = BN * BK / 2;
+    static constexpr uint32_t SFA_BYTES = 4 * SF_ATOM, SFB_BYTES = NH * 4 * SF_ATOM;
+    static constexpr uint32_t A_OFF = 0, B_OFF = A_OFF + S * A_BYTES, SFA_OFF = B_OFF + S * B_BYTES,
+                              SFB_OFF = SFA_OFF + S * SFA_BYTES, BAR_OFF = SFB_OFF + S * SFB_BYTES,
+                              MISC_OFF = BAR_OFF + (2 * S + 1) * 8, SMEM = MISC_OFF + 16;
+    // TMEM: accumulator columns [0, BN); stage s scales at BN + s * SF_COLS (A: 16, then B: 16 NH).
+    static constexpr uint32_t SF_COLS = 16 + 16 * NH, TMEM_COLS = 512;
+    static_assert(BN + S * SF_COLS <= TMEM_COLS, "TMEM plan");
+    // Instruction descriptor, block-scaled kind::mxf4nvf4: A/B E2M1 (1), K-major,
+    // N>>3 at bit 17, scale format UE4M3 (bit 23 = 0), M>>4 at bit 24, scale ids 0.
+    static constexpr uint32_t IDESC = (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+};
 
 __device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
@@ -127,9 +138,6 @@ __device__ __forceinline__ uint64_t sf_desc(uint32_t saddr) {
     return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(128 >> 4) << 32) |
            ((uint64_t)1 << 46);
 }
-// Instruction descriptor, block-scaled kind::mxf4nvf4: A/B E2M1 (1), K-major,
-// N>>3 at bit 17, scale format UE4M3 (bit 23 = 0), M>>4 at bit 24, scale ids 0.
-constexpr uint32_t kIdesc = (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 
 __device__ __forceinline__ bool wait_pf(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
     const uint32_t b = smem_u32(bar);
@@ -146,11 +154,17 @@ __device__ __forceinline__ bool wait_pf(uint64_t *bar, uint32_t parity, volatile
     return true;
 }
 
+template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
 nvfp4_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap w_map,
                      const uint8_t *__restrict__ sfa, const uint8_t *__restrict__ sfb,
                      const float *__restrict__ a_global, const float *__restrict__ w_global, void *__restrict__ C,
                      int c_dtype, int M, int N, int K) {
+    using C_ = Cfg<BN>;
+    constexpr int S = C_::S;
+    constexpr uint32_t A_BYTES = C_::A_BYTES, B_BYTES = C_::B_BYTES, A_OFF = C_::A_OFF, B_OFF = C_::B_OFF,
+                       SFA_OFF = C_::SFA_OFF, SFB_OFF = C_::SFB_OFF, SFA_BYTES = C_::SFA_BYTES,
+                       SFB_BYTES = C_::SFB_BYTES, BAR_OFF = C_::BAR_OFF, MISC_OFF = C_::MISC_OFF;
     extern __shared__ uint8_t smem_dyn[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(sm + BAR_OFF);
@@ -173,7 +187,7 @@ nvfp4_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_con
         *abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+    if (warp == 1) tmem_alloc(tmem_slot, C_::TMEM_COLS);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -181,15 +195,19 @@ nvfp4_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_con
 
     if (warp == 0) {
         if (lane == 0) {
-            const uint32_t tx = A_BYTES + B_BYTES + 2 * SF_BYTES;
+            const uint32_t tx = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
             for (int i = 0; i < nk; ++i) {
                 const int s = i % S;
                 if (i >= S && !wait_pf(&empty[s], (uint32_t)(((i / S) - 1) & 1), abort_flag)) break;
                 mbar_arrive_expect_tx(&full[s], tx);
                 tma_load_2d(sm + A_OFF + s * A_BYTES, &a_map, i * (BK / 2), m0, &full[s]);
                 tma_load_2d(sm + B_OFF + s * B_BYTES, &w_map, i * (BK / 2), n0, &full[s]);
-                bulk_load(sm + SFA_OFF + s * SF_BYTES, sfa + ((size_t)mt * kchunks + 4 * i) * 512, SF_BYTES, &full[s]);
-                bulk_load(sm + SFB_OFF + s * SF_BYTES, sfb + ((size_t)nt * kchunks + 4 * i) * 512, SF_BYTES, &full[s]);
+                bulk_load(sm + SFA_OFF + s * SFA_BYTES, sfa + ((size_t)mt * kchunks + 4 * i) * SF_ATOM, SFA_BYTES,
+                          &full[s]);
+#pragma unroll
+                for (int h = 0; h < C_::NH; ++h)  // the 128-row halves' atoms sit in separate row tiles
+                    bulk_load(sm + SFB_OFF + s * SFB_BYTES + h * 4 * SF_ATOM,
+                              sfb + ((size_t)(nt * C_::NH + h) * kchunks + 4 * i) * SF_ATOM, 4 * SF_ATOM, &full[s]);
             }
         }
     } else if (warp == 1) {
@@ -200,18 +218,21 @@ nvfp4_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_con
                 tc_fence_after();
                 const uint32_t a_addr = smem_u32(sm + A_OFF + s * A_BYTES);
                 const uint32_t b_addr = smem_u32(sm + B_OFF + s * B_BYTES);
-                const uint32_t sfa_addr = smem_u32(sm + SFA_OFF + s * SF_BYTES);
-                const uint32_t sfb_addr = smem_u32(sm + SFB_OFF + s * SF_BYTES);
-                const uint32_t col_a = tmem + SF_COL0 + 32 * s, col_b = col_a + 16;
+                const uint32_t sfa_addr = smem_u32(sm + SFA_OFF + s * SFA_BYTES);
+                const uint32_t sfb_addr = smem_u32(sm + SFB_OFF + s * SFB_BYTES);
+                const uint32_t col_a = tmem + BN + C_::SF_COLS * s, col_b = col_a + 16;
+                // per K=64 step kk: A scales in 4 columns, W scales in 4 columns per 128-row half
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    tc_cp_sf(col_a + 4 * kk, sf_desc(sfa_addr + 512 * kk));
-                    tc_cp_sf(col_b + 4 * kk, sf_desc(sfb_addr + 512 * kk));
+                    tc_cp_sf(col_a + 4 * kk, sf_desc(sfa_addr + SF_ATOM * kk));
+#pragma unroll
+                    for (int h = 0; h < C_::NH; ++h)
+                        tc_cp_sf(col_b + 4 * C_::NH * kk + 4 * h, sf_desc(sfb_addr + h * 4 * SF_ATOM + SF_ATOM * kk));
                 }
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    mma_fp4(tmem, sw128_desc(a_addr + 32 * kk), sw128_desc(b_addr + 32 * kk), kIdesc, col_a + 4 * kk,
-                            col_b + 4 * kk, (i | kk) != 0);
+                    mma_fp4(tmem, sw128_desc(a_addr + 32 * kk), sw128_desc(b_addr + 32 * kk), C_::IDESC, col_a + 4 * kk,
+                            col_b + 4 * C_::NH * kk, (i | kk) != 0);
                 tc_commit(&empty[s]);
             }
             tc_commit(done);
@@ -259,10 +280,35 @@ nvfp4_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_con
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, TMEM_COLS);
+        tmem_dealloc(tmem, C_::TMEM_COLS);
     }
 }
 
+}  // namespace fp4pf
+
+namespace fp4pf {
+template <int BN>
+static int launch(const CUtensorMap &a_map, const CUtensorMap &w_map, const uint8_t *sfa, const uint8_t *sfb,
+                  const float *a_global, const float *w_global, void *c, int c_dtype, int M, int N, int K,
+                  cudaStream_t st) {
+    const size_t smem = Cfg<BN>::SMEM + 1024;
+    auto kern = nvfp4_prefill_kernel<BN>;
+    {
+        static std::mutex mu;
+        static bool set_dev[128] = {};
+        int dev = 0;
+        W4_CUDA_TRY(cudaGetDevice(&dev));
+        std::lock_guard<std::mutex> lk(mu);
+        if (dev < 128 && !set_dev[dev]) {
+            W4_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            set_dev[dev] = true;
+        }
+    }
+    dim3 grid((M + BM - 1) / BM, N / BN), block(kThreads);
+    kern<<<grid, block, smem, st>>>(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K);
+    W4_LAUNCH_CHECK();
+    return W4_OK;
+}
 }  // namespace fp4pf
 
 size_t nvfp4_prefill_workspace(int M, int N, int K) {
@@ -276,7 +322,7 @@ int nvfp4_prefill(const uint16_t *a, const float *a_global, const uint8_t *w_nk,
                   bool w_sf_atoms, const float *w_global, void *c, int c_dtype, int M, int N, int K,
                   void *workspace, cudaStream_t st) {
     using namespace fp4pf;
-    if (K % BK || N % BN || c_dtype == W4_E4M3) return -1;
+    if (K % BK || N % 128 || c_dtype == W4_E4M3) return -1;
     char *ws = static_cast<char *>(workspace);
     const size_t mp = (size_t)(M + 127) / 128 * 128;
     uint8_t *codes = reinterpret_cast<uint8_t *>(ws);  // rows padded to the 128-row tile; the pad
@@ -293,28 +339,20 @@ int nvfp4_prefill(const uint16_t *a, const float *a_global, const uint8_t *w_nk,
         sfb = t;
     }
     CUtensorMap a_map, w_map;
+    // 256-wide tiles unless 128-wide ones need fewer waves
+    bool wide = N % 256 == 0;
+    if (wide) {
+        const long nsm = num_sms(), t256 = (long)((M + BM - 1) / BM) * (N / 256);
+        if ((2 * t256 + nsm - 1) / nsm < 2 * ((t256 + nsm - 1) / nsm)) wide = false;
+    }
+    const int bn = wide ? 256 : 128;
     if (!make_map_2d(&a_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, codes, (uint64_t)K / 2, mp, (uint64_t)K / 2, BK / 2, BM,
                      CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map_2d(&w_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_nk, (uint64_t)K / 2, N, (uint64_t)K / 2, BK / 2, BN,
+        !make_map_2d(&w_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_nk, (uint64_t)K / 2, N, (uint64_t)K / 2, BK / 2, bn,
                      CU_TENSOR_MAP_SWIZZLE_128B))
         return -1;
-    const size_t smem = SMEM + 1024;
-    {
-        static std::mutex mu;
-        static bool set_dev[128] = {};
-        int dev = 0;
-        W4_CUDA_TRY(cudaGetDevice(&dev));
-        std::lock_guard<std::mutex> lk(mu);
-        if (dev < 128 && !set_dev[dev]) {
-            W4_CUDA_TRY(cudaFuncSetAttribute(nvfp4_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem));
-            set_dev[dev] = true;
-        }
-    }
-    dim3 grid((M + BM - 1) / BM, N / BN), block(kThreads);
-    nvfp4_prefill_kernel<<<grid, block, smem, st>>>(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K);
-    W4_LAUNCH_CHECK();
-    return W4_OK;
+    return wide ? launch<256>(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K, st)
+                : launch<128>(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K, st);
 }
 
 int take_fp4_prefill_wait_status() {
