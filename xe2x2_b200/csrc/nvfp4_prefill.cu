@@ -94,6 +94,9 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 __device__ __forceinline__ void tc_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
@@ -212,26 +215,29 @@ nvfp4_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_con
         }
     } else if (warp == 1) {
         if (lane == 0) {
+            // Descriptors of stage 0; a stage / K step only moves the start-address
+            // field (address >> 4 in the low 14 bits, never carrying out of it).
+            const uint64_t a_d0 = sw128_desc(smem_u32(sm + A_OFF)), b_d0 = sw128_desc(smem_u32(sm + B_OFF));
+            const uint64_t sfa_d0 = sf_desc(smem_u32(sm + SFA_OFF)), sfb_d0 = sf_desc(smem_u32(sm + SFB_OFF));
             for (int i = 0; i < nk; ++i) {
                 const int s = i % S;
                 if (!wait_pf(&full[s], (uint32_t)((i / S) & 1), abort_flag)) break;
                 tc_fence_after();
-                const uint32_t a_addr = smem_u32(sm + A_OFF + s * A_BYTES);
-                const uint32_t b_addr = smem_u32(sm + B_OFF + s * B_BYTES);
-                const uint32_t sfa_addr = smem_u32(sm + SFA_OFF + s * SFA_BYTES);
-                const uint32_t sfb_addr = smem_u32(sm + SFB_OFF + s * SFB_BYTES);
+                const uint64_t a_d = a_d0 + (uint64_t)(s * (A_BYTES >> 4)), b_d = b_d0 + (uint64_t)(s * (B_BYTES >> 4));
+                const uint64_t sfa_d = sfa_d0 + (uint64_t)(s * (SFA_BYTES >> 4));
+                const uint64_t sfb_d = sfb_d0 + (uint64_t)(s * (SFB_BYTES >> 4));
                 const uint32_t col_a = tmem + BN + C_::SF_COLS * s, col_b = col_a + 16;
                 // per K=64 step kk: A scales in 4 columns, W scales in 4 columns per 128-row half
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    tc_cp_sf(col_a + 4 * kk, sf_desc(sfa_addr + SF_ATOM * kk));
+                    tc_cp_sf(col_a + 4 * kk, sfa_d + (uint64_t)(kk * (SF_ATOM >> 4)));
 #pragma unroll
                     for (int h = 0; h < C_::NH; ++h)
-                        tc_cp_sf(col_b + 4 * C_::NH * kk + 4 * h, sf_desc(sfb_addr + h * 4 * SF_ATOM + SF_ATOM * kk));
+                        tc_cp_sf(col_b + 4 * C_::NH * kk + 4 * h, sfb_d + (uint64_t)((h * 4 + kk) * (SF_ATOM >> 4)));
                 }
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    mma_fp4(tmem, sw128_desc(a_addr + 32 * kk), sw128_desc(b_addr + 32 * kk), C_::IDESC, col_a + 4 * kk,
+                    mma_fp4(tmem, a_d + (uint64_t)(2 * kk), b_d + (uint64_t)(2 * kk), C_::IDESC, col_a + 4 * kk,
                             col_b + 4 * C_::NH * kk, (i | kk) != 0);
                 tc_commit(&empty[s]);
             }
@@ -284,6 +290,182 @@ nvfp4_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_con
     }
 }
 
+// Persistent variant: 128 x 256 tiles in a static tile loop (tile t = blockIdx.x +
+// j * gridDim.x, M fastest so a wave shares W tiles in L2), the stage ring running
+// on across tiles.  One accumulator (256 TMEM columns): eight epilogue warps (two
+// per TMEM lane quarter, 128 columns each) pull the whole tile into registers,
+// release the accumulator to the MMA issuer at once, and only then scale and store,
+// so the next tile's MMAs overlap the stores and the producer never drains.
+namespace pcfg {
+constexpr int BN = 256, S = 4, NH = 2, kEpiWarps = 8, kThreadsP = (2 + kEpiWarps) * 32;
+constexpr uint32_t A_BYTES = BM * BK / 2, B_BYTES = BN * BK / 2, SFA_BYTES = 4 * SF_ATOM, SFB_BYTES = NH * 4 * SF_ATOM;
+constexpr uint32_t A_OFF = 0, B_OFF = A_OFF + S * A_BYTES, SFA_OFF = B_OFF + S * B_BYTES,
+                   SFB_OFF = SFA_OFF + S * SFA_BYTES, BAR_OFF = SFB_OFF + S * SFB_BYTES,
+                   MISC_OFF = BAR_OFF + (2 * S + 2) * 8, SMEM = MISC_OFF + 16;
+// TMEM: accumulator [0, 256); stage s scales at 256 + 48 s (A 16, W 32).
+constexpr uint32_t SF_COL0 = BN, SF_COLS = 16 + 16 * NH, TMEM_COLS = 512;
+static_assert(SF_COL0 + S * SF_COLS <= TMEM_COLS, "TMEM plan");
+constexpr uint32_t IDESC = (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}  // namespace pcfg
+
+__global__ void __launch_bounds__(pcfg::kThreadsP, 1)
+nvfp4_prefill_persistent_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap w_map,
+                                const uint8_t *__restrict__ sfa, const uint8_t *__restrict__ sfb,
+                                const float *__restrict__ a_global, const float *__restrict__ w_global,
+                                void *__restrict__ C, int c_dtype, int M, int N, int K) {
+    using namespace pcfg;
+    extern __shared__ uint8_t smem_dyn[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + BAR_OFF);
+    uint64_t *empty = full + S;
+    uint64_t *acc_full = empty + S;
+    uint64_t *acc_empty = acc_full + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + MISC_OFF);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + MISC_OFF + 4);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int mtiles = (M + BM - 1) / BM;
+    const int ntiles = mtiles * (N / BN);
+    const int nk = K / BK;
+    const int kchunks = K / 64;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, kEpiWarps);  // one arrival per epilogue warp
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- producer: every k-block of every tile of this CTA ----------------
+        if (lane == 0) {
+            const uint32_t tx = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+            long g = 0;  // k-blocks issued so far (stage = g % S)
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const int mt = t % mtiles, nt = t / mtiles;
+                for (int i = 0; i < nk; ++i, ++g) {
+                    const int s = (int)(g % S);
+                    if (g >= S && !wait_pf(&empty[s], (uint32_t)(((g / S) - 1) & 1), abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], tx);
+                    tma_load_2d(sm + A_OFF + s * A_BYTES, &a_map, i * (BK / 2), mt * BM, &full[s]);
+                    tma_load_2d(sm + B_OFF + s * B_BYTES, &w_map, i * (BK / 2), nt * BN, &full[s]);
+                    bulk_load(sm + SFA_OFF + s * SFA_BYTES, sfa + ((size_t)mt * kchunks + 4 * i) * SF_ATOM, SFA_BYTES,
+                              &full[s]);
+#pragma unroll
+                    for (int h = 0; h < NH; ++h)
+                        bulk_load(sm + SFB_OFF + s * SFB_BYTES + h * 4 * SF_ATOM,
+                                  sfb + ((size_t)(nt * NH + h) * kchunks + 4 * i) * SF_ATOM, 4 * SF_ATOM, &full[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint64_t a_d0 = sw128_desc(smem_u32(sm + A_OFF)), b_d0 = sw128_desc(smem_u32(sm + B_OFF));
+            const uint64_t sfa_d0 = sf_desc(smem_u32(sm + SFA_OFF)), sfb_d0 = sf_desc(smem_u32(sm + SFB_OFF));
+            long g = 0;
+            int j = 0;  // local tile index
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++j) {
+                if (j >= 1 && !wait_pf(acc_empty, (uint32_t)((j - 1) & 1), abort_flag)) break;
+                tc_fence_after();
+                for (int i = 0; i < nk; ++i, ++g) {
+                    const int s = (int)(g % S);
+                    if (!wait_pf(&full[s], (uint32_t)((g / S) & 1), abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t a_d = a_d0 + (uint64_t)(s * (A_BYTES >> 4)), b_d = b_d0 + (uint64_t)(s * (B_BYTES >> 4));
+                    const uint64_t sfa_d = sfa_d0 + (uint64_t)(s * (SFA_BYTES >> 4));
+                    const uint64_t sfb_d = sfb_d0 + (uint64_t)(s * (SFB_BYTES >> 4));
+                    const uint32_t col_a = tmem + SF_COL0 + SF_COLS * s, col_b = col_a + 16;
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        tc_cp_sf(col_a + 4 * kk, sfa_d + (uint64_t)(kk * (SF_ATOM >> 4)));
+#pragma unroll
+                        for (int h = 0; h < NH; ++h)
+                            tc_cp_sf(col_b + 4 * NH * kk + 4 * h, sfb_d + (uint64_t)((h * 4 + kk) * (SF_ATOM >> 4)));
+                    }
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_fp4(tmem, a_d + (uint64_t)(2 * kk), b_d + (uint64_t)(2 * kk), IDESC, col_a + 4 * kk,
+                                col_b + 4 * NH * kk, (i | kk) != 0);
+                    tc_commit(&empty[s]);
+                }
+                if (!ok) break;
+                tc_commit(acc_full);
+            }
+        }
+    } else {
+        // ---------------- epilogue warps 2-9: lane quarter warp % 4, column half (warp - 2) / 4 ----------------
+        const int q = warp & 3, ch = (warp - 2) >> 2;
+        const float gs = (a_global ? *a_global : 1.0f) * (w_global ? *w_global : 1.0f);
+        int j = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++j) {
+            if (!__all_sync(0xffffffffu, wait_pf(acc_full, (uint32_t)(j & 1), abort_flag))) break;
+            tc_fence_after();
+            uint32_t v[4][32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(128 * ch + 32 * c), v[c]);
+            tc_fence_before();  // TMEM reads done: the accumulator may be overwritten
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty);
+            const int mt = t % mtiles, nt = t / mtiles;
+            const int row = mt * BM + 32 * q + lane;
+            if (row < M) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const size_t base = (size_t)row * N + nt * BN + 128 * ch + 32 * c;
+                    if (c_dtype == W4_F32) {
+                        float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(C) + base);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            dst[e] = make_float4(__uint_as_float(v[c][4 * e]) * gs, __uint_as_float(v[c][4 * e + 1]) * gs,
+                                                 __uint_as_float(v[c][4 * e + 2]) * gs,
+                                                 __uint_as_float(v[c][4 * e + 3]) * gs);
+                    } else {
+                        uint32_t p[16];
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) {
+                            const float x0 = __uint_as_float(v[c][2 * e]) * gs, x1 = __uint_as_float(v[c][2 * e + 1]) * gs;
+                            if (c_dtype == W4_BF16) {
+                                __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+                                p[e] = *reinterpret_cast<uint32_t *>(&h);
+                            } else {
+                                __half2 h = __floats2half2_rn(x0, x1);
+                                p[e] = *reinterpret_cast<uint32_t *>(&h);
+                            }
+                        }
+                        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(C) + base);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) dst[e] = make_uint4(p[4 * e], p[4 * e + 1], p[4 * e + 2], p[4 * e + 3]);
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
 }  // namespace fp4pf
 
 namespace fp4pf {
@@ -306,6 +488,31 @@ static int launch(const CUtensorMap &a_map, const CUtensorMap &w_map, const uint
     }
     dim3 grid((M + BM - 1) / BM, N / BN), block(kThreads);
     kern<<<grid, block, smem, st>>>(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K);
+    W4_LAUNCH_CHECK();
+    return W4_OK;
+}
+}  // namespace fp4pf
+
+namespace fp4pf {
+static int launch_persistent(const CUtensorMap &a_map, const CUtensorMap &w_map, const uint8_t *sfa,
+                             const uint8_t *sfb, const float *a_global, const float *w_global, void *c, int c_dtype,
+                             int M, int N, int K, cudaStream_t st) {
+    const size_t smem = pcfg::SMEM + 1024;
+    auto kern = nvfp4_prefill_persistent_kernel;
+    {
+        static std::mutex mu;
+        static bool set_dev[128] = {};
+        int dev = 0;
+        W4_CUDA_TRY(cudaGetDevice(&dev));
+        std::lock_guard<std::mutex> lk(mu);
+        if (dev < 128 && !set_dev[dev]) {
+            W4_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            set_dev[dev] = true;
+        }
+    }
+    const int tiles = (M + BM - 1) / BM * (N / pcfg::BN);
+    const int grid = tiles < num_sms() ? tiles : num_sms();
+    kern<<<grid, pcfg::kThreadsP, smem, st>>>(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K);
     W4_LAUNCH_CHECK();
     return W4_OK;
 }
@@ -339,18 +546,18 @@ int nvfp4_prefill(const uint16_t *a, const float *a_global, const uint8_t *w_nk,
         sfb = t;
     }
     CUtensorMap a_map, w_map;
-    // 256-wide tiles unless 128-wide ones need fewer waves
-    bool wide = N % 256 == 0;
-    if (wide) {
-        const long nsm = num_sms(), t256 = (long)((M + BM - 1) / BM) * (N / 256);
-        if ((2 * t256 + nsm - 1) / nsm < 2 * ((t256 + nsm - 1) / nsm)) wide = false;
-    }
+    // 256-wide tiles: persistent when there are more tiles than SMs, one tile per
+    // CTA otherwise; 128-wide tiles when N is not a multiple of 256.
+    const bool wide = N % 256 == 0;
+    const long tiles256 = (long)((M + BM - 1) / BM) * (N / 256);
+    const bool persistent = wide && tiles256 > num_sms();
     const int bn = wide ? 256 : 128;
     if (!make_map_2d(&a_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, codes, (uint64_t)K / 2, mp, (uint64_t)K / 2, BK / 2, BM,
                      CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_map_2d(&w_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_nk, (uint64_t)K / 2, N, (uint64_t)K / 2, BK / 2, bn,
                      CU_TENSOR_MAP_SWIZZLE_128B))
         return -1;
+    if (persistent) return launch_persistent(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K, st);
     return wide ? launch<256>(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K, st)
                 : launch<128>(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K, st);
 }
