@@ -317,6 +317,9 @@ static int launch_tma_t(const void *a, const int32_t *qweight, const int32_t *qz
     const long ctas = (long)nchunk * mblocks;
     const long ctas_per_sm = (ctas + nsm - 1) / nsm;
     long fit = ((224L * 1024) / ctas_per_sm - 1024) / (long)per_warp;
+    // the register file must hold ctas_per_sm CTAs of W + 1 warps as well
+    const long fit_regs = 65536L / (ctas_per_sm * 32L * kTmaMaxRegs) - 1;
+    if (fit_regs < fit) fit = fit_regs;
     int W = (int)(fit < 1 ? 1 : (fit > kTmaMaxWarps ? kTmaMaxWarps : fit));
     if (W > stages_total) W = stages_total;
     const CUtensorMapDataType adt =
