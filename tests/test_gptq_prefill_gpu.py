@@ -81,3 +81,18 @@ def test_config4_act_order_sampled_rows(cuda):
     rf, _ = assert_gemm_close(f32(y[rows.to(cuda)]), ref)
     assert rf < 4e-3, rf
     assert L.lib().w4_check_device_status() == L.W4_OK
+
+
+@pytest.mark.parametrize("M,K,N", [(32, 17408, 5120), (64, 5120, 7168), (48, 2176, 5120), (200, 4096, 640), (17, 8192, 256)])
+def test_prefill_split_k(cuda, M, K, N):
+    """Few output tiles: the tensor-core GEMM splits K across CTAs and sums fp32 partials
+    (tensor-parallel down / o projection shapes)."""
+    gs = 128
+    qw, qz, sc, _ = synth.gptq_weights(K, N, gs, asym=True, seed=K + M, device=cuda)
+    a = synth.activations(M, K, torch.bfloat16, seed=M, device=cuda)
+    assert L.lib().w4_gptq_workspace_bytes(M, N, K, gs, 0, L.W4_BF16) > 0  # partials are needed
+    got = ops.gptq_gemm(a, qw, qz, sc, gs, 1, out_dtype=torch.float32)
+    rf, _ = assert_gemm_close(np_(got), _oracle(a, qw, qz, sc, K, N, gs))
+    assert rf < 4e-3, rf
+    got16 = ops.gptq_gemm(a, qw, qz, sc, gs, 1)
+    assert_gemm_close(f32(got16), _oracle(a, qw, qz, sc, K, N, gs))

@@ -169,7 +169,8 @@ template <typename T, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
 gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap qw_map,
                     const __grid_constant__ CUtensorMap sc_map, const __grid_constant__ CUtensorMap zr_map,
-                    int has_z, void *__restrict__ C, int c_dtype, int M, int N, int K, int gs, int zero_offset) {
+                    int has_z, void *__restrict__ C, int c_dtype, int M, int N, int K, int gs, int zero_offset,
+                    int kb_per_split, float *__restrict__ partial) {
     using Lay = Layout<BN>;
     extern __shared__ uint8_t smem_dyn[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
@@ -182,7 +183,10 @@ gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
     volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + Lay::MISC_OFF + 4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
-    const int nk = K / BK;
+    // split-K: this CTA reduces k-blocks [kb0, kb0 + nk) and, when split, writes an
+    // fp32 partial tile that a second kernel sums
+    const int kb0 = blockIdx.z * kb_per_split;
+    const int nk = min(kb_per_split, K / BK - kb0);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -210,10 +214,11 @@ gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
             for (int i = 0; i < nk; ++i) {
                 const int s = i % S;
                 if (i >= S && !pf_wait(&empty[s], (uint32_t)(((i / S) - 1) & 1), abort_flag)) break;
-                const int g = (i * BK) / gs;
+                const int kb = kb0 + i;
+                const int g = (kb * BK) / gs;
                 mbar_arrive_expect_tx(&full[s], tx);
-                tma_load_2d(sm + Lay::A_OFF + s * Lay::A_BYTES, &a_map, i * BK, m0, &full[s]);
-                tma_load_2d(sm + Lay::QW_OFF + s * Lay::QW_BYTES, &qw_map, n0, i * (BK / 8), &full[s]);
+                tma_load_2d(sm + Lay::A_OFF + s * Lay::A_BYTES, &a_map, kb * BK, m0, &full[s]);
+                tma_load_2d(sm + Lay::QW_OFF + s * Lay::QW_BYTES, &qw_map, n0, kb * (BK / 8), &full[s]);
                 tma_load_2d(sm + Lay::SC_OFF + s * Lay::SC_BYTES, &sc_map, n0, g, &full[s]);
                 if (has_z) tma_load_2d(sm + Lay::ZR_OFF + s * Lay::ZR_SLOT, &zr_map, n0 / 8, g, &full[s]);
             }
@@ -290,7 +295,13 @@ gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
                 tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
                 if (row < M) {
                     const size_t base = (size_t)row * N + n0 + c0;
-                    if (c_dtype == W4_F32) {
+                    if (partial) {
+                        float4 *dst = reinterpret_cast<float4 *>(partial + (size_t)blockIdx.z * M * N + base);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            dst[e] = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
+                                                 __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
+                    } else if (c_dtype == W4_F32) {
                         float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(C) + base);
 #pragma unroll
                         for (int e = 0; e < 8; ++e)
@@ -325,9 +336,36 @@ gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
     }
 }
 
+// Sum of the split-K partial tiles, converted to the output type.
+__global__ void splitk_reduce_kernel(const float *__restrict__ partial, int splits, long mn, void *__restrict__ C,
+                                     int c_dtype) {
+    const long i4 = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (i4 >= mn) return;
+    float4 acc = *reinterpret_cast<const float4 *>(partial + i4);
+    for (int sp = 1; sp < splits; ++sp) {
+        const float4 v = *reinterpret_cast<const float4 *>(partial + (size_t)sp * mn + i4);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+    }
+    if (c_dtype == W4_F32) {
+        *reinterpret_cast<float4 *>(static_cast<float *>(C) + i4) = acc;
+    } else if (c_dtype == W4_BF16) {
+        __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+        *reinterpret_cast<uint2 *>(static_cast<uint16_t *>(C) + i4) =
+            make_uint2(*reinterpret_cast<uint32_t *>(&lo), *reinterpret_cast<uint32_t *>(&hi));
+    } else {
+        __half2 lo = __floats2half2_rn(acc.x, acc.y), hi = __floats2half2_rn(acc.z, acc.w);
+        *reinterpret_cast<uint2 *>(static_cast<uint16_t *>(C) + i4) =
+            make_uint2(*reinterpret_cast<uint32_t *>(&lo), *reinterpret_cast<uint32_t *>(&hi));
+    }
+}
+
 template <typename T, int BN>
 static int launch(const void *a, const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales, void *c,
-                  int c_dtype, int M, int N, int K, int gs, int zero_offset, cudaStream_t st) {
+                  int c_dtype, int M, int N, int K, int gs, int zero_offset, int ksplit, float *partial,
+                  cudaStream_t st) {
     using Lay = Layout<BN>;
     const CUtensorMapDataType adt =
         std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -359,35 +397,78 @@ static int launch(const void *a, const int32_t *qweight, const int32_t *qzeros, 
             set_dev[dev] = true;
         }
     }
-    dim3 grid((M + BM - 1) / BM, N / BN), block(kThreads);
-    kern<<<grid, block, smem, st>>>(a_map, qw_map, sc_map, zr_map, has_z, c, c_dtype, M, N, K, gs, zero_offset);
+    const int nk = K / BK;
+    const int kb_per_split = (nk + ksplit - 1) / ksplit;
+    ksplit = (nk + kb_per_split - 1) / kb_per_split;  // every split gets at least one k-block
+    dim3 grid((M + BM - 1) / BM, N / BN, ksplit), block(kThreads);
+    kern<<<grid, block, smem, st>>>(a_map, qw_map, sc_map, zr_map, has_z, c, c_dtype, M, N, K, gs, zero_offset,
+                                    kb_per_split, ksplit > 1 ? partial : nullptr);
     W4_LAUNCH_CHECK();
+    if (ksplit > 1) {
+        const long mn = (long)M * N;  // N % 128 == 0: whole float4 groups
+        splitk_reduce_kernel<<<(unsigned)((mn / 4 + 255) / 256), 256, 0, st>>>(partial, ksplit, mn, c, c_dtype);
+        W4_LAUNCH_CHECK();
+    }
     return W4_OK;
 }
 
 }  // namespace pf
 
+namespace pf {
+static bool handled(int N, int K, int gs, int c_dtype) {
+    return K % BK == 0 && gs % BK == 0 && N % 128 == 0 && c_dtype != W4_E4M3;
+}
+// 256-wide tiles unless 128-wide ones need fewer waves (a 128-wide tile takes
+// about half as long): small M leaves SMs idle otherwise.
+static bool wide_tiles(int M, int N) {
+    if (N % 256) return false;
+    const long nsm = num_sms(), t256 = (long)((M + BM - 1) / BM) * (N / 256);
+    const long w256 = 2 * ((t256 + nsm - 1) / nsm), w128 = (2 * t256 + nsm - 1) / nsm;
+    return !(w128 < w256);
+}
+// K splits when the output tiles fill at most half the SMs: as many as still
+// fit one wave (one CTA per SM), at least four k-blocks per split, at most 8.
+static int ksplit_for(int M, int N, int K) {
+    const long nsm = num_sms();
+    const long tiles = (long)((M + BM - 1) / BM) * (N / (wide_tiles(M, N) ? 256 : 128));
+    if (2 * tiles > nsm) return 1;
+    long ks = nsm / tiles;
+    const long by_k = (K / BK) / 4;
+    if (ks > by_k) ks = by_k;
+    if (ks > 8) ks = 8;
+    return ks < 1 ? 1 : (int)ks;
+}
+}  // namespace pf
+
+size_t gptq_prefill_split_bytes(int M, int N, int K, int gs, int c_dtype) {
+    if (M < kPrefillMinM || !pf::handled(N, K, gs, c_dtype)) return 0;
+    const int ks = pf::ksplit_for(M, N, K);
+    return ks > 1 ? (size_t)ks * M * N * sizeof(float) : 0;
+}
+
 // W4_OK / a W4 error, or -1 when this shape is not handled here (the caller
-// then runs the decode kernels).
+// then runs the decode kernels).  split_ws (gptq_prefill_split_bytes) holds the
+// split-K partials; without it the GEMM runs unsplit.
 int gptq_prefill(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
-                 void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset, cudaStream_t st) {
-    if (K % pf::BK || gs % pf::BK || N % 128 || c_dtype == W4_E4M3) return -1;
+                 void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset, void *split_ws,
+                 size_t split_ws_bytes, cudaStream_t st) {
+    if (!pf::handled(N, K, gs, c_dtype)) return -1;
     if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(qweight) |
          reinterpret_cast<uintptr_t>(scales) | reinterpret_cast<uintptr_t>(qzeros)) & 15)
         return -1;
-    // 256-wide tiles unless 128-wide ones need fewer waves (a 128-wide tile takes
-    // about half as long): small M leaves SMs idle otherwise.
-    bool wide = N % 256 == 0;
-    if (wide) {
-        const long nsm = num_sms(), t256 = (long)((M + pf::BM - 1) / pf::BM) * (N / 256);
-        const long w256 = 2 * ((t256 + nsm - 1) / nsm), w128 = (2 * t256 + nsm - 1) / nsm;
-        if (w128 < w256) wide = false;
-    }
+    const bool wide = pf::wide_tiles(M, N);
+    int ks = pf::ksplit_for(M, N, K);
+    if (ks > 1 && (!split_ws || split_ws_bytes < (size_t)ks * M * N * sizeof(float))) ks = 1;
+    float *partial = static_cast<float *>(split_ws);
     if (a_dtype == W4_BF16)
-        return wide ? pf::launch<__nv_bfloat16, 256>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st)
-                    : pf::launch<__nv_bfloat16, 128>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
-    return wide ? pf::launch<__half, 256>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st)
-                : pf::launch<__half, 128>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+        return wide ? pf::launch<__nv_bfloat16, 256>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset,
+                                                     ks, partial, st)
+                    : pf::launch<__nv_bfloat16, 128>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset,
+                                                     ks, partial, st);
+    return wide ? pf::launch<__half, 256>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ks,
+                                          partial, st)
+                : pf::launch<__half, 128>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ks,
+                                          partial, st);
 }
 
 int take_prefill_wait_status() {

@@ -112,6 +112,8 @@ size_t w4_gptq_workspace_bytes(int M, int N, int K, int group_size, int has_perm
     if (M <= 0 || N <= 0 || K <= 0) return 0;
     if (has_perm) ws += align256((size_t)M * K * 2);
     if (c_dtype == W4_E4M3) ws += align256((size_t)M * N * 4);
+    // split-K partials of the tensor-core GEMM (the f32 product when the output is e4m3)
+    ws += align256(w4::gptq_prefill_split_bytes(M, N, K, group_size, c_dtype == W4_E4M3 ? W4_F32 : c_dtype));
     return ws;
 }
 
@@ -148,15 +150,18 @@ int w4_gptq_gemm(const void *a, int a_dtype, const int32_t *qweight, const int32
         if (rc) return rc;
         a_eff = ap;
     }
+    const size_t split = align256(
+        w4::gptq_prefill_split_bytes(M, N, K, group_size, c_dtype == W4_E4M3 ? W4_F32 : c_dtype));
     if (c_dtype == W4_E4M3) {
         float *y = reinterpret_cast<float *>(ws);
+        ws += align256((size_t)M * N * 4);
         rc = w4::gptq_gemv(a_eff, a_dtype, qweight, qzeros, scales, y, W4_F32, M, N, K, group_size,
-                           zero_offset, st);
+                           zero_offset, split ? ws : nullptr, split, st);
         if (rc) return rc;
         return w4::rowscale_fp8(y, W4_F32, static_cast<uint8_t *>(c), row_scale, M, N, st);
     }
     return w4::gptq_gemv(a_eff, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, group_size,
-                         zero_offset, st);
+                         zero_offset, split ? ws : nullptr, split, st);
 }
 
 int w4_gptq_gemm_s4a(const uint8_t *a_s4, const uint8_t *b_s4, const float *a_scale,

@@ -13,16 +13,20 @@ int gptq_repack_act_order(const int32_t *qweight, const int32_t *g_idx, int K, i
                           int32_t *qweight_out, int32_t *perm_out, cudaStream_t st);
 int gather_cols(const uint16_t *a, const int32_t *perm, int M, int K, uint16_t *out,
                 cudaStream_t st);
+// Any M: the tensor-core GEMM for M >= kPrefillMinM when it takes the shape, else
+// the decode kernels.  ws / ws_bytes: scratch for split-K partials (may be null).
 int gptq_gemv(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
               const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs,
-              int zero_offset, cudaStream_t st);
+              int zero_offset, void *ws, size_t ws_bytes, cudaStream_t st);
 int gptq_gemv_tma(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
                   const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
                   cudaStream_t st);
 int take_wait_status();
 // gptq_prefill.cu (tcgen05); -1 = shape not handled there
 int gptq_prefill(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
-                 void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset, cudaStream_t st);
+                 void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset, void *split_ws,
+                 size_t split_ws_bytes, cudaStream_t st);
+size_t gptq_prefill_split_bytes(int M, int N, int K, int gs, int c_dtype);
 int take_prefill_wait_status();
 constexpr int kPrefillMinM = 17;  // token counts from here on run the tensor-core prefill GEMM
 int gptq_s4a(const uint8_t *a, const uint8_t *b, const float *a_scale, const uint16_t *s,
