@@ -40,13 +40,15 @@ static __device__ unsigned int g_prefill_timeout;  // a bounded wait expired (st
 namespace pf {
 
 constexpr int BM = 128, BK = 64;
-constexpr int S = 4;          // A + raw-weight ring depth
+constexpr int S = 4;          // A + raw-weight ring depth (one A tile per CTA)
 constexpr int SB = 3;         // dequantised-B ring depth
 constexpr int kDeqWarps = 16;  // two threads per column of a 256-wide tile
 constexpr int kThreads = (2 + kDeqWarps) * 32;
 
-template <int BN> struct Layout {
-    static constexpr uint32_t A_BYTES = BM * BK * 2;         // 16 KB
+// MT: 128-row A tiles per CTA sharing one dequantised B tile (1 or 2).
+template <int BN, int MT> struct Layout {
+    static constexpr int S = MT == 2 ? 3 : 4;                // A + raw-weight ring depth
+    static constexpr uint32_t A_BYTES = MT * BM * BK * 2;    // 16 KB per 128 rows
     static constexpr uint32_t B_BYTES = BN * BK * 2;         // 32 KB at BN = 256
     static constexpr uint32_t QW_BYTES = (BK / 8) * BN * 4;  // 8 KB
     static constexpr uint32_t SC_BYTES = BN * 2;             // one f16 scale row
@@ -59,6 +61,7 @@ template <int BN> struct Layout {
     static constexpr uint32_t BAR_OFF = ZR_OFF + S * ZR_SLOT;  // full[S] empty[S] bfull[SB] bempty[SB] done
     static constexpr uint32_t MISC_OFF = BAR_OFF + (2 * S + 2 * SB + 1) * 8;
     static constexpr uint32_t TOTAL = MISC_OFF + 16;
+    static_assert(TOTAL + 1024 <= 227 * 1024, "fits the shared memory of one CTA");
     static_assert(B_OFF % 1024 == 0 && QW_OFF % 128 == 0 && SC_OFF % 128 == 0 && ZR_OFF % 128 == 0,
                   "TMA destinations: swizzled tiles 1024-aligned, others 128-aligned");
     static_assert(BN / 2 <= ZR_SLOT, "zero row fits its slot");
@@ -165,13 +168,14 @@ __device__ __forceinline__ bool pf_wait(uint64_t *bar, uint32_t parity, volatile
     return true;
 }
 
-template <typename T, int BN>
+template <typename T, int BN, int MT>
 __global__ void __launch_bounds__(kThreads, 1)
 gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap qw_map,
                     const __grid_constant__ CUtensorMap sc_map, const __grid_constant__ CUtensorMap zr_map,
                     int has_z, void *__restrict__ C, int c_dtype, int M, int N, int K, int gs, int zero_offset,
                     int kb_per_split, float *__restrict__ partial) {
-    using Lay = Layout<BN>;
+    using Lay = Layout<BN, MT>;
+    constexpr int S = Lay::S;
     extern __shared__ uint8_t smem_dyn[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(sm + Lay::BAR_OFF);
@@ -182,7 +186,7 @@ gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + Lay::MISC_OFF);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + Lay::MISC_OFF + 4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+    const int m0 = blockIdx.x * BM * MT, n0 = blockIdx.y * BN;
     // split-K: this CTA reduces k-blocks [kb0, kb0 + nk) and, when split, writes an
     // fp32 partial tile that a second kernel sums
     const int kb0 = blockIdx.z * kb_per_split;
@@ -201,7 +205,7 @@ gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
         *abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 1) tmem_alloc(tmem_slot, BN);
+    if (warp == 1) tmem_alloc(tmem_slot, MT * BN);  // one accumulator per 128-row A tile
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -236,8 +240,10 @@ gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
                 const uint32_t b_addr = smem_u32(sm + Lay::B_OFF + j * Lay::B_BYTES);
 #pragma unroll
                 for (int kk = 0; kk < BK / 16; ++kk)
-                    mma_f16_ss(tmem, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32), idesc,
-                               (i | kk) != 0);
+#pragma unroll
+                    for (int mh = 0; mh < MT; ++mh)  // same B tile, A rows 128 * mh .. +127
+                        mma_f16_ss(tmem + (uint32_t)(mh * BN), sw128_kmajor_desc(a_addr + mh * (BM * 128) + kk * 32),
+                                   sw128_kmajor_desc(b_addr + kk * 32), idesc, (i | kk) != 0);
                 tc_commit(&empty[s]);
                 tc_commit(&bempty[j]);
             }
@@ -288,11 +294,12 @@ gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
             (void)ok;
             tc_fence_after();
             const int q = warp & 3;
-            const int row = m0 + 32 * q + lane;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
+            for (int cc = 0; cc < MT * BN; cc += 32) {
+                const int mh = cc / BN, c0 = cc % BN;
+                const int row = m0 + mh * BM + 32 * q + lane;
                 uint32_t v[32];
-                tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+                tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)cc, v);
                 if (row < M) {
                     const size_t base = (size_t)row * N + n0 + c0;
                     if (partial) {
@@ -332,7 +339,7 @@ gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, BN);
+        tmem_dealloc(tmem, MT * BN);
     }
 }
 
@@ -362,15 +369,15 @@ __global__ void splitk_reduce_kernel(const float *__restrict__ partial, int spli
     }
 }
 
-template <typename T, int BN>
+template <typename T, int BN, int MT>
 static int launch(const void *a, const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales, void *c,
                   int c_dtype, int M, int N, int K, int gs, int zero_offset, int ksplit, float *partial,
                   cudaStream_t st) {
-    using Lay = Layout<BN>;
+    using Lay = Layout<BN, MT>;
     const CUtensorMapDataType adt =
         std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     CUtensorMap a_map, qw_map, sc_map, zr_map;
-    if (!make_map_2d(&a_map, adt, a, K, M, (uint64_t)K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+    if (!make_map_2d(&a_map, adt, a, K, M, (uint64_t)K * 2, BK, BM * MT, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_map_2d(&qw_map, CU_TENSOR_MAP_DATA_TYPE_INT32, qweight, N, K / 8, (uint64_t)N * 4, BN, BK / 8,
                      CU_TENSOR_MAP_SWIZZLE_NONE) ||
         !make_map_2d(&sc_map, CU_TENSOR_MAP_DATA_TYPE_UINT16, scales, N, K / gs, (uint64_t)N * 2, BN, 1,
@@ -384,7 +391,7 @@ static int launch(const void *a, const int32_t *qweight, const int32_t *qzeros, 
     } else {
         zr_map = sc_map;  // unused
     }
-    auto kern = gptq_prefill_kernel<T, BN>;
+    auto kern = gptq_prefill_kernel<T, BN, MT>;
     const size_t smem = Lay::TOTAL + 1024;
     {
         static std::mutex mu;
@@ -400,7 +407,7 @@ static int launch(const void *a, const int32_t *qweight, const int32_t *qzeros, 
     const int nk = K / BK;
     const int kb_per_split = (nk + ksplit - 1) / ksplit;
     ksplit = (nk + kb_per_split - 1) / kb_per_split;  // every split gets at least one k-block
-    dim3 grid((M + BM - 1) / BM, N / BN, ksplit), block(kThreads);
+    dim3 grid((M + BM * MT - 1) / (BM * MT), N / BN, ksplit), block(kThreads);
     kern<<<grid, block, smem, st>>>(a_map, qw_map, sc_map, zr_map, has_z, c, c_dtype, M, N, K, gs, zero_offset,
                                     kb_per_split, ksplit > 1 ? partial : nullptr);
     W4_LAUNCH_CHECK();
@@ -418,11 +425,17 @@ namespace pf {
 static bool handled(int N, int K, int gs, int c_dtype) {
     return K % BK == 0 && gs % BK == 0 && N % 128 == 0 && c_dtype != W4_E4M3;
 }
-// 256-wide tiles unless 128-wide ones need fewer waves (a 128-wide tile takes
-// about half as long): small M leaves SMs idle otherwise.
+static int m_tiles_per_cta(int M) { return M > BM ? 2 : 1; }  // two A tiles share each dequantised B tile
+static long tiles_of(int M, int N, bool wide) {
+    const int bm = BM * m_tiles_per_cta(M);
+    return (long)((M + bm - 1) / bm) * (N / (wide ? 256 : 128));
+}
+// 256-wide tiles, unless they do not fill one wave and 128-wide ones need fewer
+// waves (a 128-wide tile takes about half as long): small M leaves SMs idle.
 static bool wide_tiles(int M, int N) {
     if (N % 256) return false;
-    const long nsm = num_sms(), t256 = (long)((M + BM - 1) / BM) * (N / 256);
+    const long nsm = num_sms(), t256 = tiles_of(M, N, true);
+    if (t256 >= nsm) return true;
     const long w256 = 2 * ((t256 + nsm - 1) / nsm), w128 = (2 * t256 + nsm - 1) / nsm;
     return !(w128 < w256);
 }
@@ -430,7 +443,7 @@ static bool wide_tiles(int M, int N) {
 // fit one wave (one CTA per SM), at least four k-blocks per split, at most 8.
 static int ksplit_for(int M, int N, int K) {
     const long nsm = num_sms();
-    const long tiles = (long)((M + BM - 1) / BM) * (N / (wide_tiles(M, N) ? 256 : 128));
+    const long tiles = tiles_of(M, N, wide_tiles(M, N));
     if (2 * tiles > nsm) return 1;
     long ks = nsm / tiles;
     const long by_k = (K / BK) / 4;
@@ -460,15 +473,16 @@ int gptq_prefill(const void *a, int a_dtype, const int32_t *qweight, const int32
     int ks = pf::ksplit_for(M, N, K);
     if (ks > 1 && (!split_ws || split_ws_bytes < (size_t)ks * M * N * sizeof(float))) ks = 1;
     float *partial = static_cast<float *>(split_ws);
-    if (a_dtype == W4_BF16)
-        return wide ? pf::launch<__nv_bfloat16, 256>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset,
-                                                     ks, partial, st)
-                    : pf::launch<__nv_bfloat16, 128>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset,
-                                                     ks, partial, st);
-    return wide ? pf::launch<__half, 256>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ks,
-                                          partial, st)
-                : pf::launch<__half, 128>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ks,
-                                          partial, st);
+    const int mt = pf::m_tiles_per_cta(M);
+#define W4_PF_LAUNCH(TT, BNV, MTV) \
+    pf::launch<TT, BNV, MTV>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ks, partial, st)
+    if (a_dtype == W4_BF16) {
+        if (mt == 2) return wide ? W4_PF_LAUNCH(__nv_bfloat16, 256, 2) : W4_PF_LAUNCH(__nv_bfloat16, 128, 2);
+        return wide ? W4_PF_LAUNCH(__nv_bfloat16, 256, 1) : W4_PF_LAUNCH(__nv_bfloat16, 128, 1);
+    }
+    if (mt == 2) return wide ? W4_PF_LAUNCH(__half, 256, 2) : W4_PF_LAUNCH(__half, 128, 2);
+    return wide ? W4_PF_LAUNCH(__half, 256, 1) : W4_PF_LAUNCH(__half, 128, 1);
+#undef W4_PF_LAUNCH
 }
 
 int take_prefill_wait_status() {
