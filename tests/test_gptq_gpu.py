@@ -150,3 +150,19 @@ def test_torch_op_registration(cuda):
     a = synth.activations(M, K, torch.float16, device=cuda)
     out = torch.ops.w4.gptq_gemm(a, qw, qz, sc, None, gs, 1)
     assert torch.equal(out, ops.gptq_gemm(a, qw, qz, sc, gs, 1))
+
+
+def test_out_argument_writes_in_place(cuda):
+    K, N, gs = 1024, 256, 128
+    qw, qz, sc, _ = synth.gptq_weights(K, N, gs, asym=True, seed=31, device=cuda)
+    a = synth.activations(24, K, torch.bfloat16, seed=32, device=cuda)
+    buf = torch.full((30, N), float("nan"), dtype=torch.bfloat16, device=cuda)
+    ref = ops.gptq_gemm(a, qw, qz, sc, gs, 1)
+    got = ops.gptq_gemm(a[:8], qw, qz, sc, gs, 1, out=buf[2:10])
+    assert got.data_ptr() == buf[2:10].data_ptr()
+    assert torch.equal(buf[2:10], ops.gptq_gemm(a[:8].contiguous(), qw, qz, sc, gs, 1))
+    assert torch.isnan(buf[:2].float()).all() and torch.isnan(buf[10:].float()).all()
+    ops.gptq_gemm(a, qw, qz, sc, gs, 1, out=buf[4:28])
+    assert torch.equal(buf[4:28], ref)
+    with pytest.raises(ValueError):
+        ops.gptq_gemm(a, qw, qz, sc, gs, 1, out=buf[:10])

@@ -98,12 +98,13 @@ def gptq_repack_act_order(qweight, g_idx, group_size=128):
 
 
 def gptq_gemm(a, qweight, qzeros, scales, group_size=128, zero_offset=1, perm=None,
-              out_dtype=None, return_row_scale=False):
+              out_dtype=None, return_row_scale=False, out=None):
     """W4A16 GPTQ GEMM: a [M, K] f16/bf16 -> [M, N] (fp32 accumulate).
 
     ``perm`` comes from :func:`gptq_repack_act_order` (then ``qweight`` must be
     the repacked one).  ``out_dtype=torch.float8_e4m3fn`` applies the per-row
-    fp8 cast and also returns the f32 row scales.
+    fp8 cast and also returns the f32 row scales.  ``out`` (optional) receives
+    the result in place.
     """
     _need_cuda(a, qweight, qzeros, scales, perm)
     for t, n in ((a, "a"), (qweight, "qweight"), (qzeros, "qzeros"), (scales, "scales"), (perm, "perm")):
@@ -112,8 +113,13 @@ def gptq_gemm(a, qweight, qzeros, scales, group_size=128, zero_offset=1, perm=No
     N = qweight.shape[1]
     if qweight.shape[0] * 8 != K:
         raise ValueError(f"qweight {tuple(qweight.shape)} does not match K={K}")
-    out_dtype = out_dtype or a.dtype
-    c = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    out_dtype = out_dtype or (out.dtype if out is not None else a.dtype)
+    if out is not None:
+        if out.shape != (M, N) or out.dtype != out_dtype or not out.is_contiguous() or out.device != a.device:
+            raise ValueError(f"out must be a contiguous {out_dtype} [{M}, {N}] tensor on {a.device}")
+        c = out
+    else:
+        c = torch.empty((M, N), dtype=out_dtype, device=a.device)
     rs = torch.empty(M, dtype=torch.float32, device=a.device) if out_dtype == torch.float8_e4m3fn else None
     need = L.lib().w4_gptq_workspace_bytes(M, N, K, group_size, int(perm is not None), _DT[out_dtype])
     ws, wsb = _WS.get(a.device, need)
