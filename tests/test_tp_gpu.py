@@ -38,11 +38,41 @@ def _case_layers(rank, world):
     dev = torch.device("cuda", rank)
     comm = tp.TPComm(rank, world, timeout_ms=60000, device=dev)
     try:
-        # identity check of the collective
-        t = torch.full((4096,), float(rank + 1), dtype=torch.bfloat16, device=dev)
-        comm.allreduce_(t)
+        # identity check of the collective (one-shot peer-memory path for small messages,
+        # NCCL above its slot size)
+        for n in (4096, 8, 40000, 1 << 20):
+            t = torch.full((n,), float(rank + 1), dtype=torch.bfloat16, device=dev)
+            comm.allreduce_(t)
+            comm.wait()
+            assert torch.all(t == float(sum(r + 1 for r in range(world)))), n
+        # every rank ends with the same bits, in f32 too
+        g = torch.Generator(device=dev).manual_seed(rank)
+        x = torch.randn(12288, generator=g, device=dev)
+        ref = sum(torch.randn(12288, generator=torch.Generator(device=dev).manual_seed(r), device=dev)
+                  for r in range(world))
+        comm.allreduce_(x)
         comm.wait()
-        assert torch.all(t == float(sum(r + 1 for r in range(world))))
+        assert torch.allclose(x, ref, rtol=1e-6, atol=1e-6)
+        # captured in a CUDA graph and replayed: the per-call counters live on the device
+        y = torch.zeros(5120, dtype=torch.bfloat16, device=dev)
+        st = torch.cuda.Stream(dev)
+        st.wait_stream(torch.cuda.current_stream(dev))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(st):
+            y.fill_(float(rank + 1))
+            comm.allreduce_(y)  # warm-up outside capture
+            torch.cuda.synchronize(dev)
+            with torch.cuda.graph(graph, stream=st):
+                y.fill_(float(rank + 1))
+                comm.allreduce_(y)
+                y.mul_(2.0)
+                comm.allreduce_(y)
+        torch.cuda.current_stream(dev).wait_stream(st)
+        for _ in range(3):
+            graph.replay()
+            comm.wait()
+            assert torch.all(y == float(2 * world * sum(r + 1 for r in range(world))))
+        del graph
 
         gs = 128
         for M in (1, 32, 256):

@@ -40,7 +40,6 @@ static __device__ unsigned int g_prefill_timeout;  // a bounded wait expired (st
 namespace pf {
 
 constexpr int BM = 128, BK = 64;
-constexpr int S = 4;          // A + raw-weight ring depth (one A tile per CTA)
 constexpr int SB = 3;         // dequantised-B ring depth
 constexpr int kDeqWarps = 16;  // two threads per column of a 256-wide tile
 constexpr int kThreads = (2 + kDeqWarps) * 32;

@@ -19,62 +19,15 @@
 // joins or never reaches the collective, the wait expires, the communicator
 // is aborted (NCCL stops its in-flight kernels) and W4_ERR_TIMEOUT is
 // returned; the communicator is unusable afterwards.
-#include <dlfcn.h>
-#include <nccl.h>
-
 #include <chrono>
-#include <mutex>
 #include <thread>
 
+#include "tp_internal.h"
 #include "w4_common.cuh"
 #include "w4_internal.h"
 
-struct w4_tp_comm {
-    ncclComm_t comm;
-    int nranks, rank;
-    int timeout_ms;  // bound on every host-side wait for this communicator
-    bool dead;
-};
-
 namespace w4 {
 namespace {
-
-struct NcclApi {
-    ncclResult_t (*get_unique_id)(ncclUniqueId *);
-    ncclResult_t (*comm_init_rank_config)(ncclComm_t *, int, ncclUniqueId, int, ncclConfig_t *);
-    ncclResult_t (*comm_get_async_error)(ncclComm_t, ncclResult_t *);
-    ncclResult_t (*comm_abort)(ncclComm_t);
-    ncclResult_t (*comm_finalize)(ncclComm_t);
-    ncclResult_t (*comm_destroy)(ncclComm_t);
-    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
-                               cudaStream_t);
-    const char *(*error_string)(ncclResult_t);
-    bool ok;
-};
-
-const NcclApi &nccl() {
-    static NcclApi api{};
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
-        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
-        if (!h) return;
-        auto sym = [&](const char *n) { return dlsym(h, n); };
-        api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(sym("ncclGetUniqueId"));
-        api.comm_init_rank_config =
-            reinterpret_cast<decltype(api.comm_init_rank_config)>(sym("ncclCommInitRankConfig"));
-        api.comm_get_async_error =
-            reinterpret_cast<decltype(api.comm_get_async_error)>(sym("ncclCommGetAsyncError"));
-        api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(sym("ncclCommAbort"));
-        api.comm_finalize = reinterpret_cast<decltype(api.comm_finalize)>(sym("ncclCommFinalize"));
-        api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(sym("ncclCommDestroy"));
-        api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(sym("ncclAllReduce"));
-        api.error_string = reinterpret_cast<decltype(api.error_string)>(sym("ncclGetErrorString"));
-        api.ok = api.get_unique_id && api.comm_init_rank_config && api.comm_get_async_error &&
-                 api.comm_abort && api.comm_finalize && api.comm_destroy && api.all_reduce && api.error_string;
-    });
-    return api;
-}
 
 #define W4_NCCL_API()                                                                                     \
     const NcclApi &api = nccl();                                                                          \
@@ -158,6 +111,12 @@ extern "C" int w4_tp_comm_init(w4_tp_comm **out, int nranks, int rank, const uin
         delete c;
         return rc;
     }
+    rc = tp_peer_setup(c);  // peer-memory all-reduce; without it NCCL carries every call
+    if (rc) {
+        api.comm_abort(c->comm);
+        delete c;
+        return rc;
+    }
     *out = c;
     return W4_OK;
 }
@@ -175,6 +134,7 @@ extern "C" int w4_tp_comm_destroy(w4_tp_comm *c) {
             delete c;
             return rc;
         }
+        tp_peer_teardown(c);
         ncclResult_t r = api.comm_finalize(c->comm);
         if (r == ncclSuccess || r == ncclInProgress) rc = wait_comm_ready(api, c, c->timeout_ms);
         else rc = nccl_fail(api, r, "ncclCommFinalize");
@@ -189,6 +149,7 @@ extern "C" int w4_tp_comm_abort(w4_tp_comm *c) {
     if (!c) return W4_OK;
     W4_NCCL_API();
     if (!c->dead) api.comm_abort(c->comm);
+    tp_peer_teardown(c);
     delete c;
     return W4_OK;
 }
@@ -201,6 +162,8 @@ extern "C" int w4_tp_allreduce(w4_tp_comm *c, void *buf, size_t count, int dtype
                "dtype must be f16, bf16 or f32");
     W4_NCCL_API();
     if (count == 0 || c->nranks == 1) return W4_OK;
+    const int rp = tp_peer_allreduce(c, buf, count, dtype, reinterpret_cast<cudaStream_t>(stream));
+    if (rp >= 0) return rp;
     ncclResult_t r = api.all_reduce(buf, buf, count, nccl_dtype(dtype), ncclSum, c->comm,
                                     reinterpret_cast<cudaStream_t>(stream));
     if (r == ncclInProgress)  // a non-blocking communicator finishing the enqueue (e.g. first-use connections)
@@ -219,7 +182,15 @@ extern "C" int w4_tp_wait(w4_tp_comm *c, void *stream, int timeout_ms) {
     const auto t0 = Clock::now();
     for (;;) {
         cudaError_t q = cudaStreamQuery(st);
-        if (q == cudaSuccess) return W4_OK;
+        if (q == cudaSuccess) {
+            // a one-shot all-reduce whose peer never pushed ended with a device status
+            const int rs = c->p2p ? take_tp_wait_status() : W4_OK;
+            if (rs) {
+                api.comm_abort(c->comm);
+                c->dead = true;
+            }
+            return rs;
+        }
         if (q != cudaErrorNotReady) {
             set_error("stream error: %s", cudaGetErrorString(q));
             return W4_ERR_CUDA;

@@ -8,6 +8,7 @@
 
 #include "w4_common.cuh"
 #include "w4_internal.h"
+#include "tp_internal.h"
 
 namespace w4 {
 
@@ -70,7 +71,8 @@ int w4_check_device_status(void) {
     const int r2 = w4::take_prefill_wait_status();
     const int r3 = w4::take_fp4_wait_status();
     const int r4 = w4::take_fp4_prefill_wait_status();
-    return r1 ? r1 : r2 ? r2 : r3 ? r3 : r4;
+    const int r5 = w4::take_tp_wait_status();
+    return r1 ? r1 : r2 ? r2 : r3 ? r3 : r4 ? r4 : r5;
 }
 
 // ------------------------------------------------------------------ GPTQ
