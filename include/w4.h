@@ -81,6 +81,27 @@ const char *w4_last_error(void);
  * have no device-side waits). */
 int w4_check_device_status(void);
 
+/* How the decode GEMMs (the TMA-streamed M <= 16 kernels) are ordered behind
+ * the previous kernel on the stream (programmatic dependent launch).
+ * Process-wide; no counterpart in the reference, whose operators launch plainly.
+ *   W4_OVERLAP_OFF             plain launches.
+ *   W4_OVERLAP_DEPENDENT       (default) the GEMM may be scheduled while the
+ *                              previous kernel drains; it sets up its barriers
+ *                              and reads nothing until that kernel completed.
+ *   W4_OVERLAP_STATIC_WEIGHTS  as above, and it also starts streaming the
+ *                              weight operands (qweight, scales, zeros / NVFP4
+ *                              codes and block scales) before then.  Only for
+ *                              callers whose weights are never written by the
+ *                              kernel that precedes the GEMM on the stream
+ *                              (inference on loaded checkpoints). */
+enum w4_overlap {
+    W4_OVERLAP_OFF = 0,
+    W4_OVERLAP_DEPENDENT = 1,
+    W4_OVERLAP_STATIC_WEIGHTS = 2
+};
+int w4_set_launch_overlap(int mode);
+int w4_get_launch_overlap(void);
+
 /* ===================================================================== */
 /* GPTQ int4                                                              */
 /* ===================================================================== */

@@ -86,3 +86,17 @@ def test_nvfp4_rejects_bad_arguments_without_gpu():
 def test_oracle_library_loads():
     import oracle as O
     assert O.e2m1_value(7) == 6.0
+
+
+def test_launch_overlap_mode_round_trip():
+    lib = L.lib()
+    old = lib.w4_get_launch_overlap()
+    assert old == L.W4_OVERLAP_DEPENDENT  # the default
+    try:
+        for m in (L.W4_OVERLAP_OFF, L.W4_OVERLAP_STATIC_WEIGHTS, L.W4_OVERLAP_DEPENDENT):
+            assert lib.w4_set_launch_overlap(m) == L.W4_OK
+            assert lib.w4_get_launch_overlap() == m
+        assert lib.w4_set_launch_overlap(3) == L.W4_ERR_INVALID
+        assert lib.w4_get_launch_overlap() == L.W4_OVERLAP_DEPENDENT
+    finally:
+        lib.w4_set_launch_overlap(old)

@@ -18,6 +18,7 @@ W4_F16, W4_BF16, W4_F32, W4_E4M3, W4_S8, W4_E4M3_ATOMS = range(6)
 W4_NVFP4_KN, W4_NVFP4_NK = 0, 1
 W4_ACT_W4A16, W4_ACT_NVFP4 = 0, 1
 W4_TP_COLUMN, W4_TP_ROW = 0, 1
+W4_OVERLAP_OFF, W4_OVERLAP_DEPENDENT, W4_OVERLAP_STATIC_WEIGHTS = 0, 1, 2
 W4_TP_UNIQUE_ID_BYTES = 128
 
 HEADER = os.path.join(os.path.dirname(_build.HERE), "include", "w4.h")
@@ -39,6 +40,8 @@ _SIGS = {
     "w4_status_string": (ctypes.c_char_p, [_I]),
     "w4_last_error": (ctypes.c_char_p, []),
     "w4_check_device_status": (_I, []),
+    "w4_set_launch_overlap": (_I, [_I]),
+    "w4_get_launch_overlap": (_I, []),
     "w4_gptq_dequant": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "w4_gptq_repack_act_order": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
     "w4_gptq_workspace_bytes": (_Z, [_I, _I, _I, _I, _I, _I]),

@@ -81,7 +81,7 @@ __global__ void __maxnreg__(kTmaMaxRegs)
 gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_constant__ CUtensorMap sc_map,
                      const __grid_constant__ CUtensorMap zr_map, const __grid_constant__ CUtensorMap act_map,
                      int has_z, const T *__restrict__ A, void *__restrict__ C, int c_dtype, int M, int N, int K,
-                     int zero_offset, int stages_total, int act_rows) {
+                     int zero_offset, int stages_total, int act_rows, int pre) {
     constexpr int S = kTmaStages;
     constexpr int NE = 2 * NT * 4;
     constexpr int ROWS = 4 * GSTEPS;           // qweight rows per group
@@ -106,11 +106,28 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
         }
     }
     __syncthreads();  // barriers initialised before anyone waits on them
+    grid_dep_launch();  // the next decode GEMM may set up while this one runs
     if (warp == W) {
         if (lane == 0) {
             const uint32_t tx = kVps * (ROWS * 128 + 64 + (has_z ? 16 : 0)) + (ACT ? act_rows * SSTEPS * 64 : 0);
             bool ok = true;
             const int most = (stages_total + W - 1) / W;
+            // pre: the weight operands of the first ring fill are requested before
+            // the previous kernel on the stream has completed (static weights).
+            const int pf = pre ? (most < S ? most : S) : 0;
+            for (int it = 0; it < pf; ++it)
+                for (int w = 0; w < W; ++w) {
+                    const int sb = w * stages_total / W, se = (w + 1) * stages_total / W;
+                    if (sb + it >= se) continue;
+                    uint8_t *r = base + (size_t)w * L.total;
+                    uint64_t *full = reinterpret_cast<uint64_t *>(r + L.bars) + it;
+                    const int vg = (sb + it) * kVps;
+                    mbar_arrive_expect_tx(full, tx);
+                    tma_load_2d(r + it * L.qw_stage, &qw_map, n0, vg * ROWS, full);
+                    tma_load_2d(r + L.cst + it * 256, &sc_map, n0, vg, full);
+                    if (has_z) tma_load_2d(r + L.cst + it * 256 + 128, &zr_map, n0 / 8, vg, full);
+                }
+            grid_dep_wait();  // activations are the previous kernel's output
             for (int it = 0; it < most && ok; ++it) {
                 const int s = it % S;
                 for (int w = 0; w < W && ok; ++w) {
@@ -119,22 +136,25 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
                     uint8_t *r = base + (size_t)w * L.total;
                     uint64_t *full = reinterpret_cast<uint64_t *>(r + L.bars) + s;
                     uint64_t *empty = full + S;
-                    if (it >= S && !mbar_wait_bounded(empty, (uint32_t)(((it / S) - 1) & 1))) {
-                        atomicExch(&g_wait_timeout, 1u);
-                        ok = false;
-                        break;
-                    }
                     const int vg = (sb + it) * kVps;  // first group of the stage
-                    mbar_arrive_expect_tx(full, tx);
-                    tma_load_2d(r + s * L.qw_stage, &qw_map, n0, vg * ROWS, full);
+                    if (it >= pf) {
+                        if (it >= S && !mbar_wait_bounded(empty, (uint32_t)(((it / S) - 1) & 1))) {
+                            atomicExch(&g_wait_timeout, 1u);
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(full, tx);
+                        tma_load_2d(r + s * L.qw_stage, &qw_map, n0, vg * ROWS, full);
+                        tma_load_2d(r + L.cst + s * 256, &sc_map, n0, vg, full);
+                        if (has_z) tma_load_2d(r + L.cst + s * 256 + 128, &zr_map, n0 / 8, vg, full);
+                    }
                     if (ACT) tma_load_3d(r + L.act + s * L.act_stage, &act_map, 0, tok0, (vg * ROWS) / 8, full);  // 64-k line of the stage
-                    tma_load_2d(r + L.cst + s * 256, &sc_map, n0, vg, full);
-                    if (has_z) tma_load_2d(r + L.cst + s * 256 + 128, &zr_map, n0 / 8, vg, full);
                 }
             }
         }
         return;  // consumers wait for every copy this warp issued
     }
+    grid_dep_wait();  // nothing below touches global memory before the previous kernel completed
 
     // ---------------- consumer warps ----------------
     uint8_t *ring = base + (size_t)warp * L.total;
@@ -359,9 +379,10 @@ static int launch_tma_t(const void *a, const int32_t *qweight, const int32_t *qz
     const size_t smem = 1024 + (size_t)W * per_warp;
     if (smem > 220 * 1024) return -1;
     dim3 grid(mblocks, nchunk), block(32 * (W + 1));
-    kern<<<grid, block, smem, st>>>(qw_map, sc_map, zr_map, act_map, has_z, static_cast<const T *>(a), c, c_dtype,
-                                    M, N, K, zero_offset, stages_total, act_rows);
-    W4_LAUNCH_CHECK();
+    const int pre = launch_overlap() == W4_OVERLAP_STATIC_WEIGHTS;
+    W4_CUDA_TRY(launch_decode(kern, grid, block, smem, st, qw_map, sc_map, zr_map, act_map, has_z,
+                              static_cast<const T *>(a), c, c_dtype, M, N, K, zero_offset, stages_total, act_rows,
+                              pre));
     return W4_OK;
 }
 

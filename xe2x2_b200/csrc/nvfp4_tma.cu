@@ -92,7 +92,7 @@ template <int NT, int SDT>
 __global__ void __maxnreg__(kMaxRegs)
 nvfp4_gemv_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap sc_map,
                       const __grid_constant__ CUtensorMap act_map, const float *__restrict__ global_scale,
-                      void *__restrict__ C, int c_dtype, int M, int N, int stages_total, int act_rows) {
+                      void *__restrict__ C, int c_dtype, int M, int N, int stages_total, int act_rows, int pre) {
     constexpr int NE = 2 * NT * 4;
     constexpr int SB = SDT == W4_E4M3 ? 1 : 2;  // bytes per block scale
     extern __shared__ uint8_t smem_dyn[];
@@ -111,11 +111,26 @@ nvfp4_gemv_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_co
         fence_mbar_init();
     }
     __syncthreads();
+    grid_dep_launch();  // the next decode GEMM may set up while this one runs
     if (warp == W) {  // ---------------- producer ----------------
         if (lane == 0) {
             const uint32_t tx = Lay::W_STAGE + act_rows * KS * 2 + 16 * 32 * SB;
             bool ok = true;
             const int most = (stages_total + W - 1) / W;
+            // pre: codes and block scales of the first ring fill are requested before
+            // the previous kernel on the stream has completed (static weights).
+            const int pf = pre ? (most < S ? most : S) : 0;
+            for (int it = 0; it < pf; ++it)
+                for (int w = 0; w < W; ++w) {
+                    const int sb = w * stages_total / W, se = (w + 1) * stages_total / W;
+                    if (sb + it >= se) continue;
+                    uint8_t *r = base + (size_t)w * L.total;
+                    uint64_t *full = reinterpret_cast<uint64_t *>(r + L.bars) + it;
+                    mbar_arrive_expect_tx(full, tx);
+                    tma_load_2d(r + it * Lay::W_STAGE, &w_map, (sb + it) * (KS / 2), n0, full);
+                    tma_load_2d(r + L.sc + it * L.sc_stage, &sc_map, n0, (sb + it) * (KS / 16), full);
+                }
+            grid_dep_wait();  // activations are the previous kernel's output
             for (int it = 0; it < most && ok; ++it) {
                 const int s = it % S;
                 for (int w = 0; w < W && ok; ++w) {
@@ -123,20 +138,23 @@ nvfp4_gemv_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_co
                     if (sb + it >= se) continue;
                     uint8_t *r = base + (size_t)w * L.total;
                     uint64_t *full = reinterpret_cast<uint64_t *>(r + L.bars) + s;
-                    if (it >= S && !wait_fp4(full + S, (uint32_t)(((it / S) - 1) & 1))) {
-                        ok = false;
-                        break;
-                    }
                     const int st = sb + it;
-                    mbar_arrive_expect_tx(full, tx);
-                    tma_load_2d(r + s * Lay::W_STAGE, &w_map, st * (KS / 2), n0, full);
+                    if (it >= pf) {
+                        if (it >= S && !wait_fp4(full + S, (uint32_t)(((it / S) - 1) & 1))) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(full, tx);
+                        tma_load_2d(r + s * Lay::W_STAGE, &w_map, st * (KS / 2), n0, full);
+                        tma_load_2d(r + L.sc + s * L.sc_stage, &sc_map, n0, st * (KS / 16), full);
+                    }
                     tma_load_3d(r + L.act + s * L.act_stage, &act_map, 0, tok0, st * (KS / 64), full);
-                    tma_load_2d(r + L.sc + s * L.sc_stage, &sc_map, n0, st * (KS / 16), full);
                 }
             }
         }
         return;
     }
+    grid_dep_wait();  // nothing below touches global memory before the previous kernel completed
 
     // ---------------- consumers ----------------
     uint8_t *ring = base + (size_t)warp * L.total;
@@ -290,8 +308,9 @@ static int launch(const uint16_t *a, const uint8_t *w, const void *scale, const 
     const size_t smem = 1024 + (size_t)W * lay.total;
     if (smem > 220 * 1024) return -1;
     dim3 grid(mblocks, nchunk), block(32 * (W + 1));
-    kern<<<grid, block, smem, st>>>(w_map, sc_map, act_map, global_scale, c, c_dtype, M, N, stages_total, act_rows);
-    W4_LAUNCH_CHECK();
+    const int pre = launch_overlap() == W4_OVERLAP_STATIC_WEIGHTS;
+    W4_CUDA_TRY(launch_decode(kern, grid, block, smem, st, w_map, sc_map, act_map, global_scale, c, c_dtype, M, N,
+                              stages_total, act_rows, pre));
     return W4_OK;
 }
 

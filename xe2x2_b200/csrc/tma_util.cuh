@@ -8,6 +8,9 @@
 #include <stdint.h>
 
 #include <mutex>
+#include <utility>
+
+#include "w4_common.cuh"
 
 namespace w4 {
 
@@ -67,6 +70,11 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
         : "memory");
 }
+// Programmatic dependent launch: let the next grid on the stream start its
+// prologue now / wait until every grid this one depends on has completed and
+// its memory is visible (no-ops when the launch carries no such dependency).
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -85,6 +93,25 @@ inline PFN_cuTensorMapEncodeTiled encode_fn() {
             fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(p);
     }
     return fn;
+}
+
+// Launch of a decode kernel, with programmatic stream serialisation unless the
+// overlap mode is W4_OVERLAP_OFF: the kernel may then start while the previous
+// kernel on the stream drains, and orders itself behind it with grid_dep_wait().
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_decode(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                 Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = launch_overlap() == W4_OVERLAP_OFF ? 0 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 inline bool make_map_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *ptr, uint64_t d0, uint64_t d1,

@@ -3,6 +3,7 @@
 // Every entry point validates its arguments on the host, then enqueues on the
 // caller's stream.  Nothing here allocates: scratch comes from the caller's
 // workspace, sized by the *_workspace_bytes() functions.
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -38,6 +39,9 @@ int num_sms() {
     return cache[dev];
 }
 
+static std::atomic<int> g_overlap{W4_OVERLAP_DEPENDENT};
+int launch_overlap() { return g_overlap.load(std::memory_order_relaxed); }
+
 int nvfp4_kn_to_nk(const uint8_t *in, int K, int N, uint8_t *out, cudaStream_t st);
 
 }  // namespace w4
@@ -50,6 +54,15 @@ static inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 extern "C" {
 
 int w4_abi_version(void) { return W4_ABI_VERSION; }
+
+int w4_set_launch_overlap(int mode) {
+    W4_REQUIRE(mode == W4_OVERLAP_OFF || mode == W4_OVERLAP_DEPENDENT || mode == W4_OVERLAP_STATIC_WEIGHTS,
+               W4_ERR_INVALID, "overlap mode %d is not one of W4_OVERLAP_*", mode);
+    w4::g_overlap.store(mode, std::memory_order_relaxed);
+    return W4_OK;
+}
+
+int w4_get_launch_overlap(void) { return w4::launch_overlap(); }
 
 const char *w4_status_string(int status) {
     switch (status) {

@@ -54,6 +54,7 @@ const char *last_error();
 inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 int num_sms();
+int launch_overlap();  // the process-wide W4_OVERLAP_* mode (w4_set_launch_overlap)
 
 // ---- device helpers ----
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
