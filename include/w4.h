@@ -225,6 +225,35 @@ int w4_nvfp4_repack_kn_to_nk(const uint8_t *w_kn, int K, int N, uint8_t *w_nk, v
 size_t w4_nvfp4_scale_atoms_bytes(int N, int K);
 int w4_nvfp4_repack_scales(const uint8_t *scale, int K, int N, uint8_t *atoms, void *stream);
 
+/* Producer fusion (RMSNorm -> NVFP4 activations) and the GEMM that consumes it.
+ *
+ * w4_rmsnorm_quant_nvfp4: one pass per row of x f16/bf16 [M,K] (x_dtype):
+ *   inv = 1 / sqrt(sum_k x^2 / K + eps),  y = bf16(x * inv [* gamma])
+ * then y quantised exactly as w4_nvfp4_quant_act does, with the codes written
+ * to codes u8 [rows, K/2] and the block scales to sf_atoms in the 512-byte atom
+ * layout of the block-scaled GEMM, rows = M rounded up to 128 (the padding
+ * rows get zero codes and scales).  gamma: [K] of x_dtype or NULL (none).
+ * Buffer sizes: w4_nvfp4_act_codes_bytes(M, K), w4_nvfp4_scale_atoms_bytes(M, K).
+ * K % 64 == 0.  The normalisation is the reference's contract
+ * (kernels/epilogue_quant/rmsnorm_epilogue.cpp:39-56); the reference follows it
+ * with an s8 cast (w4_rmsnorm_quant_s8) in a second kernel or fused
+ * (:118-151); the fused NVFP4 producer is the next step its K5 summary names
+ * (results/k5/SUMMARY.md:65-80).
+ *
+ * w4_nvfp4_gemm_q: w4_nvfp4_gemm with act_mode W4_ACT_NVFP4 for activations
+ * already quantised (codes + scale atoms as written above, a_global the
+ * tensor scale they were quantised with).  Same weights, outputs and shape
+ * rules (K % 256 == 0, N % 128 == 0, E4M3 or E4M3-atom weight scales);
+ * workspace from w4_nvfp4_gemm_q_workspace_bytes. */
+size_t w4_nvfp4_act_codes_bytes(int M, int K);
+int w4_rmsnorm_quant_nvfp4(const void *x, int x_dtype, const void *gamma, float eps, const float *a_global,
+                           uint8_t *codes, uint8_t *sf_atoms, int M, int K, void *stream);
+size_t w4_nvfp4_gemm_q_workspace_bytes(int M, int N, int K, int scale_dtype, int c_dtype);
+int w4_nvfp4_gemm_q(const uint8_t *a_codes, const uint8_t *a_sf_atoms, const float *a_global, const uint8_t *w,
+                    int layout, const void *scale, int scale_dtype, const float *global_scale, void *c,
+                    int c_dtype, float *row_scale, int M, int N, int K, void *workspace, size_t workspace_bytes,
+                    void *stream);
+
 /* The reference LUT kernel's own contract, same arguments in the same order as
  * launch(q, ad, pd, asd, bsd, cd, rows, cols, dk) of
  * kernels/nvfp4/nibble_lut_sc.cpp:198-201:

@@ -89,6 +89,7 @@ def _declare(L):
         "orc_nvfp4_quant_act": (None, [_P, _I, _I, _F, _P, _P]),
         "orc_nvfp4_act_dequant": (None, [_P, _P, _F, _I, _I, _P]),
         "orc_rmsnorm_quant_s8": (None, [_P, _P, _P, _I, _I, _F]),
+        "orc_rmsnorm_nvfp4": (None, [_P, _P, _I, _I, _F, _F, _P, _P]),
         "orc_rowscale_fp8": (None, [_P, _I, _I, _P, _P]),
         "orc_cosine": (ctypes.c_double, [_P, _P, _Z]),
         "orc_max_abs": (ctypes.c_double, [_P, _P, _Z]),
@@ -325,6 +326,18 @@ def rmsnorm_quant_s8(x, eps: float = 1e-6):
     s = np.empty(m, np.float32)
     lib().orc_rmsnorm_quant_s8(_ptr(x), _ptr(q), _ptr(s), m, k, eps)
     return q, s
+
+
+def rmsnorm_nvfp4(x, gamma, eps: float, global_dec: float):
+    """-> (codes u8 [M, K/2], sf u8 [M, K/16]) of the fused RMSNorm -> NVFP4 producer."""
+    x = _c(x, np.float32)
+    m, k = x.shape
+    g = None if gamma is None else _c(gamma, np.float32)
+    codes = np.empty((m, k // 2), np.uint8)
+    sf = np.empty((m, k // 16), np.uint8)
+    lib().orc_rmsnorm_nvfp4(_ptr(x), None if g is None else _ptr(g), m, k, float(eps), float(global_dec),
+                            _ptr(codes), _ptr(sf))
+    return codes, sf
 
 
 def rowscale_fp8(y):

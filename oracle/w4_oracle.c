@@ -477,6 +477,29 @@ void orc_rmsnorm_quant_s8(const float *x, int8_t *q, float *scale, int m, int k,
     }
 }
 
+/* RMSNorm -> NVFP4 activations (the fused producer of the NVFP4 GEMM): the
+ * normalisation of rmsnorm_epilogue.cpp:49-56 (sequential fp32 sum of squares,
+ * inv = 1 / sqrt(ss / k + eps)), y = bf16(x * inv [* gamma]) rounded once, then
+ * orc_nvfp4_quant_act on the row.  codes [m, k/2], sf [m, k/16] row-major. */
+void orc_rmsnorm_nvfp4(const float *x, const float *gamma, int m, int k, float eps, float global_dec,
+                       uint8_t *codes, uint8_t *sf) {
+    float *y = (float *)malloc((size_t)k * sizeof(float));
+    if (!y) return;
+    for (int i = 0; i < m; ++i) {
+        const float *row = x + (size_t)i * k;
+        float ss = 0.f;
+        for (int j = 0; j < k; ++j) ss += row[j] * row[j];
+        const float inv = 1.f / sqrtf(ss / (float)k + eps);
+        for (int j = 0; j < k; ++j) {
+            float v = row[j] * inv;
+            if (gamma) v = v * gamma[j];
+            y[j] = orc_bf16_to_f32(orc_f32_to_bf16(v));
+        }
+        orc_nvfp4_quant_act(y, 1, k, global_dec, codes + (size_t)i * (k / 2), sf + (size_t)i * (k / 16));
+    }
+    free(y);
+}
+
 /* fp8-E4M3 per-row cast: the same absmax contract as rmsnorm_epilogue.cpp:56-69 with
  * qmax 448 (E4M3 max finite): s = amax/448 (1 if 0); q = e4m3_rne_satfinite(y / s). */
 void orc_rowscale_fp8(const float *y, int M, int N, uint8_t *q, float *scale) {

@@ -94,6 +94,8 @@ void orc_nvfp4_act_dequant(const uint8_t *codes, const uint8_t *sf, float global
 
 /* ---- epilogue quant ---- */
 void orc_rmsnorm_quant_s8(const float *x, int8_t *q, float *scale, int m, int k, float eps);
+void orc_rmsnorm_nvfp4(const float *x, const float *gamma, int m, int k, float eps, float global_dec,
+                       uint8_t *codes, uint8_t *sf);
 void orc_rowscale_fp8(const float *y, int M, int N, uint8_t *q, float *scale);
 
 /* ---- metrics (dpas_s4_gptq_sc.cpp:312-327) ---- */

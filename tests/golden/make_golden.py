@@ -10,6 +10,12 @@ records, for seeded random packed words, the outputs of the reference's
 checkpoint unpackers unpack_i32_nibbles_first (qweight, :69-73) and
 unpack_i32_nibbles_last (qzeros, :61-66), plus the reference's s4 view u - 8
 (:114).  tests/test_oracle_golden.py replays them against the C oracle.
+
+It also writes a tiny act_order GPTQ checkpoint with this repository's
+safetensors writer (gptq_tiny.safetensors, seeded values) and records what the
+reference's own reader load_meta / read_tensor (:32-58) returns for every
+tensor in it (gptq_tiny_ref.npz); tests/test_checkpoint.py reads the same file
+with xe2x2_b200.checkpoint and compares.
 """
 from __future__ import annotations
 
@@ -39,6 +45,32 @@ def main(ref_root: str) -> None:
     here = os.path.dirname(os.path.abspath(__file__))
     np.savez_compressed(os.path.join(here, "gptq_unpack.npz"), **out)
     print("wrote", os.path.join(here, "gptq_unpack.npz"), sorted(out))
+
+    path = os.path.join(here, "gptq_tiny.safetensors")
+    write_tiny_checkpoint(path)
+    meta, data0 = mod.load_meta(path)
+    ref = {name: mod.read_tensor(path, data0, info) for name, info in meta.items()}
+    np.savez_compressed(os.path.join(here, "gptq_tiny_ref.npz"), **ref)
+    print("wrote", path, "and gptq_tiny_ref.npz", sorted(ref))
+
+
+def tiny_checkpoint_tensors() -> dict:
+    """One act_order GPTQ layer, K=128, N=64, group 32, asymmetric zeros (seeded)."""
+    rng = np.random.default_rng(20261202)
+    K, N, gs = 128, 64, 32
+    qw = rng.integers(-2**31, 2**31, size=(K // 8, N), dtype=np.int64).astype(np.int32)
+    qz = rng.integers(-2**31, 2**31, size=(K // gs, N // 8), dtype=np.int64).astype(np.int32)
+    sc = (np.abs(rng.normal(0, 0.02, size=(K // gs, N))) + 1e-3).astype(np.float16)
+    g_idx = rng.permutation(np.arange(K, dtype=np.int32) // gs).astype(np.int32)
+    p = "model.layers.0.mlp.down_proj"
+    return {p + ".qweight": qw, p + ".qzeros": qz, p + ".scales": sc, p + ".g_idx": g_idx}
+
+
+def write_tiny_checkpoint(path: str) -> None:
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
+    from xe2x2_b200.checkpoint import save_safetensors
+
+    save_safetensors(path, tiny_checkpoint_tensors(), metadata={"format": "pt"})
 
 
 if __name__ == "__main__":

@@ -55,6 +55,10 @@ _SIGS = {
     "w4_nvfp4_repack_kn_to_nk": (_I, [_P, _I, _I, _P, _P]),
     "w4_nvfp4_scale_atoms_bytes": (_Z, [_I, _I]),
     "w4_nvfp4_repack_scales": (_I, [_P, _I, _I, _P, _P]),
+    "w4_nvfp4_act_codes_bytes": (_Z, [_I, _I]),
+    "w4_rmsnorm_quant_nvfp4": (_I, [_P, _I, _P, _F, _P, _P, _P, _I, _I, _P]),
+    "w4_nvfp4_gemm_q_workspace_bytes": (_Z, [_I, _I, _I, _I, _I]),
+    "w4_nvfp4_gemm_q": (_I, [_P, _P, _P, _P, _I, _P, _I, _P, _P, _I, _P, _I, _I, _I, _P, _Z, _P]),
     "w4_nvfp4_lut_gemm_s8a": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),
     "w4_rmsnorm_quant_s8": (_I, [_P, _P, _P, _I, _I, _F, _P]),
     "w4_rowscale_fp8": (_I, [_P, _I, _P, _P, _I, _I, _P]),

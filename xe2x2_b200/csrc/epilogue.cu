@@ -14,25 +14,6 @@ namespace w4 {
 
 constexpr int kRowThreads = 256;
 
-__device__ __forceinline__ float block_reduce(float v, bool is_max, float *sh) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float u = __shfl_xor_sync(0xffffffffu, v, o);
-        v = is_max ? fmaxf(v, u) : v + u;
-    }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __syncthreads();
-    if (lane == 0) sh[warp] = v;
-    __syncthreads();
-    v = lane < (blockDim.x >> 5) ? sh[lane] : 0.f;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float u = __shfl_xor_sync(0xffffffffu, v, o);
-        v = is_max ? fmaxf(v, u) : v + u;
-    }
-    return v;  // every thread holds the result
-}
-
 __device__ __forceinline__ int8_t quant_s8(float y, float s) {
     float q = rintf(__fdiv_rn(y, s));
     q = fminf(fmaxf(q, -127.f), 127.f);

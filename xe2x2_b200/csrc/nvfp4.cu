@@ -59,6 +59,39 @@ int nvfp4_dequant(const uint8_t *w, int layout, const void *scale, int scale_dty
 // correctly rounded reciprocal per block.  ATOMS: the scales go straight into
 // the 512-byte atom layout of the block-scaled GEMM (rows padded to 128 with
 // zero scales), else row-major [M, K/16].
+// Byte offset of block scale (row m, 16-k block kb) in the row-major [rows, nb]
+// layout, or in the 512-byte atoms of the block-scaled GEMM (128 rows x 4 blocks).
+template <bool ATOMS> __device__ __forceinline__ size_t sf_offset(int m, int kb, int nb) {
+    if constexpr (ATOMS)
+        return ((size_t)(m >> 7) * (nb >> 2) + (kb >> 2)) * 512 + (m & 31) * 16 + ((m >> 5) & 3) * 4 + (kb & 3);
+    else
+        return (size_t)m * nb + kb;
+}
+
+// One 16-value block: the UE4M3 scale byte and the 16 E2M1 codes (8 bytes, low
+// nibble = even k).  v holds values exactly representable in bf16.
+__device__ __forceinline__ uint32_t nvfp4_block(const float (&v)[16], float g, uint2 &codes) {
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    const uint32_t s = f_to_e4m3(__fdiv_rn(amax, __fmul_rn(6.0f, g)));
+    const float sdec = __fmul_rn(e4m3_to_f(s), g);
+    const float inv = sdec != 0.f ? __frcp_rn(sdec) : 0.f;
+    // hardware E2M1 conversion: round to nearest even, saturating at +-6 (the
+    // rounding rule of f_to_e2m1 / the host quantiser)
+    uint32_t packed[2] = {0, 0};
+    if (sdec != 0.f) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t c2 = __nv_cvt_float2_to_fp4x2(make_float2(__fmul_rn(v[2 * i], inv), __fmul_rn(v[2 * i + 1], inv)),
+                                                         __NV_E2M1, cudaRoundNearest);
+            packed[i >> 2] |= (c2 & 0xFFu) << (8 * (i & 3));
+        }
+    }
+    codes = make_uint2(packed[0], packed[1]);
+    return s;
+}
+
 template <bool ATOMS>
 __global__ void nvfp4_quant_act_kernel(const uint16_t *__restrict__ a, int M, int K,
                                        const float *__restrict__ a_global,
@@ -67,9 +100,7 @@ __global__ void nvfp4_quant_act_kernel(const uint16_t *__restrict__ a, int M, in
     const int nb = K / 16;
     if (b >= (long)rows * nb) return;
     const int m = (int)(b / nb), kb = (int)(b % nb);
-    size_t si = (size_t)m * nb + kb;
-    if constexpr (ATOMS)
-        si = ((size_t)(m >> 7) * (nb >> 2) + (kb >> 2)) * 512 + (m & 31) * 16 + ((m >> 5) & 3) * 4 + (kb & 3);
+    const size_t si = sf_offset<ATOMS>(m, kb, nb);
     if (m >= M) {  // padding row of the last tile
         sf[si] = 0;
         return;
@@ -83,27 +114,150 @@ __global__ void nvfp4_quant_act_kernel(const uint16_t *__restrict__ a, int M, in
         v[2 * i] = __uint_as_float(wv[i] << 16);
         v[2 * i + 1] = __uint_as_float(wv[i] & 0xFFFF0000u);
     }
-    float amax = 0.f;
+    uint2 q;
+    sf[si] = (uint8_t)nvfp4_block(v, *a_global, q);
+    *reinterpret_cast<uint2 *>(codes + (size_t)m * (K / 2) + (size_t)kb * 8) = q;
+}
+
+// Fused producer (RMSNorm -> NVFP4 activations, one CTA per row):
+//   inv = 1 / sqrt(sum(x^2) / K + eps)      (fp32 sum, IEEE divide / square root)
+//   y   = bf16(x * inv [* gamma])           (one rounding to bf16 per value)
+//   codes, scales = the 16-block quantisation of y (nvfp4_block), scales in the
+//   atom layout the block-scaled GEMM reads; rows M..rows-1 (the last 128-row
+//   tile's padding) get zero codes and zero scales.
+// The normalisation is the reference's contract (rmsnorm_epilogue.cpp:39-56,
+// without its s8 cast); the quantisation is w4_nvfp4_quant_act's, so the result
+// equals quantising the bf16 RMSNorm output in a second pass.
+// One 16-k block of the producer: y = bf16(x * inv [* gamma]), quantised.
+template <typename T, bool GAMMA>
+__device__ __forceinline__ void rmsnorm_nvfp4_block(const uint32_t (&wv)[8], const T *__restrict__ gamma, int kb,
+                                                    float inv, float g, uint8_t *__restrict__ cr,
+                                                    uint8_t *__restrict__ sf, int row, int nb) {
+    uint32_t gv[8] = {};
+    if constexpr (GAMMA) {
+        const uint4 g0 = ld_nc_v4(gamma + (size_t)kb * 16), g1 = ld_nc_v4(gamma + (size_t)kb * 16 + 8);
+        gv[0] = g0.x, gv[1] = g0.y, gv[2] = g0.z, gv[3] = g0.w;
+        gv[4] = g1.x, gv[5] = g1.y, gv[6] = g1.z, gv[7] = g1.w;
+    }
+    float v[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    const float g = *a_global;
-    const uint32_t s = f_to_e4m3(__fdiv_rn(amax, __fmul_rn(6.0f, g)));
-    const float sdec = __fmul_rn(e4m3_to_f(s), g);
-    const float inv = sdec != 0.f ? __frcp_rn(sdec) : 0.f;
-    sf[si] = (uint8_t)s;
-    // hardware E2M1 conversion: round to nearest even, saturating at +-6 (the
-    // rounding rule of f_to_e2m1 / the host quantiser)
-    uint32_t packed[2] = {0, 0};
-    if (sdec != 0.f) {
+    for (int i = 0; i < 8; ++i) {
+        const float2 f = Conv<T>::to_f2(wv[i]);
+        float y0 = __fmul_rn(f.x, inv), y1 = __fmul_rn(f.y, inv);
+        if constexpr (GAMMA) {
+            const float2 gg = Conv<T>::to_f2(gv[i]);
+            y0 = __fmul_rn(y0, gg.x);
+            y1 = __fmul_rn(y1, gg.y);
+        }
+        v[2 * i] = __bfloat162float(__float2bfloat16_rn(y0));
+        v[2 * i + 1] = __bfloat162float(__float2bfloat16_rn(y1));
+    }
+    uint2 q;
+    sf[sf_offset<true>(row, kb, nb)] = (uint8_t)nvfp4_block(v, g, q);
+    *reinterpret_cast<uint2 *>(cr + (size_t)kb * 8) = q;
+}
+
+// BPT > 0: thread t holds 16-k blocks t, t + blockDim, ... (at most BPT) in
+// registers, so x is read once; BPT == 0 (very wide rows): x is read twice.
+template <typename T, bool GAMMA, int BPT>
+__global__ void __launch_bounds__(256)
+rmsnorm_nvfp4_kernel(const T *__restrict__ x, const T *__restrict__ gamma, float eps,
+                     const float *__restrict__ a_global, uint8_t *__restrict__ codes, uint8_t *__restrict__ sf,
+                     int M, int K) {
+    __shared__ float sh[32];
+    const int row = blockIdx.x, nb = K / 16;
+    uint8_t *cr = codes + (size_t)row * (K / 2);
+    if (row >= M) {
+        for (int kb = threadIdx.x; kb < nb; kb += blockDim.x) {
+            sf[sf_offset<true>(row, kb, nb)] = 0;
+            *reinterpret_cast<uint2 *>(cr + (size_t)kb * 8) = make_uint2(0, 0);
+        }
+        return;
+    }
+    const T *xr = x + (size_t)row * K;
+    float ss = 0.f;
+    uint32_t xw[BPT > 0 ? BPT : 1][8];
+    if constexpr (BPT > 0) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t c2 = __nv_cvt_float2_to_fp4x2(make_float2(__fmul_rn(v[2 * i], inv), __fmul_rn(v[2 * i + 1], inv)),
-                                                         __NV_E2M1, cudaRoundNearest);
-            packed[i >> 2] |= (c2 & 0xFFu) << (8 * (i & 3));
+        for (int i = 0; i < BPT; ++i) {
+            const int kb = threadIdx.x + i * blockDim.x;
+            uint4 u0 = make_uint4(0, 0, 0, 0), u1 = u0;
+            if (kb < nb) {
+                u0 = ld_nc_v4(xr + (size_t)kb * 16);
+                u1 = ld_nc_v4(xr + (size_t)kb * 16 + 8);
+            }
+            xw[i][0] = u0.x, xw[i][1] = u0.y, xw[i][2] = u0.z, xw[i][3] = u0.w;
+            xw[i][4] = u1.x, xw[i][5] = u1.y, xw[i][6] = u1.z, xw[i][7] = u1.w;
+        }
+#pragma unroll
+        for (int i = 0; i < BPT; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float2 f = Conv<T>::to_f2(xw[i][j]);
+                ss += f.x * f.x + f.y * f.y;
+            }
+    } else {
+        for (int v = threadIdx.x; v < K / 8; v += blockDim.x) {
+            const uint4 u = ld_nc_v4(xr + (size_t)v * 8);
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = Conv<T>::to_f2(w[i]);
+                ss += f.x * f.x + f.y * f.y;
+            }
         }
     }
-    *reinterpret_cast<uint2 *>(codes + (size_t)m * (K / 2) + (size_t)kb * 8) =
-        make_uint2(packed[0], packed[1]);
+    ss = block_reduce(ss, false, sh);
+    const float inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), eps)));
+    const float g = *a_global;
+    if constexpr (BPT > 0) {
+#pragma unroll
+        for (int i = 0; i < BPT; ++i) {
+            const int kb = threadIdx.x + i * blockDim.x;
+            if (kb < nb) rmsnorm_nvfp4_block<T, GAMMA>(xw[i], gamma, kb, inv, g, cr, sf, row, nb);
+        }
+    } else {
+        for (int kb = threadIdx.x; kb < nb; kb += blockDim.x) {
+            const uint4 u0 = ld_nc_v4(xr + (size_t)kb * 16), u1 = ld_nc_v4(xr + (size_t)kb * 16 + 8);
+            const uint32_t wv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+            rmsnorm_nvfp4_block<T, GAMMA>(wv, gamma, kb, inv, g, cr, sf, row, nb);
+        }
+    }
+}
+
+template <typename T, bool GAMMA>
+static void launch_rmsnorm_nvfp4(const T *x, const T *gamma, float eps, const float *a_global, uint8_t *codes,
+                                 uint8_t *sf_atoms, int M, int K, cudaStream_t st) {
+    const int rows = (M + 127) / 128 * 128, nb = K / 16;
+    if (nb <= 128 * 4)
+        rmsnorm_nvfp4_kernel<T, GAMMA, 4><<<rows, 128, 0, st>>>(x, gamma, eps, a_global, codes, sf_atoms, M, K);
+    else if (nb <= 256 * 8)
+        rmsnorm_nvfp4_kernel<T, GAMMA, 8><<<rows, 256, 0, st>>>(x, gamma, eps, a_global, codes, sf_atoms, M, K);
+    else
+        rmsnorm_nvfp4_kernel<T, GAMMA, 0><<<rows, 256, 0, st>>>(x, gamma, eps, a_global, codes, sf_atoms, M, K);
+}
+
+int rmsnorm_nvfp4(const void *x, int x_dtype, const void *gamma, float eps, const float *a_global, uint8_t *codes,
+                  uint8_t *sf_atoms, int M, int K, cudaStream_t st) {
+    if (x_dtype == W4_BF16) {
+        using T = __nv_bfloat16;
+        if (gamma)
+            launch_rmsnorm_nvfp4<T, true>(static_cast<const T *>(x), static_cast<const T *>(gamma), eps, a_global,
+                                          codes, sf_atoms, M, K, st);
+        else
+            launch_rmsnorm_nvfp4<T, false>(static_cast<const T *>(x), nullptr, eps, a_global, codes, sf_atoms, M,
+                                           K, st);
+    } else {
+        using T = __half;
+        if (gamma)
+            launch_rmsnorm_nvfp4<T, true>(static_cast<const T *>(x), static_cast<const T *>(gamma), eps, a_global,
+                                          codes, sf_atoms, M, K, st);
+        else
+            launch_rmsnorm_nvfp4<T, false>(static_cast<const T *>(x), nullptr, eps, a_global, codes, sf_atoms, M,
+                                           K, st);
+    }
+    W4_LAUNCH_CHECK();
+    return W4_OK;
 }
 
 int nvfp4_quant_act(const uint16_t *a, int M, int K, const float *a_global, uint8_t *codes,

@@ -523,25 +523,20 @@ size_t nvfp4_prefill_workspace(int M, int N, int K) {
     return align256(mp * K / 2) + align256(mp * (K / 16)) + align256(np * (K / 16));
 }
 
-// A bf16 [M,K] -> NVFP4 codes + scale atoms in the workspace, weight scales ->
-// atoms, then the block-scaled GEMM.  -1: shape not handled (caller falls back).
-int nvfp4_prefill(const uint16_t *a, const float *a_global, const uint8_t *w_nk, const uint8_t *w_sf,
-                  bool w_sf_atoms, const float *w_global, void *c, int c_dtype, int M, int N, int K,
-                  void *workspace, cudaStream_t st) {
+// The block-scaled GEMM on activations already quantised: codes u8 [rows, K/2]
+// and scale atoms for rows = M rounded up to 128 (padding rows with zero
+// scales); weight scales rearranged into atoms in the workspace unless
+// w_sf_atoms.  -1: shape not handled.
+int nvfp4_prefill_q(const uint8_t *codes, const uint8_t *sfa, const float *a_global, const uint8_t *w_nk,
+                    const uint8_t *w_sf, bool w_sf_atoms, const float *w_global, void *c, int c_dtype, int M, int N,
+                    int K, void *workspace, cudaStream_t st) {
     using namespace fp4pf;
     if (K % BK || N % 128 || c_dtype == W4_E4M3) return -1;
-    char *ws = static_cast<char *>(workspace);
     const size_t mp = (size_t)(M + 127) / 128 * 128;
-    uint8_t *codes = reinterpret_cast<uint8_t *>(ws);  // rows padded to the 128-row tile; the pad
-    ws += align256(mp * K / 2);                         // rows' scales are 0
-    uint8_t *sfa = reinterpret_cast<uint8_t *>(ws);
-    ws += align256(mp * (K / 16));
-    int rc = nvfp4_quant_act_atoms(a, M, K, a_global, codes, sfa, st);
-    if (rc) return rc;
     const uint8_t *sfb = w_sf;
     if (!w_sf_atoms) {
-        uint8_t *t = reinterpret_cast<uint8_t *>(ws);
-        rc = nvfp4_sf_atoms(w_sf, N, K / 16, 1, N, t, st);
+        uint8_t *t = static_cast<uint8_t *>(workspace);
+        const int rc = nvfp4_sf_atoms(w_sf, N, K / 16, 1, N, t, st);
         if (rc) return rc;
         sfb = t;
     }
@@ -560,6 +555,28 @@ int nvfp4_prefill(const uint16_t *a, const float *a_global, const uint8_t *w_nk,
     if (persistent) return launch_persistent(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K, st);
     return wide ? launch<256>(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K, st)
                 : launch<128>(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K, st);
+}
+
+size_t nvfp4_prefill_q_workspace(int N, int K) {
+    const size_t np = (size_t)(N + 127) / 128 * 128;
+    return align256(np * (K / 16));
+}
+
+// A bf16 [M,K] -> NVFP4 codes + scale atoms in the workspace, then nvfp4_prefill_q.
+int nvfp4_prefill(const uint16_t *a, const float *a_global, const uint8_t *w_nk, const uint8_t *w_sf,
+                  bool w_sf_atoms, const float *w_global, void *c, int c_dtype, int M, int N, int K,
+                  void *workspace, cudaStream_t st) {
+    using namespace fp4pf;
+    if (K % BK || N % 128 || c_dtype == W4_E4M3) return -1;
+    char *ws = static_cast<char *>(workspace);
+    const size_t mp = (size_t)(M + 127) / 128 * 128;
+    uint8_t *codes = reinterpret_cast<uint8_t *>(ws);  // rows padded to the 128-row tile; the pad
+    ws += align256(mp * K / 2);                         // rows' scales are 0
+    uint8_t *sfa = reinterpret_cast<uint8_t *>(ws);
+    ws += align256(mp * (K / 16));
+    const int rc = nvfp4_quant_act_atoms(a, M, K, a_global, codes, sfa, st);
+    if (rc) return rc;
+    return nvfp4_prefill_q(codes, sfa, a_global, w_nk, w_sf, w_sf_atoms, w_global, c, c_dtype, M, N, K, ws, st);
 }
 
 int take_fp4_prefill_wait_status() {

@@ -291,6 +291,73 @@ int w4_nvfp4_gemm(const void *a, const uint8_t *w, int layout, const void *scale
                           global_scale, c, c_dtype, M, N, K, st);
 }
 
+size_t w4_nvfp4_act_codes_bytes(int M, int K) {
+    if (M <= 0 || K <= 0 || K % 64) return 0;
+    return (size_t)(M + 127) / 128 * 128 * (size_t)(K / 2);
+}
+
+int w4_rmsnorm_quant_nvfp4(const void *x, int x_dtype, const void *gamma, float eps, const float *a_global,
+                           uint8_t *codes, uint8_t *sf_atoms, int M, int K, void *stream) {
+    w4::set_error("");
+    W4_REQUIRE(x && a_global && codes && sf_atoms, W4_ERR_INVALID, "null pointer argument");
+    W4_REQUIRE(x_dtype == W4_F16 || x_dtype == W4_BF16, W4_ERR_INVALID, "x_dtype must be f16 or bf16");
+    W4_REQUIRE(M >= 1 && K > 0 && K % 64 == 0, W4_ERR_INVALID, "M=%d K=%d (K %% 64 == 0)", M, K);
+    W4_REQUIRE(eps >= 0.f, W4_ERR_INVALID, "eps must be >= 0");
+    W4_REQUIRE(aligned(x, 16) && (!gamma || aligned(gamma, 16)) && aligned(codes, 16), W4_ERR_INVALID,
+               "x, gamma and codes must be 16-byte aligned");
+    return w4::rmsnorm_nvfp4(x, x_dtype, gamma, eps, a_global, codes, sf_atoms, M, K, S(stream));
+}
+
+size_t w4_nvfp4_gemm_q_workspace_bytes(int M, int N, int K, int scale_dtype, int c_dtype) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    size_t ws = scale_dtype == W4_E4M3 ? w4::nvfp4_prefill_q_workspace(N, K) : 0;
+    if (c_dtype == W4_E4M3) ws += align256((size_t)M * N * 4);
+    return ws;
+}
+
+int w4_nvfp4_gemm_q(const uint8_t *a_codes, const uint8_t *a_sf_atoms, const float *a_global, const uint8_t *w,
+                    int layout, const void *scale, int scale_dtype, const float *global_scale, void *c,
+                    int c_dtype, float *row_scale, int M, int N, int K, void *workspace, size_t workspace_bytes,
+                    void *stream) {
+    w4::set_error("");
+    int rc = check_nvfp4_w(w, layout, scale, scale_dtype, global_scale, K, N);
+    if (rc) return rc;
+    W4_REQUIRE(a_codes && a_sf_atoms && a_global && c, W4_ERR_INVALID,
+               "a_codes, a_sf_atoms, a_global and c are required");
+    W4_REQUIRE(M >= 1, W4_ERR_INVALID, "M=%d must be >= 1", M);
+    W4_REQUIRE(c_dtype == W4_F16 || c_dtype == W4_BF16 || c_dtype == W4_F32 || c_dtype == W4_E4M3,
+               W4_ERR_INVALID, "c_dtype must be f16, bf16, f32 or e4m3");
+    W4_REQUIRE(c_dtype != W4_E4M3 || row_scale, W4_ERR_INVALID, "e4m3 output needs row_scale");
+    W4_REQUIRE(layout == W4_NVFP4_NK, W4_ERR_UNSUPPORTED, "the GEMM reads the K-contiguous [N, K/2] layout");
+    W4_REQUIRE(scale_dtype == W4_E4M3 || scale_dtype == W4_E4M3_ATOMS, W4_ERR_UNSUPPORTED,
+               "NVFP4 activations need E4M3 weight block scales (the MMA scales are UE4M3)");
+    W4_REQUIRE(K % 256 == 0 && N % 128 == 0, W4_ERR_UNSUPPORTED,
+               "NVFP4 activations need K %% 256 == 0 and N %% 128 == 0 (K=%d N=%d)", K, N);
+    W4_REQUIRE(aligned(a_codes, 16) && aligned(w, 16) && aligned(a_sf_atoms, 16) &&
+                   (scale_dtype != W4_E4M3_ATOMS || aligned(scale, 16)),
+               W4_ERR_INVALID, "a_codes, a_sf_atoms, w and scale atoms must be 16-byte aligned");
+    const size_t need = w4_nvfp4_gemm_q_workspace_bytes(M, N, K, scale_dtype, c_dtype);
+    W4_REQUIRE(workspace_bytes >= need && (need == 0 || workspace), W4_ERR_INVALID,
+               "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+    cudaStream_t st = S(stream);
+    char *wsb = static_cast<char *>(workspace);
+    void *out = c;
+    int odt = c_dtype;
+    if (c_dtype == W4_E4M3) {
+        out = wsb;
+        odt = W4_F32;
+        wsb += align256((size_t)M * N * 4);
+    }
+    rc = w4::nvfp4_prefill_q(a_codes, a_sf_atoms, a_global, w, static_cast<const uint8_t *>(scale),
+                             scale_dtype == W4_E4M3_ATOMS, global_scale, out, odt, M, N, K, wsb, st);
+    if (rc < 0) {
+        w4::set_error("NVFP4-activation GEMM: tensor maps could not be encoded for this shape");
+        return W4_ERR_UNSUPPORTED;
+    }
+    if (rc || c_dtype != W4_E4M3) return rc;
+    return w4::rowscale_fp8(out, W4_F32, static_cast<uint8_t *>(c), row_scale, M, N, st);
+}
+
 int w4_nvfp4_repack_kn_to_nk(const uint8_t *w_kn, int K, int N, uint8_t *w_nk, void *stream) {
     w4::set_error("");
     W4_REQUIRE(w_kn && w_nk && w_kn != w_nk, W4_ERR_INVALID, "distinct w_kn and w_nk are required");

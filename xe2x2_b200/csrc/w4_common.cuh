@@ -131,14 +131,41 @@ template <typename T> struct Conv;
 template <> struct Conv<__half> {
     static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
     static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+    // a packed pair (low half first) -> floats
+    static __device__ __forceinline__ float2 to_f2(uint32_t w) {
+        return __half22float2(*reinterpret_cast<const __half2 *>(&w));
+    }
 };
 template <> struct Conv<__nv_bfloat16> {
     static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
     static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+    static __device__ __forceinline__ float2 to_f2(uint32_t w) {
+        return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+    }
 };
 
 __device__ __forceinline__ float f16_bits_to_f(uint16_t b) {
     return __half2float(__ushort_as_half(b));
+}
+
+// Sum (or max) of v over the CTA, returned to every thread; sh holds 32 floats.
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float *sh) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float u = __shfl_xor_sync(0xffffffffu, v, o);
+        v = is_max ? fmaxf(v, u) : v + u;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) sh[warp] = v;
+    __syncthreads();
+    v = lane < (blockDim.x >> 5) ? sh[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float u = __shfl_xor_sync(0xffffffffu, v, o);
+        v = is_max ? fmaxf(v, u) : v + u;
+    }
+    return v;  // every thread holds the result
 }
 
 // e4m3fn -> f32 (exact; 0x7F/0xFF decode to NaN).

@@ -58,6 +58,14 @@ int nvfp4_gemv(const uint16_t *a, const uint8_t *w, int layout, const void *scal
 // epilogue.cu
 int rmsnorm_quant_s8(const uint16_t *x, int8_t *q, float *scale, int M, int K, float eps,
                      cudaStream_t st);
+// RMSNorm -> NVFP4 codes [rows, K/2] + scale atoms, rows = M rounded up to 128 (nvfp4.cu).
+int rmsnorm_nvfp4(const void *x, int x_dtype, const void *gamma, float eps, const float *a_global, uint8_t *codes,
+                  uint8_t *sf_atoms, int M, int K, cudaStream_t st);
+// The block-scaled GEMM from quantised activations (nvfp4_prefill.cu).
+int nvfp4_prefill_q(const uint8_t *codes, const uint8_t *sfa, const float *a_global, const uint8_t *w_nk,
+                    const uint8_t *w_sf, bool w_sf_atoms, const float *w_global, void *c, int c_dtype, int M, int N,
+                    int K, void *workspace, cudaStream_t st);
+size_t nvfp4_prefill_q_workspace(int N, int K);
 int rowscale_fp8(const void *y, int y_dtype, uint8_t *q, float *row_scale, int M, int N,
                  cudaStream_t st);
 

@@ -202,6 +202,58 @@ def nvfp4_quant_act(a, a_global):
     return codes, sf
 
 
+class NVFP4Activations:
+    """Activations already quantised to NVFP4 for the block-scaled GEMM: codes u8
+    [rows, K/2] and UE4M3 scale atoms for rows = M rounded up to 128, with the
+    tensor scale ``a_global`` they were quantised with."""
+
+    def __init__(self, codes, sf_atoms, a_global, M, K):
+        self.codes, self.sf_atoms, self.a_global, self.M, self.K = codes, sf_atoms, a_global, M, K
+
+
+def rmsnorm_quant_nvfp4(x, a_global, gamma=None, eps: float = 1e-6):
+    """Fused producer: RMSNorm of x (f16 / bf16 [M, K]) -> NVFP4Activations
+    (y = bf16(x * inv [* gamma]) quantised as nvfp4_quant_act does)."""
+    _need_cuda(x, a_global, gamma)
+    M, K = x.shape
+    dt = {torch.float16: L.W4_F16, torch.bfloat16: L.W4_BF16}.get(x.dtype)
+    if dt is None:
+        raise ValueError("x must be f16 or bf16")
+    if gamma is not None and (gamma.dtype != x.dtype or gamma.shape != (K,)):
+        raise ValueError(f"gamma must be {x.dtype} [{K}]")
+    lib = L.lib()
+    codes = torch.empty(lib.w4_nvfp4_act_codes_bytes(M, K), dtype=torch.uint8, device=x.device)
+    atoms = torch.empty(lib.w4_nvfp4_scale_atoms_bytes(M, K), dtype=torch.uint8, device=x.device)
+    if codes.numel() == 0:
+        raise ValueError(f"K={K} must be a positive multiple of 64")
+    L.call("w4_rmsnorm_quant_nvfp4", _p(_contig(x, "x")), dt, None if gamma is None else _p(_contig(gamma, "gamma")),
+           float(eps), _p(a_global), _p(codes), _p(atoms), M, K, _stream(x.device))
+    return NVFP4Activations(codes.view(-1, K // 2), atoms, a_global, M, K)
+
+
+def nvfp4_gemm_q(act, w, scale, global_scale, out_dtype=torch.bfloat16):
+    """The block-scaled NVFP4 GEMM on NVFP4Activations (see rmsnorm_quant_nvfp4)."""
+    _need_cuda(act.codes, w, scale, global_scale)
+    M, K, N = act.M, act.K, w.shape[1]
+    layout = _layout_of(w, K, N)
+    if layout != L.W4_NVFP4_NK:
+        raise ValueError("w must be the [K/2, N] view of [N, K/2] memory (stride(0) == 1)")
+    if scale.dtype not in (torch.float8_e4m3fn, torch.uint8):
+        raise ValueError("NVFP4 activations need E4M3 weight block scales")
+    atoms = _scale_atoms(scale)
+    cdt = {torch.float16: L.W4_F16, torch.bfloat16: L.W4_BF16, torch.float32: L.W4_F32,
+           torch.float8_e4m3fn: L.W4_E4M3}[out_dtype]
+    c = torch.empty((M, N), dtype=out_dtype, device=w.device)
+    rs = torch.empty(M, dtype=torch.float32, device=w.device) if cdt == L.W4_E4M3 else None
+    lib = L.lib()
+    need = lib.w4_nvfp4_gemm_q_workspace_bytes(M, N, K, L.W4_E4M3_ATOMS, cdt)
+    ws, wsb = _WS.get(w.device, need)
+    L.call("w4_nvfp4_gemm_q", _p(act.codes), _p(act.sf_atoms), _p(act.a_global), _p(w), L.W4_NVFP4_NK,
+           _p(atoms), L.W4_E4M3_ATOMS, _p(global_scale), _p(c), cdt, None if rs is None else _p(rs), M, N, K,
+           None if ws is None else _p(ws), wsb, _stream(w.device))
+    return (c, rs) if rs is not None else c
+
+
 # id(scale tensor) -> (weak reference, tensor version, rearranged atoms); an entry
 # goes away with its tensor (tensors compare elementwise, so they cannot be
 # dictionary keys themselves).
@@ -256,6 +308,28 @@ def nvfp4_gemm(x, w, scale, global_scale=None, out_dtype=torch.bfloat16, act_mod
            _p(global_scale), act_mode, _p(a_global), _p(c), _DT[out_dtype], _p(rs), M, N, K, _p(ws), wsb,
            _stream(x.device))
     return (c, rs) if rs is not None else c
+
+
+class NVFP4Linear:
+    """An NVFP4 linear layer held in HBM: codes u8 [K/2, N] (the [N, K/2] K-contiguous
+    memory of a ModelOpt checkpoint seen through its transpose), E4M3 block scales
+    [K/16, N], tensor scale f32 [1] and, optionally, the activation tensor scale
+    ``input_scale``.  ``act_mode`` W4A16 keeps activations in bf16; W4_ACT_NVFP4
+    quantises them with ``input_scale`` and runs the block-scaled FP4 tensor-core GEMM
+    (needs ``input_scale``)."""
+
+    def __init__(self, w, scale, global_scale, input_scale=None, act_mode=None):
+        self.w, self.scale, self.global_scale, self.input_scale = w, scale, global_scale, input_scale
+        self.K, self.N = w.shape[0] * 2, w.shape[1]
+        self.act_mode = L.W4_ACT_W4A16 if act_mode is None else act_mode
+        if self.act_mode == L.W4_ACT_NVFP4 and input_scale is None:
+            raise ValueError("NVFP4 activations need the layer's input_scale")
+
+    def __call__(self, x, out_dtype=torch.bfloat16):
+        if self.act_mode == L.W4_ACT_NVFP4:
+            return nvfp4_gemm(x, self.w, self.scale, self.global_scale, out_dtype, L.W4_ACT_NVFP4,
+                              self.input_scale)
+        return nvfp4_gemm(x, self.w, self.scale, self.global_scale, out_dtype)
 
 
 def nvfp4_gemm_w4a16(x, w, bias, scale, gs):
