@@ -476,8 +476,20 @@ def run_tp(args) -> None:
                     comm.allreduce_(outs[M]["o"])
                     comm.allreduce_(outs[M]["down"])
         torch.cuda.current_stream().wait_stream(cap)
+        # decode sizes at TP > 1: the same layer with the row-parallel GEMMs reducing in
+        # their own epilogue (the default is GEMM + one-shot all-reduce)
+        gu = None
+        if world > 1 and M <= 16:
+            comm.set_fused_epilogue(True)
+            gu = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(cap):
+                with torch.cuda.graph(gu, stream=cap):
+                    for r in range(R):
+                        sets[r].step(xs[M], outs[M])
+            torch.cuda.current_stream().wait_stream(cap)
+            comm.set_fused_epilogue(False)
         res = []
-        for g in (gm, ga):
+        for g in (gm, ga) + ((gu,) if gu is not None else ()):
             for _ in range(3):
                 g.replay()
             barrier()
@@ -490,7 +502,9 @@ def run_tp(args) -> None:
             trace(f"M={M}: {res[-1]:.2f} us")
         per_m[str(M)] = {"layer_us": round(res[0], 2), "allreduce_us": round(res[1], 2),
                          "TFLOP/s": round(sets[0].flops(M) / res[0] / 1e6, 2)}
-        del gm, ga, g  # graphs holding NCCL work must be gone before the communicator is
+        if gu is not None:
+            per_m[str(M)]["layer_fused_epilogue_us"] = round(res[2], 2)
+        del gm, ga, gu, g  # graphs holding NCCL work must be gone before the communicator is
     graphs.clear()
     torch.cuda.synchronize()
     comm.close()

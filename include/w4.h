@@ -323,6 +323,16 @@ int w4_tp_allreduce(w4_tp_comm *comm, void *buf, size_t count, int dtype, void *
  * returned; an aborted communicator refuses further calls. */
 int w4_tp_wait(w4_tp_comm *comm, void *stream, int timeout_ms);
 
+/* on = 1: row-parallel decode layers (M <= 16, no act_order permutation, peer
+ * memory mapped between the ranks) run one fused kernel: each CTA pushes its
+ * fp32 partial tile to every rank over NVLink, waits (bounded) for the same
+ * tile of every other rank and stores the rank-ordered sum, with no separate
+ * all-reduce launch.  on = 0 (the default): GEMM + w4_tp_allreduce, which
+ * measures faster on B200 pairs so far.  Every rank must choose the same.  The
+ * reference has no fused form; its TP step is a bare all-reduce
+ * (parallel/tp2/bench_xccl_p2p0.py:235-251). */
+int w4_tp_set_fused_epilogue(w4_tp_comm *comm, int on);
+
 size_t w4_tp_linear_workspace_bytes(int mode, int M, int N, int K, int group_size, int has_perm,
                                     int c_dtype);
 

@@ -109,6 +109,95 @@ def _case_layers(rank, world):
         comm.close()
 
 
+def _case_fused_row_parallel(rank, world):
+    """Decode row-parallel layers reducing in the GEMV epilogue over peer memory
+    (w4_tp_set_fused_epilogue): the same bits as GEMM + all-reduce for f32 outputs, the same bits on every rank,
+    correct under CUDA-graph replay, close to the unsharded GEMM."""
+    import torch.distributed as dist
+
+    from xe2x2_b200 import _lib as L, ops, synth, tp
+
+    dev = torch.device("cuda", rank)
+    comm = tp.TPComm(rank, world, timeout_ms=60000, device=dev)
+    try:
+        gs = 128
+        for K, N in ((2048, 5120), (4096, 1024)):
+            qw, qz, sc, _ = synth.gptq_weights(K, N, gs, asym=True, seed=K + N, device=dev)
+            lay = tp.TPLinear(comm, "row", *tp.shard_rows(qw, qz, sc, rank, world, gs), group_size=gs)
+            for M in (1, 4, 9, 16):
+                a = synth.activations(M, K, torch.bfloat16, seed=M, device=dev)
+                xs = a[:, tp.row_input_slice(K, rank, world)].contiguous()
+                full = ops.gptq_gemm(a, qw, qz, sc, gs, 1, out_dtype=torch.float32)
+                comm.set_fused_epilogue(True)
+                f32 = lay(xs, out_dtype=torch.float32)
+                b16 = lay(xs, out_dtype=torch.bfloat16)
+                q8, rs = lay(xs, out_dtype=torch.float8_e4m3fn)
+                comm.set_fused_epilogue(False)
+                u32 = lay(xs, out_dtype=torch.float32)
+                comm.wait()
+                assert torch.equal(f32, u32), (K, N, M)  # rank-ordered fp32 sums either way
+                assert _rel(f32, full) < 1e-5
+                assert _rel(b16, full) < 1e-2
+                assert _rel(q8.float() * rs[:, None], full) < 4e-2
+                got = [torch.empty_like(f32.cpu()) for _ in range(world)]
+                dist.all_gather(got, f32.cpu())
+                assert all(torch.equal(g, got[0]) for g in got)
+        # CUDA-graph replay: the call sequence lives on the device
+        comm.set_fused_epilogue(True)
+        K, N, M = 2048, 5120, 2
+        qw, qz, sc, _ = synth.gptq_weights(K, N, gs, asym=True, seed=77, device=dev)
+        lay = tp.TPLinear(comm, "row", *tp.shard_rows(qw, qz, sc, rank, world, gs), group_size=gs)
+        a = synth.activations(M, K, torch.bfloat16, seed=78, device=dev)
+        xs = a[:, tp.row_input_slice(K, rank, world)].contiguous()
+        want = lay(xs, out_dtype=torch.float32)
+        comm.wait()
+        st = torch.cuda.Stream(dev)
+        st.wait_stream(torch.cuda.current_stream(dev))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(st):
+            lay(xs, out_dtype=torch.float32)
+            torch.cuda.synchronize(dev)
+            with torch.cuda.graph(graph, stream=st):
+                y1 = lay(xs, out_dtype=torch.float32)
+                y2 = lay(xs, out_dtype=torch.float32)
+        torch.cuda.current_stream(dev).wait_stream(st)
+        for _ in range(3):
+            graph.replay()
+            comm.wait()
+            assert torch.equal(y1, want) and torch.equal(y2, want)
+        del graph
+        assert L.lib().w4_check_device_status() == L.W4_OK
+    finally:
+        comm.close()
+
+
+def _case_fused_timeout(rank, world):
+    """Rank 1 skips one fused row-parallel call (it launches nothing): rank 0's CTAs
+    stop waiting after their time limit and the wait reports W4_ERR_TIMEOUT."""
+    import torch.distributed as dist
+
+    from xe2x2_b200 import _lib as L, synth, tp
+
+    dev = torch.device("cuda", rank)
+    comm = tp.TPComm(rank, world, timeout_ms=60000, device=dev)
+    comm.set_fused_epilogue(True)
+    K, N, gs = 1024, 512, 128
+    qw, qz, sc, _ = synth.gptq_weights(K, N, gs, asym=True, seed=5, device=dev)
+    lay = tp.TPLinear(comm, "row", *tp.shard_rows(qw, qz, sc, rank, world, gs), group_size=gs)
+    xs = synth.activations(1, K // world, torch.bfloat16, seed=6, device=dev)
+    lay(xs)
+    comm.wait()
+    dist.barrier()  # every rank is between steps
+    if rank == 0:
+        lay(xs)
+        with pytest.raises(L.W4Error) as ei:
+            comm.wait(timeout_ms=20000)
+        assert ei.value.status == L.W4_ERR_TIMEOUT
+        torch.cuda.synchronize(dev)  # the kernel gave up and left the GPU
+    dist.barrier()
+    comm.abort()
+
+
 def _case_init_timeout(rank, world):
     """Rank 1 never joins: rank 0's communicator init gives up with W4_ERR_TIMEOUT."""
     import ctypes
@@ -200,6 +289,14 @@ def _run(case):
 
 def test_tp_layers_match_unsharded():
     _run("_case_layers")
+
+
+def test_tp_fused_row_parallel_epilogue():
+    _run("_case_fused_row_parallel")
+
+
+def test_tp_fused_epilogue_timeout_when_a_rank_skips():
+    _run("_case_fused_timeout")
 
 
 def test_tp_init_timeout_when_a_rank_never_joins():

@@ -68,6 +68,7 @@ _SIGS = {
     "w4_tp_comm_abort": (_I, [_P]),
     "w4_tp_allreduce": (_I, [_P, _P, _Z, _I, _P]),
     "w4_tp_wait": (_I, [_P, _P, _I]),
+    "w4_tp_set_fused_epilogue": (_I, [_P, _I]),
     "w4_tp_linear_workspace_bytes": (_Z, [_I, _I, _I, _I, _I, _I, _I]),
     "w4_tp_linear": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _P, _Z, _P]),
 }

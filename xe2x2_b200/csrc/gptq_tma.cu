@@ -26,6 +26,18 @@
 namespace w4 {
 
 static __device__ unsigned int g_wait_timeout;  // a bounded wait expired (sticky until read)
+static __device__ unsigned int g_tpf_timeout;   // a peer's tile never arrived in the fused all-reduce
+
+constexpr unsigned long long kPeerWaitNs = 500ull * 1000 * 1000;  // 500 ms
+
+__device__ __forceinline__ void peer_st_release(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t peer_ld_acquire(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 
 constexpr int kTmaStages = 3;   // ring depth per consumer warp
 constexpr int kVps = 2;         // virtual groups per stage
@@ -76,12 +88,22 @@ __device__ __forceinline__ int sigma(int g) { return (g >> 1) | ((g & 1) << 2); 
 // stage's k range, a 3-D box over [K/64][M][64] so each 64-k row segment is one
 // 128-byte-swizzled line); otherwise each lane loads them from global memory one
 // step ahead.
-template <typename T, int NT, int GSTEPS, bool ACT>
+//
+// AR: the row-parallel form.  Instead of storing its tile, a CTA pushes the fp32
+// partial tile into slot [parity][rank] of every rank's peer buffer (NVLink
+// stores), fences at system scope, raises its flag [parity][cta][rank] on every
+// rank, waits (bounded) until the same CTA of every rank has raised its flag
+// here, and stores the sum of the nranks partials in rank order (the same bits
+// on every rank).  The call's sequence number v (parity v & 1) is read from the
+// communicator's control word at the epilogue; the last CTA to finish advances
+// it, so graph replays stay in step.  Launched cooperatively: every CTA of the
+// grid is resident, so each one's peer counterpart runs as well.
+template <typename T, int NT, int GSTEPS, bool ACT, bool AR>
 __global__ void __maxnreg__(kTmaMaxRegs)
 gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_constant__ CUtensorMap sc_map,
                      const __grid_constant__ CUtensorMap zr_map, const __grid_constant__ CUtensorMap act_map,
                      int has_z, const T *__restrict__ A, void *__restrict__ C, int c_dtype, int M, int N, int K,
-                     int zero_offset, int stages_total, int act_rows, int pre) {
+                     int zero_offset, int stages_total, int act_rows, int pre, const __grid_constant__ PeerReduce pr) {
     constexpr int S = kTmaStages;
     constexpr int NE = 2 * NT * 4;
     constexpr int ROWS = 4 * GSTEPS;           // qweight rows per group
@@ -304,21 +326,95 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
 #pragma unroll
             for (int i = 0; i < 4; ++i) red[((mt * NT + nt) * 4 + i) * 32 + lane] = facc[mt][nt][i];
     asm volatile("bar.sync 1, %0;" ::"r"(W * 32) : "memory");  // consumers only
-    for (int idx = threadIdx.x; idx < NE * 32; idx += W * 32) {
-        float val = 0.f;
-        for (int w = 0; w < W; ++w) val += reinterpret_cast<const float *>(base + (size_t)w * L.total + L.red)[idx];
-        const int e = idx >> 5, l = idx & 31;
-        const int mt = e / (NT * 4), nt = (e / 4) % NT, i = e & 3;
-        const int col = n0 + 4 * sigma(l >> 2) + 2 * mt + (i >> 1);
-        const int tok = tok0 + nt * 8 + 2 * (l & 3) + (i & 1);
-        if (tok < M) store_out(C, c_dtype, (size_t)tok * N + col, val);
+    if constexpr (!AR) {
+        for (int idx = threadIdx.x; idx < NE * 32; idx += W * 32) {
+            float val = 0.f;
+            for (int w = 0; w < W; ++w) val += reinterpret_cast<const float *>(base + (size_t)w * L.total + L.red)[idx];
+            const int e = idx >> 5, l = idx & 31;
+            const int mt = e / (NT * 4), nt = (e / 4) % NT, i = e & 3;
+            const int col = n0 + 4 * sigma(l >> 2) + 2 * mt + (i >> 1);
+            const int tok = tok0 + nt * 8 + 2 * (l & 3) + (i & 1);
+            if (tok < M) store_out(C, c_dtype, (size_t)tok * N + col, val);
+        }
+    } else {
+        // tile rows of 32 fp32 outputs, 16-byte vectors to and from the peer slots
+        __shared__ __align__(16) float tile[16][32];
+        __shared__ uint32_t v_sh;
+        const int nr = pr.nranks, me = pr.rank;
+        const int b = blockIdx.y * gridDim.x + blockIdx.x;
+        const int rows = min(8 * NT, M - tok0);
+        uint32_t *ctrl = reinterpret_cast<uint32_t *>(pr.buf[me] + pr.ctrl_off);
+        if (threadIdx.x == 0) v_sh = *reinterpret_cast<volatile uint32_t *>(ctrl) + 1;
+        for (int idx = threadIdx.x; idx < NE * 32; idx += W * 32) {
+            float val = 0.f;
+            for (int w = 0; w < W; ++w) val += reinterpret_cast<const float *>(base + (size_t)w * L.total + L.red)[idx];
+            const int e = idx >> 5, l = idx & 31;
+            const int mt = e / (NT * 4), nt = (e / 4) % NT, i = e & 3;
+            tile[nt * 8 + 2 * (l & 3) + (i & 1)][4 * sigma(l >> 2) + 2 * mt + (i >> 1)] = val;
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(W * 32) : "memory");
+        const uint32_t v = v_sh;
+        const int par = v & 1;
+        const size_t slot0 = pr.data_off + (size_t)(par * nr) * pr.slot_bytes;  // slot [par][0]
+        // 1. push the fp32 partial tile into slot [par][me] of every rank
+        for (int q = threadIdx.x; q < rows * 8; q += W * 32) {
+            const int r = q >> 3, c4 = (q & 7) * 4;
+            const float4 x = *reinterpret_cast<const float4 *>(&tile[r][c4]);
+            const size_t off = slot0 + (size_t)me * pr.slot_bytes + ((size_t)(tok0 + r) * N + n0 + c4) * 4;
+            for (int p = 0; p < nr; ++p) *reinterpret_cast<float4 *>(pr.buf[p] + off) = x;
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(W * 32) : "memory");
+        // 2. flag this CTA's push on every rank (the system fence and release are
+        // cumulative over the CTA barrier above), then wait for every rank's push here
+        if (threadIdx.x < nr) {
+            __threadfence_system();
+            uint32_t *fl = reinterpret_cast<uint32_t *>(pr.buf[threadIdx.x] + pr.flags_off);
+            peer_st_release(fl + ((size_t)par * pr.max_ctas + b) * 8 + me, v);
+            const uint32_t *mine = reinterpret_cast<const uint32_t *>(pr.buf[me] + pr.flags_off) +
+                                   ((size_t)par * pr.max_ctas + b) * 8 + threadIdx.x;
+            if (peer_ld_acquire(mine) != v) {
+                const unsigned long long t0 = global_ns();
+                while (peer_ld_acquire(mine) != v) {
+                    if (global_ns() - t0 > kPeerWaitNs) {
+                        atomicExch(&g_tpf_timeout, 1u);
+                        break;
+                    }
+                }
+            }
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(W * 32) : "memory");
+        // 3. sum the partials in rank order
+        for (int q = threadIdx.x; q < rows * 8; q += W * 32) {
+            const int r = q >> 3, c4 = (q & 7) * 4;
+            const size_t e0 = (size_t)(tok0 + r) * N + n0 + c4;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int p = 0; p < nr; ++p) {
+                const float4 x = __ldcg(reinterpret_cast<const float4 *>(pr.buf[me] + slot0 + (size_t)p * pr.slot_bytes + e0 * 4));
+                acc.x += x.x, acc.y += x.y, acc.z += x.z, acc.w += x.w;
+            }
+            store_out(C, c_dtype, e0, acc.x);
+            store_out(C, c_dtype, e0 + 1, acc.y);
+            store_out(C, c_dtype, e0 + 2, acc.z);
+            store_out(C, c_dtype, e0 + 3, acc.w);
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(W * 32) : "memory");
+        // 4. the last CTA of the grid advances the call sequence
+        if (threadIdx.x == 0) {
+            __threadfence();
+            if (atomicAdd(ctrl + 1, 1u) == gridDim.x * gridDim.y - 1) {
+                *reinterpret_cast<volatile uint32_t *>(ctrl + 1) = 0;
+                __threadfence();
+                *reinterpret_cast<volatile uint32_t *>(ctrl) = v;
+            }
+        }
     }
 }
 
 // ---- host side ----
-template <typename T, int NT, int GSTEPS, bool ACT>
+template <typename T, int NT, int GSTEPS, bool ACT, bool AR>
 static int launch_tma_t(const void *a, const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
-                        void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset, cudaStream_t st) {
+                        void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset, const PeerReduce *pr,
+                        cudaStream_t st) {
     constexpr int NE = 2 * NT * 4;
     constexpr int SSTEPS = kVps * GSTEPS;
     if (gs != 32 * GSTEPS) return -1;  // one real group per virtual group only
@@ -363,7 +459,7 @@ static int launch_tma_t(const void *a, const int32_t *qweight, const int32_t *qz
     } else {
         act_map = sc_map;  // unused
     }
-    auto kern = gptq_gemv_tma_kernel<T, NT, GSTEPS, ACT>;
+    auto kern = gptq_gemv_tma_kernel<T, NT, GSTEPS, ACT, AR>;
     {
         static std::mutex mu;
         static bool set_dev[128] = {};
@@ -379,21 +475,62 @@ static int launch_tma_t(const void *a, const int32_t *qweight, const int32_t *qz
     const size_t smem = 1024 + (size_t)W * per_warp;
     if (smem > 220 * 1024) return -1;
     dim3 grid(mblocks, nchunk), block(32 * (W + 1));
-    const int pre = launch_overlap() == W4_OVERLAP_STATIC_WEIGHTS;
-    W4_CUDA_TRY(launch_decode(kern, grid, block, smem, st, qw_map, sc_map, zr_map, act_map, has_z,
-                              static_cast<const T *>(a), c, c_dtype, M, N, K, zero_offset, stages_total, act_rows,
-                              pre));
+    if constexpr (AR) {
+        // every CTA must be resident at once (each waits for its peers' counterpart)
+        if (ctas > pr->max_ctas || (size_t)M * N * 4 > pr->slot_bytes) return -1;
+        int per_sm = 0;
+        W4_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, (int)block.x, smem));
+        if ((long)per_sm * nsm < ctas) return -1;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = grid;
+        cfg.blockDim = block;
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeCooperative;
+        at[0].val.cooperative = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        W4_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, qw_map, sc_map, zr_map, act_map, has_z, static_cast<const T *>(a),
+                                       c, c_dtype, M, N, K, zero_offset, stages_total, act_rows, 0, *pr));
+    } else {
+        const int pre = launch_overlap() == W4_OVERLAP_STATIC_WEIGHTS;
+        const PeerReduce none{};
+        W4_CUDA_TRY(launch_decode(kern, grid, block, smem, st, qw_map, sc_map, zr_map, act_map, has_z,
+                                  static_cast<const T *>(a), c, c_dtype, M, N, K, zero_offset, stages_total, act_rows,
+                                  pre, none));
+    }
     return W4_OK;
 }
 
-template <typename T, int NT>
+template <typename T, int NT, bool AR>
 static int launch_tma_nt(const void *a, const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
-                         void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset, cudaStream_t st) {
+                         void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset, const PeerReduce *pr,
+                         cudaStream_t st) {
     constexpr bool ACT = NT == 1;  // staged activations fit the ring only for <= 8 tokens
-    if (gs == 128) return launch_tma_t<T, NT, 4, ACT>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
-    if (gs == 64) return launch_tma_t<T, NT, 2, ACT>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
-    if (gs == 32) return launch_tma_t<T, NT, 1, ACT>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    if (gs == 128)
+        return launch_tma_t<T, NT, 4, ACT, AR>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, pr, st);
+    if (gs == 64)
+        return launch_tma_t<T, NT, 2, ACT, AR>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, pr, st);
+    if (gs == 32)
+        return launch_tma_t<T, NT, 1, ACT, AR>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, pr, st);
     return -1;
+}
+
+template <bool AR>
+static int dispatch(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
+                    const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
+                    const PeerReduce *pr, cudaStream_t st) {
+    if (a_dtype == W4_BF16) {
+        if (M <= 8)
+            return launch_tma_nt<__nv_bfloat16, 1, AR>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs,
+                                                       zero_offset, pr, st);
+        return launch_tma_nt<__nv_bfloat16, 2, AR>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset,
+                                                   pr, st);
+    }
+    if (M <= 8)
+        return launch_tma_nt<__half, 1, AR>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, pr, st);
+    return launch_tma_nt<__half, 2, AR>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, pr, st);
 }
 
 // Returns W4_OK, a W4 error, or -1 when the tensor maps cannot be encoded (the
@@ -401,12 +538,26 @@ static int launch_tma_nt(const void *a, const int32_t *qweight, const int32_t *q
 int gptq_gemv_tma(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
                   const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
                   cudaStream_t st) {
-    if (a_dtype == W4_BF16) {
-        if (M <= 8) return launch_tma_nt<__nv_bfloat16, 1>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
-        return launch_tma_nt<__nv_bfloat16, 2>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    return dispatch<false>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, nullptr, st);
+}
+
+int gptq_gemv_tma_ar(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
+                     const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
+                     const PeerReduce &pr, cudaStream_t st) {
+    if (M > 16 || pr.nranks < 2 || pr.nranks > kPeerMaxRanks) return -1;
+    return dispatch<true>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, &pr, st);
+}
+
+int take_tp_fused_wait_status() {
+    unsigned int v = 0;
+    W4_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_tpf_timeout, sizeof(v)));
+    if (v) {
+        const unsigned int zero = 0;
+        W4_CUDA_TRY(cudaMemcpyToSymbol(g_tpf_timeout, &zero, sizeof(zero)));
+        set_error("a peer's tile never arrived in the fused row-parallel all-reduce within the time limit");
+        return W4_ERR_TIMEOUT;
     }
-    if (M <= 8) return launch_tma_nt<__half, 1>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
-    return launch_tma_nt<__half, 2>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    return W4_OK;
 }
 
 int take_wait_status() {

@@ -184,7 +184,9 @@ extern "C" int w4_tp_wait(w4_tp_comm *c, void *stream, int timeout_ms) {
         cudaError_t q = cudaStreamQuery(st);
         if (q == cudaSuccess) {
             // a one-shot all-reduce whose peer never pushed ended with a device status
-            const int rs = c->p2p ? take_tp_wait_status() : W4_OK;
+            int rs = c->p2p ? take_tp_wait_status() : W4_OK;
+            const int rf = c->p2p ? take_tp_fused_wait_status() : W4_OK;
+            if (!rs) rs = rf;
             if (rs) {
                 api.comm_abort(c->comm);
                 c->dead = true;
@@ -213,6 +215,13 @@ extern "C" int w4_tp_wait(w4_tp_comm *c, void *stream, int timeout_ms) {
     }
 }
 
+extern "C" int w4_tp_set_fused_epilogue(w4_tp_comm *c, int on) {
+    set_error("");
+    W4_REQUIRE(c, W4_ERR_INVALID, "comm is required");
+    c->fuse = on != 0;
+    return W4_OK;
+}
+
 extern "C" size_t w4_tp_linear_workspace_bytes(int mode, int M, int N, int K, int group_size, int has_perm,
                                                int c_dtype) {
     size_t ws = w4_gptq_workspace_bytes(M, N, K, group_size, has_perm, c_dtype == W4_E4M3 ? W4_F32 : c_dtype);
@@ -235,6 +244,28 @@ extern "C" int w4_tp_linear(w4_tp_comm *c, int mode, const void *a, int a_dtype,
     const size_t need = w4_tp_linear_workspace_bytes(mode, M, N, K, group_size, perm != nullptr, c_dtype);
     W4_REQUIRE(workspace_bytes >= need && (need == 0 || workspace), W4_ERR_INVALID,
                "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+    if (c->fuse && c->p2p && !perm && M <= 16) {
+        // decode: the GEMM pushes its fp32 partial tiles to every rank and sums them in
+        // its own epilogue (no separate all-reduce launch)
+        PeerReduce pr;
+        if (tp_peer_reduce_args(c, &pr)) {
+            int rc = check_gptq_gemm(a, a_dtype, qweight, scales, out, c_dtype, row_scale, M, N, K, group_size);
+            if (rc) return rc;
+            cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+            if (c_dtype != W4_E4M3) {
+                rc = gptq_gemv_tma_ar(a, a_dtype, qweight, qzeros, scales, out, c_dtype, M, N, K, group_size,
+                                      zero_offset, pr, st);
+                if (rc != -1) return rc;
+            } else {
+                const size_t gws = w4_gptq_workspace_bytes(M, N, K, group_size, 0, W4_F32);
+                float *part = reinterpret_cast<float *>(static_cast<char *>(workspace) + (gws + 255) / 256 * 256);
+                rc = gptq_gemv_tma_ar(a, a_dtype, qweight, qzeros, scales, part, W4_F32, M, N, K, group_size,
+                                      zero_offset, pr, st);
+                if (rc == W4_OK) return rowscale_fp8(part, W4_F32, static_cast<uint8_t *>(out), row_scale, M, N, st);
+                if (rc != -1) return rc;
+            }
+        }
+    }
     if (c_dtype != W4_E4M3) {
         // partial product over this rank's K rows, then the in-place sum
         int rc = w4_gptq_gemm(a, a_dtype, qweight, qzeros, scales, perm, out, c_dtype, nullptr, M, N, K,

@@ -8,6 +8,8 @@
 
 #include <mutex>
 
+#include "w4_internal.h"
+
 constexpr int kTpMaxRanks = 8;
 
 struct w4_tp_comm {
@@ -22,6 +24,7 @@ struct w4_tp_comm {
     void *sym = nullptr;
     void *peer[kTpMaxRanks] = {};
     bool p2p = false;
+    bool fuse = false;  // row-parallel decode GEMMs reduce in their own epilogue (w4_tp_set_fused_epilogue)
 };
 
 namespace w4 {
@@ -74,5 +77,7 @@ void tp_peer_teardown(w4_tp_comm *c);              // unmap peers, free the loca
 // W4_OK / a W4 error, or -1 when the one-shot path does not take this call.
 int tp_peer_allreduce(w4_tp_comm *c, void *buf, size_t count, int dtype, cudaStream_t st);
 int take_tp_wait_status();
+// The peer buffers as the fused row-parallel GEMM sees them; false without the peer path.
+bool tp_peer_reduce_args(const w4_tp_comm *c, PeerReduce *pr);
 
 }  // namespace w4

@@ -18,6 +18,8 @@
 // still reading, because each call waits for every peer's push of that call.
 // The counters live in device memory, so captured CUDA graphs replay correctly.
 // No copy here is a TMA or bulk load, and nothing uses multicast.
+// The same buffer also carries the epilogue all-reduce of the fused
+// row-parallel decode GEMM (separate slots, flags and sequence; see fdata_off).
 #include <chrono>
 #include <thread>
 
@@ -36,7 +38,17 @@ constexpr unsigned long long kTpWaitNs = 500ull * 1000 * 1000;  // 500 ms
 
 static size_t flags_off(int nranks) { return 2 * (size_t)nranks * kTpSlotBytes; }
 static size_t ctr_off(int nranks) { return flags_off(nranks) + 2 * kTpMaxBlocks * 8 * sizeof(uint32_t); }
-static size_t sym_bytes(int nranks) { return ctr_off(nranks) + kTpMaxBlocks * sizeof(uint32_t); }
+
+// A second region serves the row-parallel decode GEMM that reduces in its own
+// epilogue (gptq_tma.cu): its own fp32 slots, per-CTA flags and a control word
+// pair {call sequence, CTAs finished}, so its parity sequence never shares
+// slots with the all-reduce kernel's.
+constexpr size_t kFusedSlotBytes = size_t(512) << 10;  // M * N * 4 per rank and parity
+constexpr int kFusedMaxCtas = 1024;
+static size_t fdata_off(int nranks) { return (ctr_off(nranks) + kTpMaxBlocks * sizeof(uint32_t) + 255) & ~size_t(255); }
+static size_t fflags_off(int nranks) { return fdata_off(nranks) + 2 * (size_t)nranks * kFusedSlotBytes; }
+static size_t fctrl_off(int nranks) { return fflags_off(nranks) + 2 * (size_t)kFusedMaxCtas * 8 * sizeof(uint32_t); }
+static size_t sym_bytes(int nranks) { return fctrl_off(nranks) + 256; }
 
 struct PeerPtrs {
     char *p[kTpMaxRanks];
@@ -93,10 +105,12 @@ oneshot_allreduce_kernel(PeerPtrs pp, int rank, int nranks, T *__restrict__ data
             *reinterpret_cast<uint4 *>(slot + i) = x;
         }
     }
-    __threadfence_system();
     __syncthreads();
-    if (threadIdx.x < nranks)
+    // the system fence and release of the flagging threads are cumulative over the barrier
+    if (threadIdx.x < nranks) {
+        __threadfence_system();
         st_release_sys(reinterpret_cast<uint32_t *>(pp.p[threadIdx.x] + foff) + (par * kTpMaxBlocks + b) * 8 + rank, v);
+    }
 
     // 2. wait until every rank has pushed block b of this call into this rank's buffer
     if (threadIdx.x < nranks) {
@@ -289,6 +303,19 @@ int tp_peer_allreduce(w4_tp_comm *c, void *buf, size_t count, int dtype, cudaStr
             pp, c->rank, c->nranks, static_cast<float *>(buf), n, per, fo, co);
     W4_LAUNCH_CHECK();
     return W4_OK;
+}
+
+bool tp_peer_reduce_args(const w4_tp_comm *c, PeerReduce *pr) {
+    if (!c->p2p || c->nranks > kPeerMaxRanks) return false;
+    for (int p = 0; p < kPeerMaxRanks; ++p) pr->buf[p] = static_cast<char *>(c->peer[p]);
+    pr->data_off = fdata_off(c->nranks);
+    pr->slot_bytes = kFusedSlotBytes;
+    pr->flags_off = fflags_off(c->nranks);
+    pr->ctrl_off = fctrl_off(c->nranks);
+    pr->rank = c->rank;
+    pr->nranks = c->nranks;
+    pr->max_ctas = kFusedMaxCtas;
+    return true;
 }
 
 int take_tp_wait_status() {

@@ -85,7 +85,8 @@ int w4_check_device_status(void) {
     const int r3 = w4::take_fp4_wait_status();
     const int r4 = w4::take_fp4_prefill_wait_status();
     const int r5 = w4::take_tp_wait_status();
-    return r1 ? r1 : r2 ? r2 : r3 ? r3 : r4 ? r4 : r5;
+    const int r6 = w4::take_tp_fused_wait_status();
+    return r1 ? r1 : r2 ? r2 : r3 ? r3 : r4 ? r4 : r5 ? r5 : r6;
 }
 
 // ------------------------------------------------------------------ GPTQ
@@ -132,11 +133,12 @@ size_t w4_gptq_workspace_bytes(int M, int N, int K, int group_size, int has_perm
     return ws;
 }
 
-int w4_gptq_gemm(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
-                 const uint16_t *scales, const int32_t *perm, void *c, int c_dtype,
-                 float *row_scale, int M, int N, int K, int group_size, int zero_offset,
-                 void *workspace, size_t workspace_bytes, void *stream) {
-    w4::set_error("");
+}  // extern "C"
+
+namespace w4 {
+// The argument rules of w4_gptq_gemm (everything but the workspace).
+int check_gptq_gemm(const void *a, int a_dtype, const int32_t *qweight, const uint16_t *scales, const void *c,
+                    int c_dtype, const float *row_scale, int M, int N, int K, int group_size) {
     int rc = check_gptq_common(qweight, scales, K, N, group_size);
     if (rc) return rc;
     W4_REQUIRE(a && c, W4_ERR_INVALID, "a and c are required");
@@ -152,6 +154,19 @@ int w4_gptq_gemm(const void *a, int a_dtype, const int32_t *qweight, const int32
                "a and qweight must be 16-byte aligned, scales 8-byte aligned");
     W4_REQUIRE((size_t)(K / 8) * (size_t)N < (size_t(1) << 31), W4_ERR_UNSUPPORTED,
                "qweight of %d x %d words exceeds 2^31 elements", K / 8, N);
+    return W4_OK;
+}
+}  // namespace w4
+
+extern "C" {
+
+int w4_gptq_gemm(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
+                 const uint16_t *scales, const int32_t *perm, void *c, int c_dtype,
+                 float *row_scale, int M, int N, int K, int group_size, int zero_offset,
+                 void *workspace, size_t workspace_bytes, void *stream) {
+    w4::set_error("");
+    int rc = w4::check_gptq_gemm(a, a_dtype, qweight, scales, c, c_dtype, row_scale, M, N, K, group_size);
+    if (rc) return rc;
     const size_t need = w4_gptq_workspace_bytes(M, N, K, group_size, perm != nullptr, c_dtype);
     W4_REQUIRE(workspace_bytes >= need && (need == 0 || workspace), W4_ERR_INVALID,
                "workspace of %zu bytes needed, %zu given", need, workspace_bytes);

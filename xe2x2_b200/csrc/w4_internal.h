@@ -22,6 +22,27 @@ int gptq_gemv_tma(const void *a, int a_dtype, const int32_t *qweight, const int3
                   const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
                   cudaStream_t st);
 int take_wait_status();
+
+// Row-parallel decode GEMM with the all-reduce in its epilogue (gptq_tma.cu), over
+// the peer buffers of a tensor-parallel communicator (tp_peer.cu lays them out):
+// buf[p] is rank p's symmetric buffer mapped into this process.
+constexpr int kPeerMaxRanks = 8;
+struct PeerReduce {
+    char *buf[kPeerMaxRanks];
+    size_t data_off;    // fp32 partials [2 parities][nranks][slot_bytes]
+    size_t slot_bytes;  // per rank and parity: M * N * 4 must fit
+    size_t flags_off;   // u32 [2 parities][max_ctas][8 ranks]
+    size_t ctrl_off;    // u32 {call sequence, CTAs finished}
+    int rank, nranks, max_ctas;
+};
+// W4_OK / a W4 error, or -1 when this shape or device cannot run the fused kernel.
+int gptq_gemv_tma_ar(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
+                     const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
+                     const PeerReduce &pr, cudaStream_t st);
+int take_tp_fused_wait_status();
+// w4_api.cu: the argument rules of w4_gptq_gemm, without the workspace
+int check_gptq_gemm(const void *a, int a_dtype, const int32_t *qweight, const uint16_t *scales, const void *c,
+                    int c_dtype, const float *row_scale, int M, int N, int K, int group_size);
 // gptq_prefill.cu (tcgen05); -1 = shape not handled there
 int gptq_prefill(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
                  void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset, void *split_ws,

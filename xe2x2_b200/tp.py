@@ -118,6 +118,11 @@ class TPComm:
         L.call("w4_tp_allreduce", self.handle, ops._p(t), t.numel(), ops._DT[t.dtype], ops._stream(t.device))
         return t
 
+    def set_fused_epilogue(self, on: bool):
+        """Row-parallel decode layers reduce in the GEMM's own epilogue, or run GEMM +
+        all-reduce (the default; every rank must choose the same)."""
+        L.call("w4_tp_set_fused_epilogue", self.handle, 1 if on else 0)
+
     def wait(self, timeout_ms: int | None = None):
         """Block until the current stream is done; W4Error(W4_ERR_TIMEOUT) if a peer is missing."""
         L.call("w4_tp_wait", self.handle, ops._stream(self.device), timeout_ms or self.timeout_ms)
