@@ -351,7 +351,7 @@ def run_ours(args) -> None:
                     "ms_per_step": round(ms_e2e / args.steps, 5)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": TRAFFIC_PER_LAUNCH,
-                         "kernel": "w4::gptq_gemv_kernel", "peak_source": peak_src,
+                         "kernel": "w4::gptq_gemv_tma_kernel", "peak_source": peak_src,
                          "per_m": per_m},
             "gpu_launches": len(MS) * args.steps,
             "clocks": clk,
