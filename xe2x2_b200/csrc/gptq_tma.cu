@@ -103,7 +103,7 @@ __global__ void __maxnreg__(kTmaMaxRegs)
 gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_constant__ CUtensorMap sc_map,
                      const __grid_constant__ CUtensorMap zr_map, const __grid_constant__ CUtensorMap act_map,
                      int has_z, const T *__restrict__ A, void *__restrict__ C, int c_dtype, int M, int N, int K,
-                     int zero_offset, int stages_total, int act_rows, int pre, const __grid_constant__ PeerReduce pr) {
+                     int zero_offset, int stages_all, int act_rows, int pre, const __grid_constant__ PeerReduce pr) {
     constexpr int S = kTmaStages;
     constexpr int NE = 2 * NT * 4;
     constexpr int ROWS = 4 * GSTEPS;           // qweight rows per group
@@ -115,7 +115,11 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
     const RingLayout L(kVps * ROWS * 128, ACT ? act_rows * SSTEPS * 64 : 0, NE * 32 * 4);
     const int n0 = blockIdx.y * 32;
     const int tok0 = blockIdx.x * 8 * NT;
-    // Warp w consumes stages [w*stages_total/W, (w+1)*stages_total/W) of K; a
+    // Split K across the CTAs of a cluster (grid z): this CTA owns stages
+    // [zb, zb + stages_total) of the stages_all stages of K.
+    const int zb = (int)(blockIdx.z * (unsigned)stages_all / gridDim.z);
+    const int stages_total = (int)((blockIdx.z + 1) * (unsigned)stages_all / gridDim.z) - zb;
+    // Warp w consumes stages [w*stages_total/W, (w+1)*stages_total/W) of them; a
     // stage is kVps whole groups.
 
     if (warp == W) {  // ---------------- producer warp ----------------
@@ -143,7 +147,7 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
                     if (sb + it >= se) continue;
                     uint8_t *r = base + (size_t)w * L.total;
                     uint64_t *full = reinterpret_cast<uint64_t *>(r + L.bars) + it;
-                    const int vg = (sb + it) * kVps;
+                    const int vg = (zb + sb + it) * kVps;
                     mbar_arrive_expect_tx(full, tx);
                     tma_load_2d(r + it * L.qw_stage, &qw_map, n0, vg * ROWS, full);
                     tma_load_2d(r + L.cst + it * 256, &sc_map, n0, vg, full);
@@ -158,7 +162,7 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
                     uint8_t *r = base + (size_t)w * L.total;
                     uint64_t *full = reinterpret_cast<uint64_t *>(r + L.bars) + s;
                     uint64_t *empty = full + S;
-                    const int vg = (sb + it) * kVps;  // first group of the stage
+                    const int vg = (zb + sb + it) * kVps;  // first group of the stage
                     if (it >= pf) {
                         if (it >= S && !mbar_wait_bounded(empty, (uint32_t)(((it / S) - 1) & 1))) {
                             atomicExch(&g_wait_timeout, 1u);
@@ -173,6 +177,11 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
                     if (ACT) tma_load_3d(r + L.act + s * L.act_stage, &act_map, 0, tok0, (vg * ROWS) / 8, full);  // 64-k line of the stage
                 }
             }
+        }
+        __syncwarp();
+        if (gridDim.z > 1) {  // meet the consumers at the cluster reduction's two barriers
+            cluster_sync_all();
+            cluster_sync_all();
         }
         return;  // consumers wait for every copy this warp issued
     }
@@ -206,7 +215,7 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
         } else {
             const int tok = tok0 + nt * 8 + g;
             av[nt] = tok < M;
-            ap[nt] = A + (size_t)(av[nt] ? tok : 0) * K + (size_t)(sbeg * kVps * ROWS + t) * 8;
+            ap[nt] = A + (size_t)(av[nt] ? tok : 0) * K + (size_t)((zb + sbeg) * kVps * ROWS + t) * 8;
             xa[nt] = (av[nt] && nsteps > 0) ? __ldg(reinterpret_cast<const uint4 *>(ap[nt])) : make_uint4(0, 0, 0, 0);
             ap[nt] += 32;
         }
@@ -327,14 +336,38 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
             for (int i = 0; i < 4; ++i) red[((mt * NT + nt) * 4 + i) * 32 + lane] = facc[mt][nt][i];
     asm volatile("bar.sync 1, %0;" ::"r"(W * 32) : "memory");  // consumers only
     if constexpr (!AR) {
-        for (int idx = threadIdx.x; idx < NE * 32; idx += W * 32) {
-            float val = 0.f;
-            for (int w = 0; w < W; ++w) val += reinterpret_cast<const float *>(base + (size_t)w * L.total + L.red)[idx];
-            const int e = idx >> 5, l = idx & 31;
-            const int mt = e / (NT * 4), nt = (e / 4) % NT, i = e & 3;
-            const int col = n0 + 4 * sigma(l >> 2) + 2 * mt + (i >> 1);
-            const int tok = tok0 + nt * 8 + 2 * (l & 3) + (i & 1);
-            if (tok < M) store_out(C, c_dtype, (size_t)tok * N + col, val);
+        if (gridDim.z == 1) {
+            for (int idx = threadIdx.x; idx < NE * 32; idx += W * 32) {
+                float val = 0.f;
+                for (int w = 0; w < W; ++w) val += reinterpret_cast<const float *>(base + (size_t)w * L.total + L.red)[idx];
+                const int e = idx >> 5, l = idx & 31;
+                const int mt = e / (NT * 4), nt = (e / 4) % NT, i = e & 3;
+                const int col = n0 + 4 * sigma(l >> 2) + 2 * mt + (i >> 1);
+                const int tok = tok0 + nt * 8 + 2 * (l & 3) + (i & 1);
+                if (tok < M) store_out(C, c_dtype, (size_t)tok * N + col, val);
+            }
+        } else {
+            // K split over the cluster: each CTA leaves its partial tile in its own
+            // shared memory; CTA r of the cluster sums elements r, r + ks, ... over
+            // the cluster's CTAs in rank order (DSMEM loads) and stores them.
+            float *fin = reinterpret_cast<float *>(base + (size_t)W * L.total);
+            for (int idx = threadIdx.x; idx < NE * 32; idx += W * 32) {
+                float val = 0.f;
+                for (int w = 0; w < W; ++w) val += reinterpret_cast<const float *>(base + (size_t)w * L.total + L.red)[idx];
+                fin[idx] = val;
+            }
+            cluster_sync_all();
+            const int ks = (int)gridDim.z, cr = (int)cluster_rank();
+            for (int idx = cr + ks * (int)threadIdx.x; idx < NE * 32; idx += ks * W * 32) {
+                float val = 0.f;
+                for (int c = 0; c < ks; ++c) val += ld_cluster_f32(fin + idx, (uint32_t)c);
+                const int e = idx >> 5, l = idx & 31;
+                const int mt = e / (NT * 4), nt = (e / 4) % NT, i = e & 3;
+                const int col = n0 + 4 * sigma(l >> 2) + 2 * mt + (i >> 1);
+                const int tok = tok0 + nt * 8 + 2 * (l & 3) + (i & 1);
+                if (tok < M) store_out(C, c_dtype, (size_t)tok * N + col, val);
+            }
+            cluster_sync_all();  // no CTA leaves while another still reads its tile
         }
     } else {
         // tile rows of 32 fp32 outputs, 16-byte vectors to and from the peer slots
@@ -431,13 +464,23 @@ static int launch_tma_t(const void *a, const int32_t *qweight, const int32_t *qz
     // resident in one wave (ctas_per_sm CTAs sharing an SM's 224 KB), at most
     // one per stage.
     const long ctas = (long)nchunk * mblocks;
-    const long ctas_per_sm = (ctas + nsm - 1) / nsm;
-    long fit = ((224L * 1024) / ctas_per_sm - 1024) / (long)per_warp;
+    // Fewer column tiles than two per SM: split K over a cluster of ks CTAs per
+    // tile (reduced through distributed shared memory), so more warps share the
+    // stages and the tiles spread evenly over the SMs.
+    int ks = 1;
+    if (!AR && ctas < 2L * nsm) {
+        ks = (int)((2L * nsm + ctas - 1) / ctas);
+        if (ks > 4) ks = 4;
+        if (ks > stages_total) ks = stages_total;
+    }
+    const size_t fin_bytes = ks > 1 ? (size_t)NE * 32 * 4 : 0;
+    const long ctas_per_sm = (ctas * ks + nsm - 1) / nsm;
+    long fit = ((224L * 1024) / ctas_per_sm - 1024 - (long)fin_bytes) / (long)per_warp;
     // the register file must hold ctas_per_sm CTAs of W + 1 warps as well
     const long fit_regs = 65536L / (ctas_per_sm * 32L * kTmaMaxRegs) - 1;
     if (fit_regs < fit) fit = fit_regs;
     int W = (int)(fit < 1 ? 1 : (fit > kTmaMaxWarps ? kTmaMaxWarps : fit));
-    if (W > stages_total) W = stages_total;
+    if (W > stages_total / ks) W = stages_total / ks;  // every warp of every CTA gets a stage
     const CUtensorMapDataType adt =
         std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     CUtensorMap qw_map, sc_map, zr_map, act_map;
@@ -472,9 +515,9 @@ static int launch_tma_t(const void *a, const int32_t *qweight, const int32_t *qz
             set_dev[dev] = true;
         }
     }
-    const size_t smem = 1024 + (size_t)W * per_warp;
+    const size_t smem = 1024 + (size_t)W * per_warp + fin_bytes;
     if (smem > 220 * 1024) return -1;
-    dim3 grid(mblocks, nchunk), block(32 * (W + 1));
+    dim3 grid(mblocks, nchunk, ks), block(32 * (W + 1));
     if constexpr (AR) {
         // every CTA must be resident at once (each waits for its peers' counterpart)
         if (ctas > pr->max_ctas || (size_t)M * N * 4 > pr->slot_bytes) return -1;
@@ -496,7 +539,7 @@ static int launch_tma_t(const void *a, const int32_t *qweight, const int32_t *qz
     } else {
         const int pre = launch_overlap() == W4_OVERLAP_STATIC_WEIGHTS;
         const PeerReduce none{};
-        W4_CUDA_TRY(launch_decode(kern, grid, block, smem, st, qw_map, sc_map, zr_map, act_map, has_z,
+        W4_CUDA_TRY(launch_decode(kern, grid, block, smem, st, (unsigned)ks, qw_map, sc_map, zr_map, act_map, has_z,
                                   static_cast<const T *>(a), c, c_dtype, M, N, K, zero_offset, stages_total, act_rows,
                                   pre, none));
     }

@@ -41,7 +41,9 @@ namespace fp4t {
 constexpr int S = 3;            // ring depth per consumer warp
 constexpr int KS = 256;         // k per stage (two 128-k steps)
 constexpr int kMaxWarps = 8;    // consumer warps per CTA (one more warp produces)
-constexpr int kMaxRegs = 128;   // 4 CTAs of 4 warps per SM fit the register file
+// Register cap: 128 lets 4 CTAs of 4 warps share an SM; two token tiles (NT = 2)
+// need more to keep both activation fragments and accumulators in registers.
+template <int NT> constexpr int max_regs() { return NT == 1 ? 128 : 192; }
 
 // Byte offsets inside one consumer warp's ring (from a 1024-aligned base).
 struct Lay {
@@ -89,10 +91,10 @@ template <int SDT> __device__ __forceinline__ void load_scales4(const uint8_t *p
 }
 
 template <int NT, int SDT>
-__global__ void __maxnreg__(kMaxRegs)
+__global__ void __maxnreg__(max_regs<NT>())
 nvfp4_gemv_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap sc_map,
                       const __grid_constant__ CUtensorMap act_map, const float *__restrict__ global_scale,
-                      void *__restrict__ C, int c_dtype, int M, int N, int stages_total, int act_rows, int pre) {
+                      void *__restrict__ C, int c_dtype, int M, int N, int stages_all, int act_rows, int pre) {
     constexpr int NE = 2 * NT * 4;
     constexpr int SB = SDT == W4_E4M3 ? 1 : 2;  // bytes per block scale
     extern __shared__ uint8_t smem_dyn[];
@@ -102,6 +104,10 @@ nvfp4_gemv_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_co
     const Lay L(act_rows, SB, NE * 32 * 4);
     const int n0 = blockIdx.y * 32;
     const int tok0 = blockIdx.x * 8 * NT;
+    // Split K across the CTAs of a cluster (grid z): this CTA owns stages
+    // [zb, zb + stages_total) of the stages_all stages of K.
+    const int zb = (int)(blockIdx.z * (unsigned)stages_all / gridDim.z);
+    const int stages_total = (int)((blockIdx.z + 1) * (unsigned)stages_all / gridDim.z) - zb;
 
     if (warp == W && lane == 0) {
         for (int w = 0; w < W; ++w) {
@@ -127,8 +133,8 @@ nvfp4_gemv_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_co
                     uint8_t *r = base + (size_t)w * L.total;
                     uint64_t *full = reinterpret_cast<uint64_t *>(r + L.bars) + it;
                     mbar_arrive_expect_tx(full, tx);
-                    tma_load_2d(r + it * Lay::W_STAGE, &w_map, (sb + it) * (KS / 2), n0, full);
-                    tma_load_2d(r + L.sc + it * L.sc_stage, &sc_map, n0, (sb + it) * (KS / 16), full);
+                    tma_load_2d(r + it * Lay::W_STAGE, &w_map, (zb + sb + it) * (KS / 2), n0, full);
+                    tma_load_2d(r + L.sc + it * L.sc_stage, &sc_map, n0, (zb + sb + it) * (KS / 16), full);
                 }
             grid_dep_wait();  // activations are the previous kernel's output
             for (int it = 0; it < most && ok; ++it) {
@@ -138,7 +144,7 @@ nvfp4_gemv_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_co
                     if (sb + it >= se) continue;
                     uint8_t *r = base + (size_t)w * L.total;
                     uint64_t *full = reinterpret_cast<uint64_t *>(r + L.bars) + s;
-                    const int st = sb + it;
+                    const int st = zb + sb + it;
                     if (it >= pf) {
                         if (it >= S && !wait_fp4(full + S, (uint32_t)(((it / S) - 1) & 1))) {
                             ok = false;
@@ -151,6 +157,11 @@ nvfp4_gemv_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_co
                     tma_load_3d(r + L.act + s * L.act_stage, &act_map, 0, tok0, st * (KS / 64), full);
                 }
             }
+        }
+        __syncwarp();
+        if (gridDim.z > 1) {  // meet the consumers at the cluster reduction's two barriers
+            cluster_sync_all();
+            cluster_sync_all();
         }
         return;
     }
@@ -257,14 +268,37 @@ nvfp4_gemv_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_co
             for (int i = 0; i < 4; ++i) red[((mt * NT + nt) * 4 + i) * 32 + lane] = acc[mt][nt][i];
     asm volatile("bar.sync 1, %0;" ::"r"(W * 32) : "memory");
     const float gsc = global_scale ? *global_scale : 1.0f;
-    for (int idx = threadIdx.x; idx < NE * 32; idx += W * 32) {
-        float v = 0.f;
-        for (int w = 0; w < W; ++w) v += reinterpret_cast<const float *>(base + (size_t)w * L.total + L.red)[idx];
-        const int e = idx >> 5, l = idx & 31;
-        const int mt = e / (NT * 4), nt = (e / 4) % NT, i = e & 3;
-        const int col = n0 + 4 * (l >> 2) + 2 * mt + (i >> 1);
-        const int tok = tok0 + nt * 8 + 2 * (l & 3) + (i & 1);
-        if (tok < M) store_out(C, c_dtype, (size_t)tok * N + col, v * gsc);
+    if (gridDim.z == 1) {
+        for (int idx = threadIdx.x; idx < NE * 32; idx += W * 32) {
+            float v = 0.f;
+            for (int w = 0; w < W; ++w) v += reinterpret_cast<const float *>(base + (size_t)w * L.total + L.red)[idx];
+            const int e = idx >> 5, l = idx & 31;
+            const int mt = e / (NT * 4), nt = (e / 4) % NT, i = e & 3;
+            const int col = n0 + 4 * (l >> 2) + 2 * mt + (i >> 1);
+            const int tok = tok0 + nt * 8 + 2 * (l & 3) + (i & 1);
+            if (tok < M) store_out(C, c_dtype, (size_t)tok * N + col, v * gsc);
+        }
+    } else {
+        // K split over the cluster: partial tiles stay in each CTA's shared memory;
+        // CTA r sums elements r, r + ks, ... over the cluster in rank order.
+        float *fin = reinterpret_cast<float *>(base + (size_t)W * L.total);
+        for (int idx = threadIdx.x; idx < NE * 32; idx += W * 32) {
+            float v = 0.f;
+            for (int w = 0; w < W; ++w) v += reinterpret_cast<const float *>(base + (size_t)w * L.total + L.red)[idx];
+            fin[idx] = v;
+        }
+        cluster_sync_all();
+        const int ks = (int)gridDim.z, cr = (int)cluster_rank();
+        for (int idx = cr + ks * (int)threadIdx.x; idx < NE * 32; idx += ks * W * 32) {
+            float v = 0.f;
+            for (int c = 0; c < ks; ++c) v += ld_cluster_f32(fin + idx, (uint32_t)c);
+            const int e = idx >> 5, l = idx & 31;
+            const int mt = e / (NT * 4), nt = (e / 4) % NT, i = e & 3;
+            const int col = n0 + 4 * (l >> 2) + 2 * mt + (i >> 1);
+            const int tok = tok0 + nt * 8 + 2 * (l & 3) + (i & 1);
+            if (tok < M) store_out(C, c_dtype, (size_t)tok * N + col, v * gsc);
+        }
+        cluster_sync_all();  // no CTA leaves while another still reads its tile
     }
 }
 
@@ -281,10 +315,21 @@ static int launch(const uint16_t *a, const uint8_t *w, const void *scale, const 
     const int act_rows = M < 8 * NT ? M : 8 * NT;
     const Lay lay(act_rows, SB, NE * 32 * 4);
     const long ctas = (long)nchunk * mblocks;
-    const long ctas_per_sm = (ctas + nsm - 1) / nsm;
-    const long fit = ((224L * 1024) / ctas_per_sm - 1024) / (long)lay.total;
+    // Fewer column tiles than two per SM: split K over a cluster of ks CTAs per
+    // tile (reduced through distributed shared memory).
+    int ks = 1;
+    if (ctas < 2L * nsm) {
+        ks = (int)((2L * nsm + ctas - 1) / ctas);
+        if (ks > 4) ks = 4;
+        if (ks > stages_total) ks = stages_total;
+    }
+    const size_t fin_bytes = ks > 1 ? (size_t)NE * 32 * 4 : 0;
+    const long ctas_per_sm = (ctas * ks + nsm - 1) / nsm;
+    long fit = ((224L * 1024) / ctas_per_sm - 1024 - (long)fin_bytes) / (long)lay.total;
+    const long fit_regs = 65536L / (ctas_per_sm * 32L * max_regs<NT>()) - 1;  // the register file too
+    if (fit_regs < fit) fit = fit_regs;
     int W = (int)(fit < 1 ? 1 : (fit > kMaxWarps ? kMaxWarps : fit));
-    if (W > stages_total) W = stages_total;
+    if (W > stages_total / ks) W = stages_total / ks;  // every warp of every CTA gets a stage
     CUtensorMap w_map, sc_map, act_map;
     if (!make_map_2d(&w_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)K / 2, N, (uint64_t)K / 2, KS / 2, 32,
                      CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -305,11 +350,11 @@ static int launch(const uint16_t *a, const uint8_t *w, const void *scale, const 
             set_dev[dev] = true;
         }
     }
-    const size_t smem = 1024 + (size_t)W * lay.total;
+    const size_t smem = 1024 + (size_t)W * lay.total + fin_bytes;
     if (smem > 220 * 1024) return -1;
-    dim3 grid(mblocks, nchunk), block(32 * (W + 1));
+    dim3 grid(mblocks, nchunk, ks), block(32 * (W + 1));
     const int pre = launch_overlap() == W4_OVERLAP_STATIC_WEIGHTS;
-    W4_CUDA_TRY(launch_decode(kern, grid, block, smem, st, w_map, sc_map, act_map, global_scale, c, c_dtype, M, N,
+    W4_CUDA_TRY(launch_decode(kern, grid, block, smem, st, (unsigned)ks, w_map, sc_map, act_map, global_scale, c, c_dtype, M, N,
                               stages_total, act_rows, pre));
     return W4_OK;
 }

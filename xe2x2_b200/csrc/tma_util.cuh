@@ -75,6 +75,24 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
 // its memory is visible (no-ops when the launch carries no such dependency).
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Thread-block clusters: a full barrier over every thread of every CTA of the
+// cluster (release / acquire at cluster scope), this CTA's rank in it, and a
+// load from the same shared-memory offset in another CTA of the cluster.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ float ld_cluster_f32(const float *p, uint32_t rank) {
+    uint32_t a;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+    return v;
+}
 __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -98,19 +116,31 @@ inline PFN_cuTensorMapEncodeTiled encode_fn() {
 // Launch of a decode kernel, with programmatic stream serialisation unless the
 // overlap mode is W4_OVERLAP_OFF: the kernel may then start while the previous
 // kernel on the stream drains, and orders itself behind it with grid_dep_wait().
+// cluster_z > 1: thread-block clusters of (1, 1, cluster_z) CTAs along grid z.
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_decode(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                                 Args &&...args) {
+                                 unsigned cluster_z, Args &&...args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute at[2];
+    unsigned n = 0;
+    if (launch_overlap() != W4_OVERLAP_OFF) {
+        at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    if (cluster_z > 1) {
+        at[n].id = cudaLaunchAttributeClusterDimension;
+        at[n].val.clusterDim.x = 1;
+        at[n].val.clusterDim.y = 1;
+        at[n].val.clusterDim.z = cluster_z;
+        ++n;
+    }
     cfg.attrs = at;
-    cfg.numAttrs = launch_overlap() == W4_OVERLAP_OFF ? 0 : 1;
+    cfg.numAttrs = n;
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
