@@ -111,7 +111,7 @@ def _case_layers(rank, world):
 
 def _case_fused_row_parallel(rank, world):
     """Decode row-parallel layers reducing in the GEMV epilogue over peer memory
-    (w4_tp_set_fused_epilogue): the same bits as GEMM + all-reduce for f32 outputs, the same bits on every rank,
+    (w4_tp_set_fused_epilogue): equal to GEMM + all-reduce up to fp32 summation order, the same bits on every rank,
     correct under CUDA-graph replay, close to the unsharded GEMM."""
     import torch.distributed as dist
 
@@ -135,7 +135,9 @@ def _case_fused_row_parallel(rank, world):
                 comm.set_fused_epilogue(False)
                 u32 = lay(xs, out_dtype=torch.float32)
                 comm.wait()
-                assert torch.equal(f32, u32), (K, N, M)  # rank-ordered fp32 sums either way
+                # fp32 partials summed in rank order either way; the un-fused GEMM may split K
+                # over a CTA cluster, which changes the order of the fp32 partial sums
+                assert _rel(f32, u32) < 1e-6, (K, N, M)
                 assert _rel(f32, full) < 1e-5
                 assert _rel(b16, full) < 1e-2
                 assert _rel(q8.float() * rs[:, None], full) < 4e-2
