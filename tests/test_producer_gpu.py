@@ -43,6 +43,8 @@ def _exact_inputs(M, K, dtype, seed):
     (130, 2048, torch.bfloat16, True),
     (3, 17408, torch.bfloat16, True),   # 256 threads, 8 register blocks each
     (2, 40960, torch.float16, False),   # rows too wide for registers: two passes over x
+    (600, 2048, torch.bfloat16, True),  # streaming kernel: rows arrive by bulk copy, persistent grid
+    (333, 12288, torch.float16, False), # streaming kernel at its widest row
 ])
 def test_producer_bit_exact_on_order_independent_sums(cuda, M, K, dtype, use_gamma):
     x = _exact_inputs(M, K, dtype, seed=M)

@@ -8,8 +8,12 @@
 // [K/16, N] in both.
 #include <cooperative_groups.h>
 #include <cuda_fp4.h>
+#include <cuda_fp8.h>
+
+#include <mutex>
 
 #include "nvfp4_util.cuh"
+#include "tma_util.cuh"
 #include "w4_common.cuh"
 #include "w4_internal.h"
 
@@ -74,8 +78,11 @@ __device__ __forceinline__ uint32_t nvfp4_block(const float (&v)[16], float g, u
     float amax = 0.f;
 #pragma unroll
     for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    const uint32_t s = f_to_e4m3(__fdiv_rn(amax, __fmul_rn(6.0f, g)));
-    const float sdec = __fmul_rn(e4m3_to_f(s), g);
+    // hardware conversions (one instruction each): f32 -> e4m3 rounds to nearest
+    // even and saturates at 448 like f_to_e4m3 (amax is never NaN here); e4m3 ->
+    // f16 is exact
+    const uint32_t s = (uint32_t)__nv_cvt_float_to_fp8(__fdiv_rn(amax, __fmul_rn(6.0f, g)), __NV_SATFINITE, __NV_E4M3);
+    const float sdec = __fmul_rn(__half2float(__ushort_as_half(__nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)s, __NV_E4M3).x)), g);
     const float inv = sdec != 0.f ? __frcp_rn(sdec) : 0.f;
     // hardware E2M1 conversion: round to nearest even, saturating at +-6 (the
     // rounding rule of f_to_e2m1 / the host quantiser)
@@ -225,16 +232,133 @@ rmsnorm_nvfp4_kernel(const T *__restrict__ x, const T *__restrict__ gamma, float
     }
 }
 
+static __device__ unsigned int g_rn_timeout;  // a bounded wait expired in the streaming producer
+
+// Streaming form of the producer for rows up to kRnStreamMaxK values: a
+// persistent grid; each CTA walks rows blockIdx.x, + gridDim.x, ... and keeps
+// kRnBufs rows in flight, each brought into shared memory by one bulk copy
+// (cp.async.bulk, completion on an mbarrier, bounded wait), so the next rows
+// stream in while this one is reduced and quantised.  The arithmetic is the
+// per-row kernel's (rmsnorm_nvfp4_block); the padding rows of the last tile get
+// zero codes and scales.
+constexpr int kRnBufs = 3;
+constexpr int kRnStreamMaxK = 12288;  // 768 threads, one per 16-k block
+
 template <typename T, bool GAMMA>
-static void launch_rmsnorm_nvfp4(const T *x, const T *gamma, float eps, const float *a_global, uint8_t *codes,
-                                 uint8_t *sf_atoms, int M, int K, cudaStream_t st) {
+__global__ void __launch_bounds__(kRnStreamMaxK / 16)
+rmsnorm_nvfp4_stream_kernel(const T *__restrict__ x, const T *__restrict__ gamma, float eps,
+                            const float *__restrict__ a_global, uint8_t *__restrict__ codes,
+                            uint8_t *__restrict__ sf, int M, int K, int rows_padded) {
+    extern __shared__ __align__(128) uint8_t rn_smem[];
+    __shared__ __align__(8) uint64_t full[kRnBufs];
+    __shared__ float sh[32];
+    const int nb = K / 16;
+    const uint32_t row_bytes = (uint32_t)K * 2;
+    const int nrows = M > (int)blockIdx.x ? (M - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    if (threadIdx.x == 0) {
+        for (int b = 0; b < kRnBufs; ++b) mbar_init(&full[b], 1);
+        fence_mbar_init();
+        for (int i = 0; i < nrows && i < kRnBufs; ++i) {
+            mbar_arrive_expect_tx(&full[i], row_bytes);
+            bulk_load_1d(rn_smem + (size_t)i * row_bytes, x + (size_t)(blockIdx.x + i * gridDim.x) * K, row_bytes,
+                         &full[i]);
+        }
+    }
+    __syncthreads();
+    const float g = *a_global;
+    for (int i = 0; i < nrows; ++i) {
+        const int b = i % kRnBufs;
+        const int row = blockIdx.x + i * gridDim.x;
+        const bool ok = mbar_wait_bounded(&full[b], (uint32_t)((i / kRnBufs) & 1));
+        if (__syncthreads_or(!ok)) {  // a copy never landed: stop every thread here
+            if (threadIdx.x == 0) atomicExch(&g_rn_timeout, 1u);
+            break;
+        }
+        // thread t owns 16-k block t of the row (blockDim = nb rounded up to a warp)
+        const T *xr = reinterpret_cast<const T *>(rn_smem + (size_t)b * row_bytes);
+        const int kb = threadIdx.x;
+        uint32_t wv[8] = {};
+        if (kb < nb) {
+            const uint4 u0 = *reinterpret_cast<const uint4 *>(xr + (size_t)kb * 16);
+            const uint4 u1 = *reinterpret_cast<const uint4 *>(xr + (size_t)kb * 16 + 8);
+            wv[0] = u0.x, wv[1] = u0.y, wv[2] = u0.z, wv[3] = u0.w;
+            wv[4] = u1.x, wv[5] = u1.y, wv[6] = u1.z, wv[7] = u1.w;
+        }
+        __syncthreads();  // the row is in registers: buffer b takes the row kRnBufs ahead
+        if (threadIdx.x == 0 && i + kRnBufs < nrows) {
+            fence_proxy_async();  // generic reads of buffer b before the copy that overwrites it
+            mbar_arrive_expect_tx(&full[b], row_bytes);
+            bulk_load_1d(rn_smem + (size_t)b * row_bytes, x + (size_t)(row + kRnBufs * gridDim.x) * K, row_bytes,
+                         &full[b]);
+        }
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float2 f = Conv<T>::to_f2(wv[j]);
+            ss += f.x * f.x + f.y * f.y;
+        }
+        ss = block_reduce(ss, false, sh);
+        const float inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), eps)));
+        if (kb < nb) rmsnorm_nvfp4_block<T, GAMMA>(wv, gamma, kb, inv, g, codes + (size_t)row * (K / 2), sf, row, nb);
+    }
+    // padding rows of the last 128-row tile
+    for (int row = M + blockIdx.x; row < rows_padded; row += gridDim.x) {
+        uint8_t *cr = codes + (size_t)row * (K / 2);
+        for (int kb = threadIdx.x; kb < nb; kb += blockDim.x) {
+            sf[sf_offset<true>(row, kb, nb)] = 0;
+            *reinterpret_cast<uint2 *>(cr + (size_t)kb * 8) = make_uint2(0, 0);
+        }
+    }
+}
+
+int take_rn_wait_status() {
+    unsigned int v = 0;
+    W4_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_rn_timeout, sizeof(v)));
+    if (v) {
+        const unsigned int zero = 0;
+        W4_CUDA_TRY(cudaMemcpyToSymbol(g_rn_timeout, &zero, sizeof(zero)));
+        set_error("a bulk copy never completed in the RMSNorm -> NVFP4 producer within the time limit");
+        return W4_ERR_TIMEOUT;
+    }
+    return W4_OK;
+}
+
+template <typename T, bool GAMMA>
+static int launch_rmsnorm_nvfp4(const T *x, const T *gamma, float eps, const float *a_global, uint8_t *codes,
+                                uint8_t *sf_atoms, int M, int K, cudaStream_t st) {
     const int rows = (M + 127) / 128 * 128, nb = K / 16;
+    if (K <= kRnStreamMaxK && M >= 2 * num_sms()) {
+        auto kern = rmsnorm_nvfp4_stream_kernel<T, GAMMA>;
+        const size_t smem = (size_t)kRnBufs * K * 2;
+        {
+            static std::mutex mu;
+            static bool set_dev[128] = {};
+            int dev = 0;
+            W4_CUDA_TRY(cudaGetDevice(&dev));
+            std::lock_guard<std::mutex> lk(mu);
+            if (dev < 128 && !set_dev[dev]) {
+                W4_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 kRnBufs * kRnStreamMaxK * 2));
+                set_dev[dev] = true;
+            }
+        }
+        const int threads = (nb + 31) / 32 * 32;
+        int per_sm = 0;
+        W4_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem));
+        if (per_sm < 1) per_sm = 1;
+        const int grid = per_sm * num_sms() < M ? per_sm * num_sms() : M;
+        kern<<<grid, threads, smem, st>>>(x, gamma, eps, a_global, codes, sf_atoms, M, K, rows);
+        W4_LAUNCH_CHECK();
+        return W4_OK;
+    }
     if (nb <= 128 * 4)
         rmsnorm_nvfp4_kernel<T, GAMMA, 4><<<rows, 128, 0, st>>>(x, gamma, eps, a_global, codes, sf_atoms, M, K);
     else if (nb <= 256 * 8)
         rmsnorm_nvfp4_kernel<T, GAMMA, 8><<<rows, 256, 0, st>>>(x, gamma, eps, a_global, codes, sf_atoms, M, K);
     else
         rmsnorm_nvfp4_kernel<T, GAMMA, 0><<<rows, 256, 0, st>>>(x, gamma, eps, a_global, codes, sf_atoms, M, K);
+    W4_LAUNCH_CHECK();
+    return W4_OK;
 }
 
 int rmsnorm_nvfp4(const void *x, int x_dtype, const void *gamma, float eps, const float *a_global, uint8_t *codes,
@@ -242,22 +366,20 @@ int rmsnorm_nvfp4(const void *x, int x_dtype, const void *gamma, float eps, cons
     if (x_dtype == W4_BF16) {
         using T = __nv_bfloat16;
         if (gamma)
-            launch_rmsnorm_nvfp4<T, true>(static_cast<const T *>(x), static_cast<const T *>(gamma), eps, a_global,
+            return launch_rmsnorm_nvfp4<T, true>(static_cast<const T *>(x), static_cast<const T *>(gamma), eps, a_global,
                                           codes, sf_atoms, M, K, st);
         else
-            launch_rmsnorm_nvfp4<T, false>(static_cast<const T *>(x), nullptr, eps, a_global, codes, sf_atoms, M,
+            return launch_rmsnorm_nvfp4<T, false>(static_cast<const T *>(x), nullptr, eps, a_global, codes, sf_atoms, M,
                                            K, st);
     } else {
         using T = __half;
         if (gamma)
-            launch_rmsnorm_nvfp4<T, true>(static_cast<const T *>(x), static_cast<const T *>(gamma), eps, a_global,
+            return launch_rmsnorm_nvfp4<T, true>(static_cast<const T *>(x), static_cast<const T *>(gamma), eps, a_global,
                                           codes, sf_atoms, M, K, st);
         else
-            launch_rmsnorm_nvfp4<T, false>(static_cast<const T *>(x), nullptr, eps, a_global, codes, sf_atoms, M,
+            return launch_rmsnorm_nvfp4<T, false>(static_cast<const T *>(x), nullptr, eps, a_global, codes, sf_atoms, M,
                                            K, st);
     }
-    W4_LAUNCH_CHECK();
-    return W4_OK;
 }
 
 int nvfp4_quant_act(const uint16_t *a, int M, int K, const float *a_global, uint8_t *codes,

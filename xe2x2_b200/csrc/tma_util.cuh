@@ -70,6 +70,14 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
         : "memory");
 }
+// Untiled bulk copy global -> this CTA's shared memory (no multicast): 16-byte
+// aligned addresses, a size that is a multiple of 16, completion on bar.
+__device__ __forceinline__ void bulk_load_1d(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
 // Programmatic dependent launch: let the next grid on the stream start its
 // prologue now / wait until every grid this one depends on has completed and
 // its memory is visible (no-ops when the launch carries no such dependency).

@@ -86,7 +86,8 @@ int w4_check_device_status(void) {
     const int r4 = w4::take_fp4_prefill_wait_status();
     const int r5 = w4::take_tp_wait_status();
     const int r6 = w4::take_tp_fused_wait_status();
-    return r1 ? r1 : r2 ? r2 : r3 ? r3 : r4 ? r4 : r5 ? r5 : r6;
+    const int r7 = w4::take_rn_wait_status();
+    return r1 ? r1 : r2 ? r2 : r3 ? r3 : r4 ? r4 : r5 ? r5 : r6 ? r6 : r7;
 }
 
 // ------------------------------------------------------------------ GPTQ

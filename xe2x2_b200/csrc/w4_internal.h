@@ -79,6 +79,7 @@ int nvfp4_gemv(const uint16_t *a, const uint8_t *w, int layout, const void *scal
 // epilogue.cu
 int rmsnorm_quant_s8(const uint16_t *x, int8_t *q, float *scale, int M, int K, float eps,
                      cudaStream_t st);
+int take_rn_wait_status();
 // RMSNorm -> NVFP4 codes [rows, K/2] + scale atoms, rows = M rounded up to 128 (nvfp4.cu).
 int rmsnorm_nvfp4(const void *x, int x_dtype, const void *gamma, float eps, const float *a_global, uint8_t *codes,
                   uint8_t *sf_atoms, int M, int K, cudaStream_t st);
