@@ -132,7 +132,6 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
         }
     }
     __syncthreads();  // barriers initialised before anyone waits on them
-    grid_dep_launch();  // the next decode GEMM may set up while this one runs
     if (warp == W) {
         if (lane == 0) {
             const uint32_t tx = kVps * (ROWS * 128 + 64 + (has_z ? 16 : 0)) + (ACT ? act_rows * SSTEPS * 64 : 0);
@@ -179,6 +178,7 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
             }
         }
         __syncwarp();
+        grid_dep_launch();  // every copy is issued: the next decode GEMM may be scheduled
         if (gridDim.z > 1) {  // meet the consumers at the cluster reduction's two barriers
             cluster_sync_all();
             cluster_sync_all();
@@ -328,6 +328,9 @@ gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_co
     }
 
     // ---- K-split reduction across the W consumer warps ----
+    // The next decode GEMM may be scheduled once every thread of every CTA is here
+    // (late, so its CTAs take the slots this grid frees, evenly).
+    grid_dep_launch();
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt)
 #pragma unroll

@@ -117,7 +117,6 @@ nvfp4_gemv_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_co
         fence_mbar_init();
     }
     __syncthreads();
-    grid_dep_launch();  // the next decode GEMM may set up while this one runs
     if (warp == W) {  // ---------------- producer ----------------
         if (lane == 0) {
             const uint32_t tx = Lay::W_STAGE + act_rows * KS * 2 + 16 * 32 * SB;
@@ -159,6 +158,7 @@ nvfp4_gemv_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_co
             }
         }
         __syncwarp();
+        grid_dep_launch();  // every copy is issued: the next decode GEMM may be scheduled
         if (gridDim.z > 1) {  // meet the consumers at the cluster reduction's two barriers
             cluster_sync_all();
             cluster_sync_all();
@@ -260,6 +260,9 @@ nvfp4_gemv_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_co
         }
     }
 
+    // The next decode GEMM may be scheduled once every thread of every CTA is here
+    // (late, so its CTAs take the slots this grid frees, evenly).
+    grid_dep_launch();
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
