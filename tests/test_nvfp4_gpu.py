@@ -123,14 +123,25 @@ def test_config3_decode(cuda, M):
     assert rf < 5e-3
 
 
-def test_bf16_folded_scale_operator(cuda):
-    """nvfp4_gemm_w4a16(x, w, None, scale_bf16, 16): folded scales, weights rounded to bf16."""
-    M, K, N = 3, 1024, 128
+@pytest.mark.parametrize("M", [3, 12, 40])
+def test_bf16_folded_scale_operator(cuda, M):
+    """nvfp4_gemm_w4a16(x, w, None, scale_bf16, 16): folded scales, weights rounded to bf16
+    (always the decode kernels, two token tiles from M = 9)."""
+    K, N = 1024, 128
     w, _, _ = synth.nvfp4_weights(K, N, seed=6, device=cuda)
     scale = (torch.rand((K // 16, N), device=cuda) * 0.05 + 0.001).to(torch.bfloat16)
     x = synth.activations(M, K, torch.bfloat16, seed=7, device=cuda)
     out = ops.nvfp4_gemm_w4a16(x, w, None, scale, 16)
     assert_gemm_close(f32(out), _oracle_gemm(x, w, scale, None))
+
+
+def test_two_token_tile_decode_on_shapes_the_tensor_path_skips(cuda):
+    """N % 128 != 0 keeps M = 9..16 on the two-token-tile decode kernel."""
+    M, K, N = 12, 1024, 96
+    w, scale, gscale = synth.nvfp4_weights(K, N, seed=12, device=cuda)
+    x = synth.activations(M, K, torch.bfloat16, seed=13, device=cuda)
+    out = ops.nvfp4_gemm(x, w, scale, gscale, out_dtype=torch.float32)
+    assert_gemm_close(np_(out), _oracle_gemm(x, w, scale, gscale), rel=1e-5, nmax=1e-5)
 
 
 def test_kn_weights_accepted_by_operator(cuda):

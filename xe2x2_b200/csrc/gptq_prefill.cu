@@ -24,11 +24,21 @@
 //              to the async proxy and arrives on bfull[j].  Warps 2-5 then read
 //              the accumulator out of TMEM (32 lanes each) and store C.
 // (q - z) is exact in bf16; the product is rounded once to the MMA input type.
+//
+// FP4: the same GEMM for NVFP4 weights with bf16 activations (W4A16; the
+// reference operator nvfp4_gemm_w4a16, kernels/nvfp4/bench_nvfp4_m1.py:58-96, at
+// prefill sizes).  The raw weight pieces are the k-block's 32 code bytes of each
+// of the BN columns ([N, K/2] K-contiguous) and its four E4M3 block-scale rows;
+// a dequantiser turns 8 codes into e2m1 * scale in bf16 (exact: at most six
+// significant bits) and the epilogue multiplies by the fp32 tensor scale.
 // Every mbarrier wait is bounded (tma_util.cuh): on expiry the CTA stops its
 // loops, the MMA thread still signals completion, TMEM is freed, and
 // w4_check_device_status() reports W4_ERR_TIMEOUT.  No copy uses multicast.
 #include <type_traits>
 
+#include <cuda_fp8.h>
+
+#include "nvfp4_util.cuh"
 #include "tma_util.cuh"
 #include "w4_common.cuh"
 #include "w4_internal.h"
@@ -45,12 +55,12 @@ constexpr int kDeqWarps = 16;  // two threads per column of a 256-wide tile
 constexpr int kThreads = (2 + kDeqWarps) * 32;
 
 // MT: 128-row A tiles per CTA sharing one dequantised B tile (1 or 2).
-template <int BN, int MT> struct Layout {
+template <int BN, int MT, bool FP4 = false> struct Layout {
     static constexpr int S = MT == 2 ? 3 : 4;                // A + raw-weight ring depth
     static constexpr uint32_t A_BYTES = MT * BM * BK * 2;    // 16 KB per 128 rows
     static constexpr uint32_t B_BYTES = BN * BK * 2;         // 32 KB at BN = 256
-    static constexpr uint32_t QW_BYTES = (BK / 8) * BN * 4;  // 8 KB
-    static constexpr uint32_t SC_BYTES = BN * 2;             // one f16 scale row
+    static constexpr uint32_t QW_BYTES = (BK / 8) * BN * 4;  // 8 KB (FP4: BN x 32 code bytes, the same)
+    static constexpr uint32_t SC_BYTES = FP4 ? (BK / 16) * BN : BN * 2;  // f16 scale row / 4 E4M3 rows
     static constexpr uint32_t ZR_SLOT = 128;                 // one packed zero row (BN/2 bytes), 128-aligned
     static constexpr uint32_t A_OFF = 0;
     static constexpr uint32_t B_OFF = A_OFF + S * A_BYTES;
@@ -167,13 +177,14 @@ __device__ __forceinline__ bool pf_wait(uint64_t *bar, uint32_t parity, volatile
     return true;
 }
 
-template <typename T, int BN, int MT>
+template <typename T, int BN, int MT, bool FP4>
 __global__ void __launch_bounds__(kThreads, 1)
 gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap qw_map,
                     const __grid_constant__ CUtensorMap sc_map, const __grid_constant__ CUtensorMap zr_map,
                     int has_z, void *__restrict__ C, int c_dtype, int M, int N, int K, int gs, int zero_offset,
-                    int kb_per_split, float *__restrict__ partial) {
-    using Lay = Layout<BN, MT>;
+                    int kb_per_split, float *__restrict__ partial, const float *__restrict__ w_global) {
+    static_assert(!FP4 || std::is_same<T, __nv_bfloat16>::value, "NVFP4 weights meet bf16 activations");
+    using Lay = Layout<BN, MT, FP4>;
     constexpr int S = Lay::S;
     extern __shared__ uint8_t smem_dyn[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
@@ -221,9 +232,14 @@ gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
                 const int g = (kb * BK) / gs;
                 mbar_arrive_expect_tx(&full[s], tx);
                 tma_load_2d(sm + Lay::A_OFF + s * Lay::A_BYTES, &a_map, kb * BK, m0, &full[s]);
-                tma_load_2d(sm + Lay::QW_OFF + s * Lay::QW_BYTES, &qw_map, n0, kb * (BK / 8), &full[s]);
-                tma_load_2d(sm + Lay::SC_OFF + s * Lay::SC_BYTES, &sc_map, n0, g, &full[s]);
-                if (has_z) tma_load_2d(sm + Lay::ZR_OFF + s * Lay::ZR_SLOT, &zr_map, n0 / 8, g, &full[s]);
+                if constexpr (FP4) {
+                    tma_load_2d(sm + Lay::QW_OFF + s * Lay::QW_BYTES, &qw_map, kb * (BK / 2), n0, &full[s]);
+                    tma_load_2d(sm + Lay::SC_OFF + s * Lay::SC_BYTES, &sc_map, n0, kb * (BK / 16), &full[s]);
+                } else {
+                    tma_load_2d(sm + Lay::QW_OFF + s * Lay::QW_BYTES, &qw_map, n0, kb * (BK / 8), &full[s]);
+                    tma_load_2d(sm + Lay::SC_OFF + s * Lay::SC_BYTES, &sc_map, n0, g, &full[s]);
+                    if (has_z) tma_load_2d(sm + Lay::ZR_OFF + s * Lay::ZR_SLOT, &zr_map, n0 / 8, g, &full[s]);
+                }
             }
         }
     } else if (warp == 1) {
@@ -260,6 +276,42 @@ gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
             bool ok = pf_wait(&full[s], (uint32_t)((i / S) & 1), abort_flag);
             if (ok && i >= SB) ok = pf_wait(&bempty[j], (uint32_t)(((i / SB) - 1) & 1), abort_flag);
             if (!__all_sync(0xffffffffu, ok)) break;
+            if constexpr (FP4) {
+                // thread r0 of column n dequantises code chunks [r0 * CPT, (r0 + 1) * CPT) of the
+                // k-block (a chunk = 8 k = 4 code bytes; 16-k block scale row = chunk / 2)
+                constexpr int CPT = 8 / TPC;
+                const uint8_t *codes = sm + Lay::QW_OFF + s * Lay::QW_BYTES + n * (BK / 2) + r0 * CPT * 4;
+                const uint8_t *srow = sm + Lay::SC_OFF + s * Lay::SC_BYTES + n;
+                uint8_t *brow = sm + Lay::B_OFF + j * Lay::B_BYTES + n * 128;
+                uint32_t cw[CPT];
+                if constexpr (CPT == 4) {
+                    const uint4 u = *reinterpret_cast<const uint4 *>(codes);
+                    cw[0] = u.x, cw[1] = u.y, cw[2] = u.z, cw[3] = u.w;
+                } else {
+#pragma unroll
+                    for (int t = 0; t < CPT; ++t) cw[t] = reinterpret_cast<const uint32_t *>(codes)[t];
+                }
+#pragma unroll
+                for (int t = 0; t < CPT; ++t) {
+                    const int kr = r0 * CPT + t;
+                    const __half_raw sh = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)srow[(kr >> 1) * BN], __NV_E4M3);
+                    const uint32_t sb = __bfloat16_as_ushort(__float2bfloat16_rn(__half2float(__ushort_as_half(sh.x))));
+                    const uint32_t sc2 = sb | (sb << 16);
+                    uint32_t v01, v23, v45, v67;
+                    e2m1x4_to_bf16(cw[t], v01, v23);
+                    e2m1x4_to_bf16(cw[t] >> 16, v45, v67);
+                    uint4 o;  // k0..k7 in order
+                    o.x = bf16x2_mul(v01, sc2);
+                    o.y = bf16x2_mul(v23, sc2);
+                    o.z = bf16x2_mul(v45, sc2);
+                    o.w = bf16x2_mul(v67, sc2);
+                    *reinterpret_cast<uint4 *>(brow + ((kr ^ (n & 7)) << 4)) = o;
+                }
+                fence_proxy_async();  // make the generic-proxy writes visible to the tensor core
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bfull[j]);
+                continue;
+            }
             const uint16_t sbits = reinterpret_cast<const uint16_t *>(sm + Lay::SC_OFF + s * Lay::SC_BYTES)[n];
             const uint32_t zq =
                 has_z ? (reinterpret_cast<const uint32_t *>(sm + Lay::ZR_OFF + s * Lay::ZR_SLOT)[n >> 3] >> zsh) & 15u
@@ -293,12 +345,17 @@ gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
             (void)ok;
             tc_fence_after();
             const int q = warp & 3;
+            const float gsc = w_global ? *w_global : 1.0f;  // NVFP4 tensor scale
 #pragma unroll 1
             for (int cc = 0; cc < MT * BN; cc += 32) {
                 const int mh = cc / BN, c0 = cc % BN;
                 const int row = m0 + mh * BM + 32 * q + lane;
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)cc, v);
+                if (w_global) {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * gsc);
+                }
                 if (row < M) {
                     const size_t base = (size_t)row * N + n0 + c0;
                     if (partial) {
@@ -390,7 +447,7 @@ static int launch(const void *a, const int32_t *qweight, const int32_t *qzeros, 
     } else {
         zr_map = sc_map;  // unused
     }
-    auto kern = gptq_prefill_kernel<T, BN, MT>;
+    auto kern = gptq_prefill_kernel<T, BN, MT, false>;
     const size_t smem = Lay::TOTAL + 1024;
     {
         static std::mutex mu;
@@ -408,7 +465,49 @@ static int launch(const void *a, const int32_t *qweight, const int32_t *qzeros, 
     ksplit = (nk + kb_per_split - 1) / kb_per_split;  // every split gets at least one k-block
     dim3 grid((M + BM * MT - 1) / (BM * MT), N / BN, ksplit), block(kThreads);
     kern<<<grid, block, smem, st>>>(a_map, qw_map, sc_map, zr_map, has_z, c, c_dtype, M, N, K, gs, zero_offset,
-                                    kb_per_split, ksplit > 1 ? partial : nullptr);
+                                    kb_per_split, ksplit > 1 ? partial : nullptr, nullptr);
+    W4_LAUNCH_CHECK();
+    if (ksplit > 1) {
+        const long mn = (long)M * N;  // N % 128 == 0: whole float4 groups
+        splitk_reduce_kernel<<<(unsigned)((mn / 4 + 255) / 256), 256, 0, st>>>(partial, ksplit, mn, c, c_dtype);
+        W4_LAUNCH_CHECK();
+    }
+    return W4_OK;
+}
+
+// NVFP4 weights (codes [N, K/2] K-contiguous, E4M3 block scales [K/16, N], fp32
+// tensor scale) with bf16 activations.
+template <int BN, int MT>
+static int launch_fp4(const uint16_t *a, const uint8_t *w_nk, const uint8_t *scale, const float *w_global, void *c,
+                      int c_dtype, int M, int N, int K, int ksplit, float *partial, cudaStream_t st) {
+    using Lay = Layout<BN, MT, true>;
+    CUtensorMap a_map, qw_map, sc_map;
+    if (!make_map_2d(&a_map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a, K, M, (uint64_t)K * 2, BK, BM * MT,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map_2d(&qw_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_nk, (uint64_t)K / 2, N, (uint64_t)K / 2, BK / 2, BN,
+                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map_2d(&sc_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, scale, N, K / 16, (uint64_t)N, BN, BK / 16,
+                     CU_TENSOR_MAP_SWIZZLE_NONE))
+        return -1;
+    auto kern = gptq_prefill_kernel<__nv_bfloat16, BN, MT, true>;
+    const size_t smem = Lay::TOTAL + 1024;
+    {
+        static std::mutex mu;
+        static bool set_dev[128] = {};
+        int dev = 0;
+        W4_CUDA_TRY(cudaGetDevice(&dev));
+        std::lock_guard<std::mutex> lk(mu);
+        if (dev < 128 && !set_dev[dev]) {
+            W4_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            set_dev[dev] = true;
+        }
+    }
+    const int nk = K / BK;
+    const int kb_per_split = (nk + ksplit - 1) / ksplit;
+    ksplit = (nk + kb_per_split - 1) / kb_per_split;
+    dim3 grid((M + BM * MT - 1) / (BM * MT), N / BN, ksplit), block(kThreads);
+    kern<<<grid, block, smem, st>>>(a_map, qw_map, sc_map, sc_map, 0, c, c_dtype, M, N, K, BK, 0, kb_per_split,
+                                    ksplit > 1 ? partial : nullptr, w_global);
     W4_LAUNCH_CHECK();
     if (ksplit > 1) {
         const long mn = (long)M * N;  // N % 128 == 0: whole float4 groups
@@ -482,6 +581,32 @@ int gptq_prefill(const void *a, int a_dtype, const int32_t *qweight, const int32
     if (mt == 2) return wide ? W4_PF_LAUNCH(__half, 256, 2) : W4_PF_LAUNCH(__half, 128, 2);
     return wide ? W4_PF_LAUNCH(__half, 256, 1) : W4_PF_LAUNCH(__half, 128, 1);
 #undef W4_PF_LAUNCH
+}
+
+size_t nvfp4_w4a16_prefill_split_bytes(int M, int N, int K, int c_dtype) {
+    if (M < kFp4PrefillMinM || !pf::handled(N, K, pf::BK, c_dtype)) return 0;
+    const int ks = pf::ksplit_for(M, N, K);
+    return ks > 1 ? (size_t)ks * M * N * sizeof(float) : 0;
+}
+
+// NVFP4 W4A16 on the tensor cores (M >= kFp4PrefillMinM): W4_OK / a W4 error, or -1
+// when the shape is not handled here (the caller then runs the decode kernel).
+int nvfp4_w4a16_prefill(const uint16_t *a, const uint8_t *w_nk, const uint8_t *scale, const float *w_global,
+                        void *c, int c_dtype, int M, int N, int K, void *split_ws, size_t split_ws_bytes,
+                        cudaStream_t st) {
+    if (M < kFp4PrefillMinM || !pf::handled(N, K, pf::BK, c_dtype)) return -1;
+    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(w_nk) | reinterpret_cast<uintptr_t>(scale)) &
+        15)
+        return -1;
+    const bool wide = pf::wide_tiles(M, N);
+    int ks = pf::ksplit_for(M, N, K);
+    if (ks > 1 && (!split_ws || split_ws_bytes < (size_t)ks * M * N * sizeof(float))) ks = 1;
+    float *partial = static_cast<float *>(split_ws);
+    if (pf::m_tiles_per_cta(M) == 2)
+        return wide ? pf::launch_fp4<256, 2>(a, w_nk, scale, w_global, c, c_dtype, M, N, K, ks, partial, st)
+                    : pf::launch_fp4<128, 2>(a, w_nk, scale, w_global, c, c_dtype, M, N, K, ks, partial, st);
+    return wide ? pf::launch_fp4<256, 1>(a, w_nk, scale, w_global, c, c_dtype, M, N, K, ks, partial, st)
+                : pf::launch_fp4<128, 1>(a, w_nk, scale, w_global, c, c_dtype, M, N, K, ks, partial, st);
 }
 
 int take_prefill_wait_status() {

@@ -244,6 +244,9 @@ size_t w4_nvfp4_workspace_bytes(int M, int N, int K, int act_mode, int c_dtype) 
     if (M <= 0 || N <= 0 || K <= 0) return 0;
     if (act_mode == W4_ACT_NVFP4) ws += w4::nvfp4_prefill_workspace(M, N, K);
     if (c_dtype == W4_E4M3) ws += align256((size_t)M * N * 4);
+    // split-K partials of the W4A16 tensor-core GEMM (the f32 product when the output is e4m3)
+    if (act_mode == W4_ACT_W4A16)
+        ws += align256(w4::nvfp4_w4a16_prefill_split_bytes(M, N, K, c_dtype == W4_E4M3 ? W4_F32 : c_dtype));
     return ws;
 }
 
@@ -296,15 +299,27 @@ int w4_nvfp4_gemm(const void *a, const uint8_t *w, int layout, const void *scale
         if (rc || c_dtype != W4_E4M3) return rc;
         return w4::rowscale_fp8(out, W4_F32, static_cast<uint8_t *>(c), row_scale, M, N, st);
     }
+    // W4A16: the tensor-core GEMM from kFp4PrefillMinM tokens on (E4M3 block scales),
+    // else the decode kernels
+    char *wsb = static_cast<char *>(workspace);
+    void *out = c;
+    int odt = c_dtype;
     if (c_dtype == W4_E4M3) {
-        float *y = static_cast<float *>(workspace);
-        rc = w4::nvfp4_gemv(static_cast<const uint16_t *>(a), w, layout, scale, scale_dtype,
-                            global_scale, y, W4_F32, M, N, K, st);
-        if (rc) return rc;
-        return w4::rowscale_fp8(y, W4_F32, static_cast<uint8_t *>(c), row_scale, M, N, st);
+        out = wsb;
+        odt = W4_F32;
+        wsb += align256((size_t)M * N * 4);
     }
-    return w4::nvfp4_gemv(static_cast<const uint16_t *>(a), w, layout, scale, scale_dtype,
-                          global_scale, c, c_dtype, M, N, K, st);
+    rc = -1;
+    if (scale_dtype == W4_E4M3) {
+        const size_t split = w4::nvfp4_w4a16_prefill_split_bytes(M, N, K, odt);
+        rc = w4::nvfp4_w4a16_prefill(static_cast<const uint16_t *>(a), w, static_cast<const uint8_t *>(scale),
+                                     global_scale, out, odt, M, N, K, split ? wsb : nullptr, split, st);
+    }
+    if (rc == -1)
+        rc = w4::nvfp4_gemv(static_cast<const uint16_t *>(a), w, layout, scale, scale_dtype, global_scale, out, odt,
+                            M, N, K, st);
+    if (rc || c_dtype != W4_E4M3) return rc;
+    return w4::rowscale_fp8(out, W4_F32, static_cast<uint8_t *>(c), row_scale, M, N, st);
 }
 
 size_t w4_nvfp4_act_codes_bytes(int M, int K) {

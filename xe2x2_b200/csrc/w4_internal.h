@@ -49,7 +49,15 @@ int gptq_prefill(const void *a, int a_dtype, const int32_t *qweight, const int32
                  size_t split_ws_bytes, cudaStream_t st);
 size_t gptq_prefill_split_bytes(int M, int N, int K, int gs, int c_dtype);
 int take_prefill_wait_status();
+// NVFP4 weights, bf16 activations, on the tensor cores (gptq_prefill.cu); -1 = not handled
+int nvfp4_w4a16_prefill(const uint16_t *a, const uint8_t *w_nk, const uint8_t *scale, const float *w_global,
+                        void *c, int c_dtype, int M, int N, int K, void *split_ws, size_t split_ws_bytes,
+                        cudaStream_t st);
+size_t nvfp4_w4a16_prefill_split_bytes(int M, int N, int K, int c_dtype);
 constexpr int kPrefillMinM = 17;  // token counts from here on run the tensor-core prefill GEMM
+// NVFP4 W4A16: the two-token-tile decode kernel (M = 9..16) is slower than the tensor-core
+// GEMM, which therefore starts at 9 tokens
+constexpr int kFp4PrefillMinM = 9;
 int gptq_s4a(const uint8_t *a, const uint8_t *b, const float *a_scale, const uint16_t *s,
              uint16_t *c, int rows, int cols, int dk, cudaStream_t st);
 
