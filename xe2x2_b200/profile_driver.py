@@ -74,7 +74,8 @@ def nvfp4_bytes(M, K, N):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", choices=["gptq", "nvfp4"], default="gptq")
+    ap.add_argument("--kernel", choices=["gptq", "nvfp4", "producer"], default="gptq",
+                    help="producer: the fused RMSNorm -> NVFP4 activation kernel on [M, K]")
     ap.add_argument("--M", default="16", help="comma-separated token counts")
     ap.add_argument("--K", type=int, default=5120)
     ap.add_argument("--N", type=int, default=17408)
@@ -89,10 +90,15 @@ def main(argv=None):
     dt = torch.bfloat16 if args.dtype == "bf16" else torch.float16
     K, N = args.K, args.N
     wbytes = gptq_bytes(0, K, N, args.gs) if args.kernel == "gptq" else nvfp4_bytes(0, K, N)
+    if args.kernel == "producer":
+        wbytes = 1 << 40  # no weights: one copy
     l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 << 20) or (126 << 20)
     copies = max(1, math.ceil(2 * l2 / wbytes) + 1) if args.time else 1
     if args.kernel == "gptq":
         ws = [synth.gptq_weights(K, N, args.gs, asym=True, seed=s, device=dev)[:3] for s in range(copies)]
+    elif args.kernel == "producer":
+        copies = 1  # no weights; inputs are the activations
+        ws = [None]
     else:
         ws = [synth.nvfp4_weights(K, N, seed=s, device=dev) for s in range(copies)]
     results = []
@@ -105,6 +111,8 @@ def main(argv=None):
             w = ws[i % copies]
             if args.kernel == "gptq":
                 return ops.gptq_gemm(a, w[0], w[1], w[2], args.gs, 1)
+            if args.kernel == "producer":
+                return ops.rmsnorm_quant_nvfp4(a, ag)
             return ops.nvfp4_gemm(a, w[0], w[1], w[2], act_mode=act_mode, a_global=ag)
 
         if not args.time:
@@ -117,6 +125,8 @@ def main(argv=None):
         us = statistics.median(time_launches(run, max(args.iters, 20)))
         gus = time_graph(run, max(args.iters, 20, copies))
         nb = gptq_bytes(M, K, N, args.gs) if args.kernel == "gptq" else nvfp4_bytes(M, K, N)
+        if args.kernel == "producer":
+            nb = 2 * M * K + M * K // 2 + M * K // 16
         results.append({"kernel": args.kernel, "M": M, "K": K, "N": N, "us": round(us, 3), "graph_us": round(gus, 3),
                         "GB/s": round(nb / us / 1e3, 1), "TFLOP/s": round(2 * M * N * K / us / 1e6, 2)})
     for r in results:
