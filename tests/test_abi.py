@@ -102,3 +102,44 @@ def test_launch_overlap_mode_round_trip():
         assert lib.w4_get_launch_overlap() == L.W4_OVERLAP_DEPENDENT
     finally:
         lib.w4_set_launch_overlap(old)
+
+
+def test_producer_and_prequantised_gemm_reject_bad_arguments_without_gpu():
+    lib = L.lib()
+    f = _fake()
+    # K not a multiple of 64
+    assert lib.w4_rmsnorm_quant_nvfp4(f, L.W4_BF16, None, 1e-6, f, f, f, 4, 96, None) == L.W4_ERR_INVALID
+    # fp32 input
+    assert lib.w4_rmsnorm_quant_nvfp4(f, L.W4_F32, None, 1e-6, f, f, f, 4, 128, None) == L.W4_ERR_INVALID
+    # negative eps
+    assert lib.w4_rmsnorm_quant_nvfp4(f, L.W4_BF16, None, -1.0, f, f, f, 4, 128, None) == L.W4_ERR_INVALID
+    assert lib.w4_nvfp4_act_codes_bytes(200, 1024) == 256 * 512  # rows padded to the 128-row tile
+    # the pre-quantised GEMM: bf16 (folded) weight scales cannot feed the block-scaled MMA
+    rc = lib.w4_nvfp4_gemm_q(f, f, f, f, L.W4_NVFP4_NK, f, L.W4_BF16, None, f, L.W4_BF16, None, 128, 256,
+                             1024, None, 0, None)
+    assert rc == L.W4_ERR_UNSUPPORTED
+    # K not a multiple of 256
+    rc = lib.w4_nvfp4_gemm_q(f, f, f, f, L.W4_NVFP4_NK, f, L.W4_E4M3, f, f, L.W4_BF16, None, 128, 256,
+                             640, None, 0, None)
+    assert rc == L.W4_ERR_UNSUPPORTED
+    # missing activation scale atoms
+    rc = lib.w4_nvfp4_gemm_q(f, None, f, f, L.W4_NVFP4_NK, f, L.W4_E4M3, f, f, L.W4_BF16, None, 128, 256,
+                             1024, None, 0, None)
+    assert rc == L.W4_ERR_INVALID
+
+
+def test_tp_option_needs_a_communicator():
+    assert L.lib().w4_tp_set_fused_epilogue(None, 1) == L.W4_ERR_INVALID
+
+
+def test_python_wrappers_refuse_cpu_tensors_and_missing_scales():
+    import torch
+
+    from xe2x2_b200 import ops
+
+    x = torch.zeros(2, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        ops.rmsnorm_quant_nvfp4(x, torch.ones(1))
+    w = torch.zeros(64, 32, dtype=torch.uint8)
+    with pytest.raises(ValueError):
+        ops.NVFP4Linear(w, torch.zeros(8, 32, dtype=torch.uint8), torch.ones(1), None, L.W4_ACT_NVFP4)
