@@ -23,7 +23,8 @@
 // Tile 128 x 128 per CTA, 256 k per pipeline stage (four K=64 MMAs).  Warp 0
 // produces (TMA + bulk copies), warp 1 allocates TMEM and issues the scale
 // copies and MMAs, warps 2-5 read the fp32 accumulator out of TMEM, apply the
-// tensor scales and store C.  Every wait is bounded; no copy uses multicast.
+// tensor scales and store C.  The persistent form (large grids) gives the scale
+// copies a warp of their own.  Every wait is bounded; no copy uses multicast.
 #include <mutex>
 
 #include "tma_util.cuh"
@@ -297,11 +298,12 @@ nvfp4_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_con
 // release the accumulator to the MMA issuer at once, and only then scale and store,
 // so the next tile's MMAs overlap the stores and the producer never drains.
 namespace pcfg {
-constexpr int BN = 256, S = 4, NH = 2, kEpiWarps = 8, kThreadsP = (2 + kEpiWarps) * 32;
+// warps: 0 producer, 1 MMA issuer, 2-9 epilogue, 10 scale copier
+constexpr int BN = 256, S = 4, NH = 2, kEpiWarps = 8, kSfWarp = 2 + kEpiWarps, kThreadsP = (3 + kEpiWarps) * 32;
 constexpr uint32_t A_BYTES = BM * BK / 2, B_BYTES = BN * BK / 2, SFA_BYTES = 4 * SF_ATOM, SFB_BYTES = NH * 4 * SF_ATOM;
 constexpr uint32_t A_OFF = 0, B_OFF = A_OFF + S * A_BYTES, SFA_OFF = B_OFF + S * B_BYTES,
                    SFB_OFF = SFA_OFF + S * SFA_BYTES, BAR_OFF = SFB_OFF + S * SFB_BYTES,
-                   MISC_OFF = BAR_OFF + (2 * S + 2) * 8, SMEM = MISC_OFF + 16;
+                   MISC_OFF = BAR_OFF + (3 * S + 2) * 8, SMEM = MISC_OFF + 16;
 // TMEM: accumulator [0, 256); stage s scales at 256 + 48 s (A 16, W 32).
 constexpr uint32_t SF_COL0 = BN, SF_COLS = 16 + 16 * NH, TMEM_COLS = 512;
 static_assert(SF_COL0 + S * SF_COLS <= TMEM_COLS, "TMEM plan");
@@ -320,6 +322,7 @@ nvfp4_prefill_persistent_kernel(const __grid_constant__ CUtensorMap a_map, const
     uint64_t *empty = full + S;
     uint64_t *acc_full = empty + S;
     uint64_t *acc_empty = acc_full + 1;
+    uint64_t *sf_full = acc_empty + 1;  // stage s's scale atoms are in TMEM
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + MISC_OFF);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + MISC_OFF + 4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -335,6 +338,7 @@ nvfp4_prefill_persistent_kernel(const __grid_constant__ CUtensorMap a_map, const
         }
         mbar_init(acc_full, 1);
         mbar_init(acc_empty, kEpiWarps);  // one arrival per epilogue warp
+        for (int s = 0; s < S; ++s) mbar_init(&sf_full[s], 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -383,12 +387,41 @@ nvfp4_prefill_persistent_kernel(const __grid_constant__ CUtensorMap a_map, const
                 tc_fence_after();
                 for (int i = 0; i < nk; ++i, ++g) {
                     const int s = (int)(g % S);
-                    if (!wait_pf(&full[s], (uint32_t)((g / S) & 1), abort_flag)) {
+                    // operands landed (full) and the scale copier's atoms are in TMEM (sf_full)
+                    if (!wait_pf(&full[s], (uint32_t)((g / S) & 1), abort_flag) ||
+                        !wait_pf(&sf_full[s], (uint32_t)((g / S) & 1), abort_flag)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint64_t a_d = a_d0 + (uint64_t)(s * (A_BYTES >> 4)), b_d = b_d0 + (uint64_t)(s * (B_BYTES >> 4));
+                    const uint32_t col_a = tmem + SF_COL0 + SF_COLS * s, col_b = col_a + 16;
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_fp4(tmem, a_d + (uint64_t)(2 * kk), b_d + (uint64_t)(2 * kk), IDESC, col_a + 4 * kk,
+                                col_b + 4 * NH * kk, (i | kk) != 0);
+                    tc_commit(&empty[s]);
+                }
+                if (!ok) break;
+                tc_commit(acc_full);
+            }
+        }
+    } else if (warp == kSfWarp) {
+        // ---------------- scale copier: stage s's atoms into its TMEM columns ----------------
+        // A stage's columns are rewritten only after the producer refilled the stage,
+        // i.e. after the MMAs that read them committed empty[s].
+        if (lane == 0) {
+            const uint64_t sfa_d0 = sf_desc(smem_u32(sm + SFA_OFF)), sfb_d0 = sf_desc(smem_u32(sm + SFB_OFF));
+            long g = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                for (int i = 0; i < nk; ++i, ++g) {
+                    const int s = (int)(g % S);
+                    if (!wait_pf(&full[s], (uint32_t)((g / S) & 1), abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
                     const uint64_t sfa_d = sfa_d0 + (uint64_t)(s * (SFA_BYTES >> 4));
                     const uint64_t sfb_d = sfb_d0 + (uint64_t)(s * (SFB_BYTES >> 4));
                     const uint32_t col_a = tmem + SF_COL0 + SF_COLS * s, col_b = col_a + 16;
@@ -399,15 +432,12 @@ nvfp4_prefill_persistent_kernel(const __grid_constant__ CUtensorMap a_map, const
                         for (int h = 0; h < NH; ++h)
                             tc_cp_sf(col_b + 4 * NH * kk + 4 * h, sfb_d + (uint64_t)((h * 4 + kk) * (SF_ATOM >> 4)));
                     }
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        mma_fp4(tmem, a_d + (uint64_t)(2 * kk), b_d + (uint64_t)(2 * kk), IDESC, col_a + 4 * kk,
-                                col_b + 4 * NH * kk, (i | kk) != 0);
-                    tc_commit(&empty[s]);
+                    tc_commit(&sf_full[s]);
                 }
-                if (!ok) break;
-                tc_commit(acc_full);
             }
+            // nothing of this warp may still be in flight when TMEM is freed
+            if (g > 0 && !mbar_wait_bounded(&sf_full[(int)((g - 1) % S)], (uint32_t)(((g - 1) / S) & 1)))
+                atomicExch(&g_fp4pf_timeout, 1u);
         }
     } else {
         // ---------------- epilogue warps 2-9: lane quarter warp % 4, column half (warp - 2) / 4 ----------------
