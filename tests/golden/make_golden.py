@@ -15,7 +15,9 @@ It also writes a tiny act_order GPTQ checkpoint with this repository's
 safetensors writer (gptq_tiny.safetensors, seeded values) and records what the
 reference's own reader load_meta / read_tensor (:32-58) returns for every
 tensor in it (gptq_tiny_ref.npz); tests/test_checkpoint.py reads the same file
-with xe2x2_b200.checkpoint and compares.
+with xe2x2_b200.checkpoint and compares.  Finally it runs the reference's own
+main() on that checkpoint, which writes its tile dumps gptq_tiny_s4.bin and
+gptq_tiny_s4_sc.bin (:153-181).
 """
 from __future__ import annotations
 
@@ -52,6 +54,25 @@ def main(ref_root: str) -> None:
     ref = {name: mod.read_tensor(path, data0, info) for name, info in meta.items()}
     np.savez_compressed(os.path.join(here, "gptq_tiny_ref.npz"), **ref)
     print("wrote", path, "and gptq_tiny_ref.npz", sorted(ref))
+
+    # the reference's own tile dumps of that checkpoint (its main(): plain and scaled forms)
+    env = {"GPTQ_ST": path, "GPTQ_DUMP": os.path.join(here, "gptq_tiny_s4.bin"),
+           "GPTQ_DUMP_SC": os.path.join(here, "gptq_tiny_s4_sc.bin"), "TILE_K": "128", "TILE_N": "64"}
+    old_env = {k: os.environ.get(k) for k in env}
+    os.environ.update(env)
+    try:
+        spec = importlib.util.spec_from_file_location("gptq_s4_dump_main", os.path.join(ref_root, "kernels", "nvfp4",
+                                                                                       "gptq_s4_dump.py"))
+        dump_mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(dump_mod)  # reads the env at import
+        rc = dump_mod.main()
+    finally:
+        for k, v in old_env.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+    print("reference dump main() ->", rc)
 
 
 def tiny_checkpoint_tensors() -> dict:

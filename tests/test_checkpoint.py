@@ -271,3 +271,58 @@ def test_save_nvfp4_layer_inverts_load(tmp_path):
     C.save_safetensors(str(tmp_path / "m.safetensors"), ts)
     t = C.load_nvfp4_tensors(C.Checkpoint(str(tmp_path)), "x")
     assert torch.equal(t.w.t(), lay["weight"])
+
+
+# ---------------------------------------------------------------- reference tile dumps
+def test_reads_the_reference_tile_dumps():
+    """gptq_tiny_s4[_sc].bin were written by the reference's own gptq_s4_dump.py main()
+    from gptq_tiny.safetensors: the codes are its u - 8 and the scaled form carries its
+    group-128 header and first scale row."""
+    import oracle as O
+
+    ck = C.Checkpoint(os.path.join(GOLD, "gptq_tiny.safetensors"))
+    (p,) = C.gptq_prefixes(ck)
+    u = O.unpack_i32_nibbles_first(ck.numpy(p + ".qweight")).astype(np.int16)
+    s4, sc, gs = C.read_s4_dump(os.path.join(GOLD, "gptq_tiny_s4.bin"))
+    assert sc is None and gs is None and s4.shape == (128, 64)
+    assert np.array_equal(s4.astype(np.int16), u - 8)
+    s4b, scb, gsb = C.read_s4_dump(os.path.join(GOLD, "gptq_tiny_s4_sc.bin"))
+    assert gsb == 128 and np.array_equal(s4b, s4)
+    assert np.array_equal(scb, ck.numpy(p + ".scales")[:1])
+
+
+def test_writer_reproduces_the_reference_dumps(tmp_path):
+    s4, _, _ = C.read_s4_dump(os.path.join(GOLD, "gptq_tiny_s4.bin"))
+    _, sc, gs = C.read_s4_dump(os.path.join(GOLD, "gptq_tiny_s4_sc.bin"))
+    C.write_s4_dump(str(tmp_path / "a.bin"), s4)
+    C.write_s4_dump(str(tmp_path / "b.bin"), s4, sc, gs)
+    for mine, ref in (("a.bin", "gptq_tiny_s4.bin"), ("b.bin", "gptq_tiny_s4_sc.bin")):
+        assert (tmp_path / mine).read_bytes() == open(os.path.join(GOLD, ref), "rb").read()
+
+
+def test_dump_as_gptq_tensors_dequantises_to_s4_times_scale():
+    import oracle as O
+
+    rng = np.random.default_rng(7)
+    k, n, gs = 256, 32, 64
+    s4 = rng.integers(-8, 8, size=(k, n)).astype(np.int8)
+    sc = (np.abs(rng.normal(0, 0.02, size=(k // gs, n))) + 1e-3).astype(np.float16)
+    qw, qz, sc2 = C.gptq_tensors_from_s4(s4, sc, gs)
+    assert qw.dtype == np.int32 and qw.shape == (k // 8, n) and qz.shape == (k // gs, n // 8)
+    w = O.gptq_dequant(qw, qz, sc2.view(np.uint16), None, k, n, gs, 1)
+    want = s4.astype(np.float32) * np.repeat(sc.astype(np.float32), gs, axis=0)
+    assert np.array_equal(w, want)
+
+
+def test_dump_format_errors(tmp_path):
+    p = tmp_path / "x.bin"
+    p.write_bytes(struct.pack("<II", 4, 4) + b"\0" * 15)
+    with pytest.raises(C.CheckpointError, match="match neither"):
+        C.read_s4_dump(str(p))
+    p.write_bytes(struct.pack("<II", 2, 2) + bytes([0, 1, 2, 9]))
+    with pytest.raises(C.CheckpointError, match="signed 4-bit"):
+        C.read_s4_dump(str(p))
+    with pytest.raises(C.CheckpointError):
+        C.write_s4_dump(str(p), np.full((2, 2), 9, np.int8))
+    with pytest.raises(C.CheckpointError):
+        C.write_s4_dump(str(p), np.zeros((4, 2), np.int8), np.zeros((3, 2), np.float16), 2)

@@ -458,3 +458,68 @@ def load_nvfp4_linear(ckpt: Checkpoint, prefix: str, cfg: Optional[NVFP4Config] 
 
     t = load_nvfp4_tensors(ckpt, prefix, cfg, device)
     return ops.NVFP4Linear(t.w, t.scale, t.global_scale, t.input_scale, act_mode)
+
+
+# ===================================================================== reference tile dumps
+def read_s4_dump(path: str):
+    """Read a GPTQ weight tile as the reference dumps it (kernels/nvfp4/gptq_s4_dump.py:153-181
+    writes, kernels/esimd_dpas/dpas_s4_gptq_sc.cpp:404-440 reads): ``u32 k, u32 n`` and the
+    int8 codes s4 = u - 8 in [-8, 7], [k, n] row-major; the scaled form adds ``u32 gs``
+    after n and f16 scales [k/gs, n] after the codes.
+    -> (s4 int8 [k, n], scales f16 [k/gs, n] or None, gs or None)."""
+    with open(path, "rb") as f:
+        data = f.read()
+    if len(data) < 8:
+        raise CheckpointError(f"{path}: shorter than the 8-byte header")
+    k, n = struct.unpack_from("<II", data, 0)
+    scales, gs, off = None, None, 8
+    if len(data) != 8 + k * n:
+        if len(data) < 12:
+            raise CheckpointError(f"{path}: {len(data)} bytes do not hold a {k} x {n} tile")
+        (gs,) = struct.unpack_from("<I", data, 8)
+        if gs == 0 or k % gs or len(data) != 12 + k * n + (k // gs) * n * 2:
+            raise CheckpointError(f"{path}: {len(data)} bytes match neither the plain {k} x {n} tile nor "
+                                  f"the tile with group-{gs} scales")
+        off = 12
+        scales = np.frombuffer(data, dtype="<f2", count=(k // gs) * n, offset=12 + k * n).reshape(k // gs, n).copy()
+    s4 = np.frombuffer(data, dtype=np.int8, count=k * n, offset=off).reshape(k, n).copy()
+    if s4.size and (s4.min() < -8 or s4.max() > 7):
+        raise CheckpointError(f"{path}: codes outside the signed 4-bit range")
+    return s4, scales, gs
+
+
+def write_s4_dump(path: str, s4: np.ndarray, scales: Optional[np.ndarray] = None,
+                  group_size: Optional[int] = None) -> None:
+    """Write a tile in the reference's dump format (see read_s4_dump)."""
+    s4 = np.ascontiguousarray(s4, dtype=np.int8)
+    if s4.ndim != 2 or (s4.size and (s4.min() < -8 or s4.max() > 7)):
+        raise CheckpointError("s4 must be a 2-D array of codes in [-8, 7]")
+    k, n = s4.shape
+    with open(path, "wb") as f:
+        if scales is None:
+            f.write(struct.pack("<II", k, n))
+            f.write(s4.tobytes())
+            return
+        sc = np.ascontiguousarray(scales, dtype="<f2")
+        if not group_size or k % group_size or sc.shape != (k // group_size, n):
+            raise CheckpointError(f"scales {sc.shape} do not match a group-{group_size} {k} x {n} tile")
+        f.write(struct.pack("<III", k, n, group_size))
+        f.write(s4.tobytes())
+        f.write(sc.tobytes())
+
+
+def gptq_tensors_from_s4(s4: np.ndarray, scales: np.ndarray, group_size: int):
+    """A dumped tile as GPTQ checkpoint tensors for w4_gptq_gemm: codes u = s4 + 8 packed
+    eight per int32 along K (LSB first), stored zeros 7 (zero 8 under zero_offset 1, the
+    reference's u - 8), the scales unchanged.  -> (qweight i32 [k/8, n], qzeros i32 [k/gs, n/8],
+    scales f16 [k/gs, n])."""
+    s4 = np.asarray(s4, dtype=np.int16)
+    k, n = s4.shape
+    if k % 8 or n % 8 or k % group_size:
+        raise CheckpointError(f"a {k} x {n} tile cannot be packed (k % 8, n % 8, k % group_size)")
+    u = (s4 + 8).astype(np.uint32).reshape(k // 8, 8, n)
+    qw = np.zeros((k // 8, n), dtype=np.uint32)
+    for j in range(8):
+        qw |= u[:, j, :] << np.uint32(4 * j)
+    qz = np.full((k // group_size, n // 8), 0x77777777, dtype=np.uint32)
+    return qw.view(np.int32), qz.view(np.int32), np.ascontiguousarray(scales, dtype="<f2")
