@@ -583,6 +583,12 @@ int gptq_prefill(const void *a, int a_dtype, const int32_t *qweight, const int32
 #undef W4_PF_LAUNCH
 }
 
+int splitk_reduce(const float *partial, int splits, long mn, void *c, int c_dtype, cudaStream_t st) {
+    pf::splitk_reduce_kernel<<<(unsigned)((mn / 4 + 255) / 256), 256, 0, st>>>(partial, splits, mn, c, c_dtype);
+    W4_LAUNCH_CHECK();
+    return W4_OK;
+}
+
 size_t nvfp4_w4a16_prefill_split_bytes(int M, int N, int K, int c_dtype) {
     if (M < kFp4PrefillMinM || !pf::handled(N, K, pf::BK, c_dtype)) return 0;
     const int ks = pf::ksplit_for(M, N, K);

@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 nvfp4_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap w_map,
                      const uint8_t *__restrict__ sfa, const uint8_t *__restrict__ sfb,
                      const float *__restrict__ a_global, const float *__restrict__ w_global, void *__restrict__ C,
-                     int c_dtype, int M, int N, int K) {
+                     int c_dtype, int M, int N, int K, int kb_per_split, float *__restrict__ partial) {
     using C_ = Cfg<BN>;
     constexpr int S = C_::S;
     constexpr uint32_t A_BYTES = C_::A_BYTES, B_BYTES = C_::B_BYTES, A_OFF = C_::A_OFF, B_OFF = C_::B_OFF,
@@ -179,7 +179,10 @@ nvfp4_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_con
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int mt = blockIdx.x, nt = blockIdx.y;
     const int m0 = mt * BM, n0 = nt * BN;
-    const int nk = K / BK;
+    // split-K (grid z): this CTA reduces k-blocks [kb0, kb0 + nk) and, when split,
+    // writes its scaled fp32 partial tile for a second kernel to sum
+    const int kb0 = blockIdx.z * kb_per_split;
+    const int nk = min(kb_per_split, K / BK - kb0);
     const int kchunks = K / 64;
 
     if (threadIdx.x == 0) {
@@ -203,15 +206,16 @@ nvfp4_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_con
             for (int i = 0; i < nk; ++i) {
                 const int s = i % S;
                 if (i >= S && !wait_pf(&empty[s], (uint32_t)(((i / S) - 1) & 1), abort_flag)) break;
+                const int kb = kb0 + i;
                 mbar_arrive_expect_tx(&full[s], tx);
-                tma_load_2d(sm + A_OFF + s * A_BYTES, &a_map, i * (BK / 2), m0, &full[s]);
-                tma_load_2d(sm + B_OFF + s * B_BYTES, &w_map, i * (BK / 2), n0, &full[s]);
-                bulk_load(sm + SFA_OFF + s * SFA_BYTES, sfa + ((size_t)mt * kchunks + 4 * i) * SF_ATOM, SFA_BYTES,
+                tma_load_2d(sm + A_OFF + s * A_BYTES, &a_map, kb * (BK / 2), m0, &full[s]);
+                tma_load_2d(sm + B_OFF + s * B_BYTES, &w_map, kb * (BK / 2), n0, &full[s]);
+                bulk_load(sm + SFA_OFF + s * SFA_BYTES, sfa + ((size_t)mt * kchunks + 4 * kb) * SF_ATOM, SFA_BYTES,
                           &full[s]);
 #pragma unroll
                 for (int h = 0; h < C_::NH; ++h)  // the 128-row halves' atoms sit in separate row tiles
                     bulk_load(sm + SFB_OFF + s * SFB_BYTES + h * 4 * SF_ATOM,
-                              sfb + ((size_t)(nt * C_::NH + h) * kchunks + 4 * i) * SF_ATOM, 4 * SF_ATOM, &full[s]);
+                              sfb + ((size_t)(nt * C_::NH + h) * kchunks + 4 * kb) * SF_ATOM, 4 * SF_ATOM, &full[s]);
             }
         }
     } else if (warp == 1) {
@@ -257,8 +261,9 @@ nvfp4_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_con
             tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
             if (row < M) {
                 const size_t base = (size_t)row * N + n0 + c0;
-                if (c_dtype == W4_F32) {
-                    float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(C) + base);
+                if (partial || c_dtype == W4_F32) {
+                    float4 *dst = reinterpret_cast<float4 *>(partial ? partial + (size_t)blockIdx.z * M * N + base
+                                                                     : static_cast<float *>(C) + base);
 #pragma unroll
                     for (int e = 0; e < 8; ++e)
                         dst[e] = make_float4(__uint_as_float(v[4 * e]) * gs, __uint_as_float(v[4 * e + 1]) * gs,
@@ -502,7 +507,7 @@ namespace fp4pf {
 template <int BN>
 static int launch(const CUtensorMap &a_map, const CUtensorMap &w_map, const uint8_t *sfa, const uint8_t *sfb,
                   const float *a_global, const float *w_global, void *c, int c_dtype, int M, int N, int K,
-                  cudaStream_t st) {
+                  int ksplit, float *partial, cudaStream_t st) {
     const size_t smem = Cfg<BN>::SMEM + 1024;
     auto kern = nvfp4_prefill_kernel<BN>;
     {
@@ -516,10 +521,29 @@ static int launch(const CUtensorMap &a_map, const CUtensorMap &w_map, const uint
             set_dev[dev] = true;
         }
     }
-    dim3 grid((M + BM - 1) / BM, N / BN), block(kThreads);
-    kern<<<grid, block, smem, st>>>(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K);
+    const int nk = K / BK;
+    const int kb_per_split = (nk + ksplit - 1) / ksplit;
+    ksplit = (nk + kb_per_split - 1) / kb_per_split;  // every split gets at least one k-block
+    dim3 grid((M + BM - 1) / BM, N / BN, ksplit), block(kThreads);
+    kern<<<grid, block, smem, st>>>(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K, kb_per_split,
+                                    ksplit > 1 ? partial : nullptr);
     W4_LAUNCH_CHECK();
+    if (ksplit > 1) return splitk_reduce(partial, ksplit, (long)M * N, c, c_dtype, st);  // N % 128 == 0
     return W4_OK;
+}
+
+// K splits for grids that fill at most half the SMs (the non-persistent form):
+// up to one wave, at least two k-blocks per split, at most 4 (each split adds an
+// M x N fp32 partial to write and read back).
+static int ksplit_for(int M, int N, int K) {
+    const bool wide = N % 256 == 0;
+    const long tiles = (long)((M + BM - 1) / BM) * (N / (wide ? 256 : 128));
+    const long nsm = num_sms();
+    if (2 * tiles > nsm) return 1;
+    long ks = nsm / tiles;
+    if (ks > (K / BK) / 2) ks = (K / BK) / 2;
+    if (ks > 4) ks = 4;
+    return ks < 1 ? 1 : (int)ks;
 }
 }  // namespace fp4pf
 
@@ -548,9 +572,15 @@ static int launch_persistent(const CUtensorMap &a_map, const CUtensorMap &w_map,
 }
 }  // namespace fp4pf
 
+static size_t split_bytes(int M, int N, int K) {
+    if (K % fp4pf::BK || N % 128) return 0;
+    const int ks = fp4pf::ksplit_for(M, N, K);
+    return ks > 1 ? align256((size_t)ks * M * N * sizeof(float)) : 0;
+}
+
 size_t nvfp4_prefill_workspace(int M, int N, int K) {
     const size_t mp = (size_t)(M + 127) / 128 * 128, np = (size_t)(N + 127) / 128 * 128;
-    return align256(mp * K / 2) + align256(mp * (K / 16)) + align256(np * (K / 16));
+    return align256(mp * K / 2) + align256(mp * (K / 16)) + align256(np * (K / 16)) + split_bytes(M, N, K);
 }
 
 // The block-scaled GEMM on activations already quantised: codes u8 [rows, K/2]
@@ -564,12 +594,15 @@ int nvfp4_prefill_q(const uint8_t *codes, const uint8_t *sfa, const float *a_glo
     if (K % BK || N % 128 || c_dtype == W4_E4M3) return -1;
     const size_t mp = (size_t)(M + 127) / 128 * 128;
     const uint8_t *sfb = w_sf;
+    char *wsb = static_cast<char *>(workspace);
     if (!w_sf_atoms) {
-        uint8_t *t = static_cast<uint8_t *>(workspace);
+        uint8_t *t = reinterpret_cast<uint8_t *>(wsb);
         const int rc = nvfp4_sf_atoms(w_sf, N, K / 16, 1, N, t, st);
         if (rc) return rc;
         sfb = t;
+        wsb += align256((size_t)(N + 127) / 128 * 128 * (K / 16));
     }
+    float *partial = reinterpret_cast<float *>(wsb);  // split-K partials (split_bytes)
     CUtensorMap a_map, w_map;
     // 256-wide tiles: persistent when there are more tiles than SMs, one tile per
     // CTA otherwise; 128-wide tiles when N is not a multiple of 256.
@@ -583,13 +616,14 @@ int nvfp4_prefill_q(const uint8_t *codes, const uint8_t *sfa, const float *a_glo
                      CU_TENSOR_MAP_SWIZZLE_128B))
         return -1;
     if (persistent) return launch_persistent(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K, st);
-    return wide ? launch<256>(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K, st)
-                : launch<128>(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K, st);
+    const int ks = workspace ? ksplit_for(M, N, K) : 1;
+    return wide ? launch<256>(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K, ks, partial, st)
+                : launch<128>(a_map, w_map, sfa, sfb, a_global, w_global, c, c_dtype, M, N, K, ks, partial, st);
 }
 
-size_t nvfp4_prefill_q_workspace(int N, int K) {
+size_t nvfp4_prefill_q_workspace(int M, int N, int K, bool scale_atoms_needed) {
     const size_t np = (size_t)(N + 127) / 128 * 128;
-    return align256(np * (K / 16));
+    return (scale_atoms_needed ? align256(np * (K / 16)) : 0) + split_bytes(M, N, K);
 }
 
 // A bf16 [M,K] -> NVFP4 codes + scale atoms in the workspace, then nvfp4_prefill_q.

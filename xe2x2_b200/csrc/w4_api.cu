@@ -341,7 +341,7 @@ int w4_rmsnorm_quant_nvfp4(const void *x, int x_dtype, const void *gamma, float 
 
 size_t w4_nvfp4_gemm_q_workspace_bytes(int M, int N, int K, int scale_dtype, int c_dtype) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
-    size_t ws = scale_dtype == W4_E4M3 ? w4::nvfp4_prefill_q_workspace(N, K) : 0;
+    size_t ws = w4::nvfp4_prefill_q_workspace(M, N, K, scale_dtype == W4_E4M3);
     if (c_dtype == W4_E4M3) ws += align256((size_t)M * N * 4);
     return ws;
 }

@@ -95,7 +95,9 @@ int rmsnorm_nvfp4(const void *x, int x_dtype, const void *gamma, float eps, cons
 int nvfp4_prefill_q(const uint8_t *codes, const uint8_t *sfa, const float *a_global, const uint8_t *w_nk,
                     const uint8_t *w_sf, bool w_sf_atoms, const float *w_global, void *c, int c_dtype, int M, int N,
                     int K, void *workspace, cudaStream_t st);
-size_t nvfp4_prefill_q_workspace(int N, int K);
+size_t nvfp4_prefill_q_workspace(int M, int N, int K, bool scale_atoms_needed);
+// C = sum over splits of the fp32 partials [splits][mn] (mn % 4 == 0), in c_dtype (gptq_prefill.cu).
+int splitk_reduce(const float *partial, int splits, long mn, void *c, int c_dtype, cudaStream_t st);
 int rowscale_fp8(const void *y, int y_dtype, uint8_t *q, float *row_scale, int M, int N,
                  cudaStream_t st);
 
