@@ -113,3 +113,45 @@ def test_dense_layer_shapes_shard_at_tp8():
                 assert n % 8 == 0 and (n // 8) % 8 == 0 and (n // 8) % 32 == 0
         else:
             assert p.K % (8 * 128) == 0
+
+
+# ---------------------------------------------------------------- NVFP4 shards
+def _fp4_oracle(x, w, scale, gscale):
+    K, N = w.shape[0] * 2, w.shape[1]
+    return O.nvfp4_gemm(x.float().numpy(), w.contiguous().numpy(), O.NVFP4_KN, scale.view(torch.uint8).numpy(),
+                        O.SCALE_E4M3, float(gscale), x.shape[0], N, K, threads=1)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_nvfp4_shards_reproduce_unsharded_layer(world):
+    """NVFP4 column shards (q|k|v splits) concatenate to the full product bit for bit; row
+    shards (K split on whole 256-k blocks, scale rows following) sum to it within fp32
+    rounding; the shards keep the operator layout (stride(0) == 1)."""
+    M, K = 3, 1024
+    splits = (256, 128, 128)
+    N = sum(splits)
+    w, scale, gscale = synth.nvfp4_weights(K, N, seed=11)
+    x = synth.activations(M, K, torch.bfloat16, seed=12)
+    full = _fp4_oracle(x, w, scale, gscale)
+    parts = []
+    for rank in range(world):
+        ws, sc = tp.shard_nvfp4_columns(w, scale, rank, world, splits)
+        assert ws.stride(0) == 1 and ws.shape == (K // 2, N // world) and sc.shape == (K // 16, N // world)
+        got = _fp4_oracle(x, ws, sc, gscale)
+        want = np.concatenate([full[:, s] for s in tp.column_slices(splits, rank, world)], axis=1)
+        assert np.array_equal(got, want)
+        wr, sr = tp.shard_nvfp4_rows(w, scale, rank, world)
+        assert wr.stride(0) == 1 and wr.shape == (K // world // 2, N) and sr.shape == (K // world // 16, N)
+        parts.append(_fp4_oracle(x[:, tp.row_input_slice(K, rank, world)].contiguous(), wr, sr, gscale))
+    total = np.sum(np.stack(parts), axis=0, dtype=np.float32)
+    assert float(np.linalg.norm(total - full) / np.linalg.norm(full)) < 1e-6
+
+
+def test_nvfp4_shard_helpers_reject_bad_layouts():
+    w, scale, _ = synth.nvfp4_weights(512, 128, seed=1)
+    with pytest.raises(ValueError, match="stride"):
+        tp.shard_nvfp4_columns(w.contiguous(), scale, 0, 2)  # [K/2, N] row-major is not the operator view
+    with pytest.raises(ValueError, match="multiple of 256"):
+        tp.shard_nvfp4_rows(w, scale, 0, 4)  # 512 / 4 = 128 k per shard
+    with pytest.raises(ValueError):
+        tp.TPLinearNVFP4(None, "row", w, scale, torch.ones(1))

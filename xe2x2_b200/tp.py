@@ -1,4 +1,4 @@
-"""Tensor-parallel GPTQ linear layers: one process per GPU.
+"""Tensor-parallel GPTQ and NVFP4 linear layers: one process per GPU.
 
 Column-parallel layers (QKV, gate|up) keep ``N/world`` output columns of every
 sub-matrix (head-aligned: rank r holds its q heads, its k heads and its v
@@ -76,6 +76,41 @@ def shard_rows(qweight, qzeros, scales, rank: int, world: int, group_size: int):
 def row_input_slice(K: int, rank: int, world: int) -> slice:
     """Columns of the layer input that the rank's row shard consumes."""
     return slice(rank * K // world, (rank + 1) * K // world)
+
+
+def _nvfp4_nk(w):
+    """The [N, K/2] K-contiguous codes behind an operator-layout w ([K/2, N], stride(0) == 1)."""
+    if w.dim() != 2 or w.stride(0) != 1:
+        raise ValueError("w must be the [K/2, N] view of [N, K/2] memory (stride(0) == 1)")
+    return w.t()
+
+
+def shard_nvfp4_columns(w, scale, rank: int, world: int, splits=None):
+    """Column-parallel shard of an NVFP4 matrix: codes w [K/2, N] (operator layout, stride(0)
+    == 1) and block scales [K/16, N]; ``splits`` as in shard_columns.  The codes keep their
+    K-contiguous memory, so the shard is again an operator-layout view."""
+    N = w.shape[1]
+    splits = list(splits) if splits else [N]
+    if sum(splits) != N:
+        raise ValueError(f"splits {splits} do not add up to N={N}")
+    rng = _column_ranges(splits, rank, world)
+    w_nk = _nvfp4_nk(w)
+    ws = torch.cat([w_nk[a:b] for a, b in rng], dim=0).contiguous().t()
+    sc = torch.cat([scale[:, a:b] for a, b in rng], dim=1).contiguous()
+    return ws, sc
+
+
+def shard_nvfp4_rows(w, scale, rank: int, world: int, k_multiple: int = 256):
+    """Row-parallel shard of an NVFP4 matrix: K/world input rows, a multiple of ``k_multiple``
+    (16 keeps whole scale blocks; 256 keeps the block-scaled tensor-core path)."""
+    K = w.shape[0] * 2
+    if K % (world * k_multiple):
+        raise ValueError(f"K={K} does not split into {world} shards of a multiple of {k_multiple}")
+    kr = K // world
+    k0 = rank * kr
+    ws = _nvfp4_nk(w)[:, k0 // 2:(k0 + kr) // 2].contiguous().t()
+    sc = scale[k0 // 16:(k0 + kr) // 16].contiguous()
+    return ws, sc
 
 
 # ------------------------------------------------------------------ communicator
@@ -171,6 +206,31 @@ class TPLinear:
                ops._p(self.scales), None, ops._p(c), ops._DT[out_dtype], ops._p(rs), M, self.N, K,
                self.group_size, self.zero_offset, ops._p(ws), wsb, ops._stream(a.device))
         return (c, rs) if rs is not None else c
+
+
+class TPLinearNVFP4:
+    """One rank's shard of an NVFP4 linear layer (``mode`` "column" or "row"), bf16
+    activations (W4A16) or NVFP4 activations (``act_mode`` W4_ACT_NVFP4 with the layer's
+    ``a_global``).  Row-parallel outputs are summed in place with the communicator's
+    all-reduce on the GEMM's stream (f32 / bf16 / f16 outputs)."""
+
+    def __init__(self, comm: TPComm | None, mode: str, w, scale, global_scale, act_mode=None, a_global=None):
+        if mode not in ("column", "row"):
+            raise ValueError("mode must be 'column' or 'row'")
+        if mode == "row" and comm is None:
+            raise ValueError("a row-parallel layer needs a communicator")
+        self.comm, self.mode = comm, mode
+        self.w, self.scale, self.global_scale = w, scale, global_scale
+        self.act_mode = L.W4_ACT_W4A16 if act_mode is None else act_mode
+        self.a_global = a_global
+
+    def __call__(self, x, out_dtype=torch.bfloat16):
+        if out_dtype == torch.float8_e4m3fn:
+            raise ValueError("fp8 row-scaled outputs need the full sum first: reduce in f32, then ops.rowscale_fp8")
+        y = ops.nvfp4_gemm(x, self.w, self.scale, self.global_scale, out_dtype, self.act_mode, self.a_global)
+        if self.mode == "row":
+            self.comm.allreduce_(y)
+        return y
 
 
 @dataclass(frozen=True)
