@@ -10,6 +10,12 @@
  *     enqueued asynchronously; the call returns once it is launched.
  *   - Nothing is allocated inside a call.  Scratch space, where needed, is the
  *     caller's `workspace` buffer, sized by the matching *_workspace_bytes().
+ *     Every workspace begins with a sync area of W4_WORKSPACE_SYNC_BYTES bytes
+ *     (counters of the decode GEMMs' K split).  It must be all zero before the
+ *     workspace is first used; every call that completes leaves it zero, so a
+ *     workspace zeroed once stays usable for any later call.  After a call
+ *     whose kernel reported W4_ERR_TIMEOUT (w4_check_device_status), zero it
+ *     again.
  *   - Argument errors are reported synchronously (W4_ERR_INVALID /
  *     W4_ERR_UNSUPPORTED) before anything is launched; launch failures are
  *     W4_ERR_CUDA.  w4_last_error() gives a one-line reason (thread-local).
@@ -31,6 +37,9 @@
 #ifdef __cplusplus
 extern "C" {
 #endif
+
+/* Size of the zero-initialised sync area at the start of every workspace. */
+#define W4_WORKSPACE_SYNC_BYTES 16384
 
 #define W4_ABI_VERSION 1
 
@@ -102,6 +111,13 @@ enum w4_overlap {
 int w4_set_launch_overlap(int mode);
 int w4_get_launch_overlap(void);
 
+/* Number of decode GEMM calls (GPTQ or NVFP4 W4A16, M <= 16) made by this process that
+ * ran a register-streamed fallback kernel because none of the TMA-streamed decode kernels
+ * takes the shape (for example a column count that is not a multiple of 32 for the NVFP4
+ * decode kernel).  Those run correctly but 2-3x slower; benchmarks and tests assert the
+ * count stays 0 on the shapes they measure.  No counterpart in the reference. */
+unsigned long long w4_decode_fallback_count(void);
+
 /* ===================================================================== */
 /* GPTQ int4                                                              */
 /* ===================================================================== */
@@ -125,7 +141,11 @@ int w4_gptq_repack_act_order(const int32_t *qweight, const int32_t *g_idx, int K
                              int group_size, int32_t *qweight_out, int32_t *perm_out,
                              void *stream);
 
-/* Workspace needed by w4_gptq_gemm for these arguments (0 if none). */
+/* Workspace needed by w4_gptq_gemm for these arguments: the sync area, plus the
+ * gathered activations (act_order), the f32 product (W4_E4M3 output) and the
+ * K-split partials.  At decode sizes (M <= 16) a workspace smaller than this
+ * still works if it holds the sync area: the GEMM then runs without a K split
+ * (correct, slower on narrow layers). */
 size_t w4_gptq_workspace_bytes(int M, int N, int K, int group_size, int has_perm, int c_dtype);
 
 /* W4A16 GPTQ GEMM:  C[m,n] = sum_k A[m,k'] * w[k,n]   (fp32 accumulate)

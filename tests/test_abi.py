@@ -63,10 +63,17 @@ def test_gptq_gemm_rejects_bad_arguments_without_gpu():
 
 def test_workspace_sizes():
     lib = L.lib()
-    assert lib.w4_gptq_workspace_bytes(16, 4096, 4096, 128, 0, L.W4_F16) == 0
-    assert lib.w4_gptq_workspace_bytes(16, 4096, 4096, 128, 1, L.W4_F16) >= 16 * 4096 * 2
-    assert lib.w4_gptq_workspace_bytes(16, 4096, 4096, 128, 0, L.W4_E4M3) >= 16 * 4096 * 4
-    assert lib.w4_nvfp4_workspace_bytes(8, 5120, 5120, L.W4_ACT_W4A16, L.W4_BF16) == 0  # decode GEMV
+    sync = L.W4_WORKSPACE_SYNC_BYTES
+    assert f"#define W4_WORKSPACE_SYNC_BYTES {sync}" in open(L.HEADER).read()
+    # every workspace starts with the zeroed sync area
+    assert lib.w4_gptq_workspace_bytes(16, 4096, 4096, 128, 0, L.W4_F16) >= sync
+    assert lib.w4_gptq_workspace_bytes(16, 4096, 4096, 128, 1, L.W4_F16) >= sync + 16 * 4096 * 2
+    assert lib.w4_gptq_workspace_bytes(16, 4096, 4096, 128, 0, L.W4_E4M3) >= sync + 16 * 4096 * 4
+    assert lib.w4_nvfp4_workspace_bytes(8, 5120, 5120, L.W4_ACT_W4A16, L.W4_BF16) == sync  # decode GEMV
+    assert lib.w4_nvfp4_gemm_q_workspace_bytes(128, 256, 256, L.W4_E4M3_ATOMS, L.W4_BF16) >= sync
+    # the decode GEMM's K-split partials (4-column tiles too few for the SMs): config 1 shape
+    dec = lib.w4_gptq_workspace_bytes(16, 4096, 4096, 128, 0, L.W4_F16) - sync
+    assert dec >= 2 * 16 * 4096 * 4 and dec % 256 == 0
     # from 9 tokens the W4A16 tensor-core GEMM splits K over CTAs for few output tiles
     assert lib.w4_nvfp4_workspace_bytes(16, 5120, 5120, L.W4_ACT_W4A16, L.W4_BF16) % 256 == 0
 

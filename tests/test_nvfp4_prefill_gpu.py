@@ -96,7 +96,7 @@ def test_scale_atoms_cached_and_equivalent(cuda):
     # the raw [K/16, N] scales through the C ABI (rearranged per call in the workspace)
     c = torch.empty((M, N), dtype=torch.float32, device=cuda)
     need = L.lib().w4_nvfp4_workspace_bytes(M, N, K, L.W4_ACT_NVFP4, L.W4_F32)
-    ws = torch.empty(need, dtype=torch.uint8, device=cuda)
+    ws = torch.zeros(need, dtype=torch.uint8, device=cuda)  # the sync area starts zeroed
     L.call("w4_nvfp4_gemm", ops._p(x), ops._p(w), L.W4_NVFP4_NK, ops._p(scale), L.W4_E4M3, ops._p(gscale),
            L.W4_ACT_NVFP4, ops._p(ag), ops._p(c), L.W4_F32, None, M, N, K, ops._p(ws), need, ops._stream(x.device))
     assert torch.equal(y1, c)

@@ -53,5 +53,10 @@ def test_mbarrier_try_wait_only_inside_bounded_helpers():
         for m in re.finditer(r"while\s*\(\s*!\s*mbar_try_wait\([^)]*\)\s*\)", text):
             body = text[m.end():m.end() + 400]
             uses.append((os.path.basename(p), "global_ns" in body or "abort_flag" in body))
+        # the suspending form: the loop that calls it reads the global timer and gives up
+        for m in re.finditer(r"for\s*\(\s*;\s*;\s*\)\s*\{", text):
+            body = text[m.end():m.end() + 400]
+            if "mbar_try_wait_suspend(" in body:
+                uses.append((os.path.basename(p), "global_ns" in body and "return false" in body))
     assert uses, "expected bounded waits built on mbar_try_wait"
     assert all(ok for _, ok in uses), uses

@@ -2,11 +2,14 @@
 NCCL communicator against the unsharded single-GPU GEMM, the collective's
 identity check (parallel/tp2/bench_xccl_p2p0.py:235-245: ranks add r+1), and
 the bounded waits: a rank that never joins the communicator, or never reaches
-a collective, makes the other rank's call return W4_ERR_TIMEOUT.
+a collective, makes the other rank's call return W4_ERR_TIMEOUT.  The NVFP4
+layers (TPLinearNVFP4, bf16 and NVFP4 activations) against the unsharded
+NVFP4 GEMM.
 
 Each case runs as child processes (one per GPU) bootstrapped over gloo, with
 NVLS off (NCCL_NVLS_ENABLE=0).  A rank leaves only between steps, with
-nothing of its own in flight.  Skipped with fewer than 2 GPUs.
+nothing of its own in flight.  The layer cases run at 2 ranks and at
+min(4, GPU count) ranks; everything is skipped with fewer than 2 GPUs.
 """
 import os
 import socket
@@ -248,6 +251,42 @@ def _case_collective_timeout(rank, world):
         comm.abort()
 
 
+def _case_nvfp4_layers(rank, world):
+    """TPLinearNVFP4 column and row shards (bf16 activations, and NVFP4 activations with the
+    layer's tensor scale) against the unsharded NVFP4 GEMM on the same inputs."""
+    from xe2x2_b200 import _lib as L, ops, synth, tp
+
+    dev = torch.device("cuda", rank)
+    comm = tp.TPComm(rank, world, timeout_ms=60000, device=dev)
+    try:
+        K, N = 2048, 1536
+        splits = (1024, 256, 256)
+        w, scale, gscale = synth.nvfp4_weights(K, N, seed=21, device=dev)
+        for M in (1, 16, 256):
+            x = synth.activations(M, K, torch.bfloat16, seed=M, device=dev)
+            ag = torch.tensor([float(x.float().abs().max()) / (448.0 * 6.0)], device=dev)
+            for act_mode, a_global, tol in ((L.W4_ACT_W4A16, None, 1e-5), (L.W4_ACT_NVFP4, ag, 1e-5)):
+                full = ops.nvfp4_gemm(x, w, scale, gscale, torch.float32, act_mode, a_global)
+                ws, sc = tp.shard_nvfp4_columns(w, scale, rank, world, splits)
+                col = tp.TPLinearNVFP4(comm, "column", ws, sc, gscale, act_mode, a_global)
+                got = col(x, out_dtype=torch.float32)
+                want = torch.cat([full[:, s] for s in tp.column_slices(splits, rank, world)], dim=1)
+                assert _rel(got, want) < tol, (M, act_mode)
+                wr, sr = tp.shard_nvfp4_rows(w, scale, rank, world)
+                row = tp.TPLinearNVFP4(comm, "row", wr, sr, gscale, act_mode, a_global)
+                xs = x[:, tp.row_input_slice(K, rank, world)].contiguous()
+                got = row(xs, out_dtype=torch.float32)
+                b16 = row(xs, out_dtype=torch.bfloat16)
+                comm.wait()
+                # NVFP4 activations: the shard quantises its own K slice with the same global scale
+                # and 16-element blocks, so the codes match the unsharded quantiser's
+                assert _rel(got, full) < 1e-5, (M, act_mode)
+                assert _rel(b16, full) < 1e-2, (M, act_mode)
+        assert L.lib().w4_check_device_status() == L.W4_OK
+    finally:
+        comm.close()
+
+
 def _child(rank, world, port, case, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import datetime
@@ -265,20 +304,20 @@ def _child(rank, world, port, case, q):
         dist.destroy_process_group()
 
 
-def _run(case):
-    if torch.cuda.device_count() < WORLD:
-        pytest.skip(f"needs {WORLD} GPUs")
+def _run(case, world=WORLD):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_child, args=(r, WORLD, port, case, q)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_child, args=(r, world, port, case, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
     try:
-        for _ in range(WORLD):
+        for _ in range(world):
             r, v = q.get(timeout=300)
             res[r] = v
     finally:
@@ -286,15 +325,27 @@ def _run(case):
             p.join(timeout=60)
             if p.is_alive():
                 p.kill()
-    assert res == {r: "ok" for r in range(WORLD)}, res
+    assert res == {r: "ok" for r in range(world)}, res
 
 
-def test_tp_layers_match_unsharded():
-    _run("_case_layers")
+def _worlds():
+    n = torch.cuda.device_count() if torch.cuda.is_available() else 0
+    return sorted({2, max(2, min(4, n))})
 
 
-def test_tp_fused_row_parallel_epilogue():
-    _run("_case_fused_row_parallel")
+@pytest.mark.parametrize("world", _worlds())
+def test_tp_layers_match_unsharded(world):
+    _run("_case_layers", world)
+
+
+@pytest.mark.parametrize("world", _worlds())
+def test_tp_fused_row_parallel_epilogue(world):
+    _run("_case_fused_row_parallel", world)
+
+
+@pytest.mark.parametrize("world", _worlds())
+def test_tp_nvfp4_layers_match_unsharded(world):
+    _run("_case_nvfp4_layers", world)
 
 
 def test_tp_fused_epilogue_timeout_when_a_rank_skips():

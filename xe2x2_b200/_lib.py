@@ -20,6 +20,7 @@ W4_ACT_W4A16, W4_ACT_NVFP4 = 0, 1
 W4_TP_COLUMN, W4_TP_ROW = 0, 1
 W4_OVERLAP_OFF, W4_OVERLAP_DEPENDENT, W4_OVERLAP_STATIC_WEIGHTS = 0, 1, 2
 W4_TP_UNIQUE_ID_BYTES = 128
+W4_WORKSPACE_SYNC_BYTES = 16384  # zeroed sync area at the start of every workspace
 
 HEADER = os.path.join(os.path.dirname(_build.HERE), "include", "w4.h")
 
@@ -42,6 +43,7 @@ _SIGS = {
     "w4_check_device_status": (_I, []),
     "w4_set_launch_overlap": (_I, [_I]),
     "w4_get_launch_overlap": (_I, []),
+    "w4_decode_fallback_count": (ctypes.c_ulonglong, []),
     "w4_gptq_dequant": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "w4_gptq_repack_act_order": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
     "w4_gptq_workspace_bytes": (_Z, [_I, _I, _I, _I, _I, _I]),

@@ -373,17 +373,19 @@ static int launch_gemv(const void *a, const int32_t *qweight, const int32_t *qze
 
 int gptq_gemv(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
               const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs,
-              int zero_offset, void *ws, size_t ws_bytes, cudaStream_t st) {
-    // Prefill-sized token counts: the tcgen05 GEMM (gptq_prefill.cu).  Decode:
-    // the TMA-streamed kernel (gptq_tma.cu); the register-batched kernel below
-    // runs only for shapes neither handles.
+              int zero_offset, void *sync, void *ws, size_t ws_bytes, cudaStream_t st) {
+    // Prefill-sized token counts: the tcgen05 GEMM (gptq_prefill.cu).  Decode: the
+    // shared-ring TMA kernel (gptq_decode.cu); the register-batched kernel below runs only
+    // for shapes it does not take, and every such call is counted (w4_decode_fallback_count).
     if (M >= kPrefillMinM) {
         const int rp = gptq_prefill(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ws,
                                     ws_bytes, st);
         if (rp >= 0) return rp;
     }
-    const int rc = gptq_gemv_tma(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+    const int rc = gptq_gemv_decode(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, sync,
+                                    ws, ws_bytes, st);
     if (rc >= 0) return rc;
+    note_decode_fallback();
     if (a_dtype == W4_BF16)
         return launch_gemv<__nv_bfloat16>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
     return launch_gemv<__half>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);

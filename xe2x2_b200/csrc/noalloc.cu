@@ -73,7 +73,7 @@ extern "C" int w4_gptq_gemm_fp8_noalloc(const void *a, int a_dtype, const int32_
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     rc = w4::gptq_gemv(a, a_dtype, qweight, qzeros, scales, y, W4_F32, M, N, K, group_size,
-                       zero_offset, nullptr, 0, st);  // no scratch for split-K: unsplit
+                       zero_offset, nullptr, nullptr, 0, st);  // no scratch for split-K: unsplit
     if (rc) return rc;
     return w4::rowscale_fp8(y, W4_F32, q_out, row_scale, M, N, st);
 }

@@ -663,6 +663,7 @@ int nvfp4_gemv(const uint16_t *a, const uint8_t *w, int layout, const void *scal
     // covers shapes it does not take.
     const int rc = nvfp4_gemv_tma(a, w, scale, scale_dtype, global_scale, c, c_dtype, M, N, K, st);
     if (rc >= 0) return rc;
+    note_decode_fallback();
     if (scale_dtype == W4_E4M3) {
         if (M <= 8) return launch_nvfp4_gemv_t<1, W4_E4M3>(a, w, scale, global_scale, c, c_dtype, M, N, K, st);
         if (M <= 16) return launch_nvfp4_gemv_t<2, W4_E4M3>(a, w, scale, global_scale, c, c_dtype, M, N, K, st);

@@ -45,14 +45,31 @@ __device__ __forceinline__ unsigned long long global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-// Wait for the phase with the given parity; false if kWaitLimitNs passed first.
+// try_wait that lets the hardware suspend the thread for up to kSuspendNs while the phase
+// is incomplete (it resumes as soon as the phase completes), so a waiting warp issues few
+// instructions and leaves the issue slots to the warps that compute.
+constexpr uint32_t kSuspendNs = 20000;
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\nselp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity), "r"(kSuspendNs)
+        : "memory");
+    return done != 0;
+}
+// Wait for the phase with the given parity; false if kWaitLimitNs passed first.  The clock is
+// read once per 16 suspending tries.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
     const uint32_t b = smem_u32(bar);
     if (mbar_try_wait(b, parity)) return true;
     const unsigned long long t0 = global_ns();
-    while (!mbar_try_wait(b, parity))
+    for (;;) {
+#pragma unroll 1
+        for (int i = 0; i < 16; ++i)
+            if (mbar_try_wait_suspend(b, parity)) return true;
         if (global_ns() - t0 > kWaitLimitNs) return false;
-    return true;
+    }
 }
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
                                             uint64_t *bar) {

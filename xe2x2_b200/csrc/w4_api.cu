@@ -42,6 +42,9 @@ int num_sms() {
 static std::atomic<int> g_overlap{W4_OVERLAP_DEPENDENT};
 int launch_overlap() { return g_overlap.load(std::memory_order_relaxed); }
 
+static std::atomic<unsigned long long> g_decode_fallbacks{0};
+void note_decode_fallback() { g_decode_fallbacks.fetch_add(1, std::memory_order_relaxed); }
+
 int nvfp4_kn_to_nk(const uint8_t *in, int K, int N, uint8_t *out, cudaStream_t st);
 
 }  // namespace w4
@@ -63,6 +66,10 @@ int w4_set_launch_overlap(int mode) {
 }
 
 int w4_get_launch_overlap(void) { return w4::launch_overlap(); }
+
+unsigned long long w4_decode_fallback_count(void) {
+    return w4::g_decode_fallbacks.load(std::memory_order_relaxed);
+}
 
 const char *w4_status_string(int status) {
     switch (status) {
@@ -87,7 +94,8 @@ int w4_check_device_status(void) {
     const int r5 = w4::take_tp_wait_status();
     const int r6 = w4::take_tp_fused_wait_status();
     const int r7 = w4::take_rn_wait_status();
-    return r1 ? r1 : r2 ? r2 : r3 ? r3 : r4 ? r4 : r5 ? r5 : r6 ? r6 : r7;
+    const int r8 = w4::take_decode_wait_status();
+    return r1 ? r1 : r2 ? r2 : r3 ? r3 : r4 ? r4 : r5 ? r5 : r6 ? r6 : r7 ? r7 : r8;
 }
 
 // ------------------------------------------------------------------ GPTQ
@@ -123,14 +131,20 @@ int w4_gptq_repack_act_order(const int32_t *qweight, const int32_t *g_idx, int K
     return w4::gptq_repack_act_order(qweight, g_idx, K, N, group_size, qweight_out, perm_out, S(stream));
 }
 
+// Workspace of w4_gptq_gemm: sync area | gathered activations (act_order) | f32 product
+// (e4m3 output) | K-split partials (tensor-core GEMM or decode GEMM).
+static size_t gptq_split_bytes(int M, int N, int K, int group_size, int c_dtype) {
+    const size_t pf = w4::gptq_prefill_split_bytes(M, N, K, group_size, c_dtype == W4_E4M3 ? W4_F32 : c_dtype);
+    const size_t dc = w4::gptq_decode_split_bytes(M, N, K, group_size);
+    return pf > dc ? pf : dc;
+}
+
 size_t w4_gptq_workspace_bytes(int M, int N, int K, int group_size, int has_perm, int c_dtype) {
-    (void)group_size;
-    size_t ws = 0;
     if (M <= 0 || N <= 0 || K <= 0) return 0;
+    size_t ws = W4_WORKSPACE_SYNC_BYTES;
     if (has_perm) ws += align256((size_t)M * K * 2);
     if (c_dtype == W4_E4M3) ws += align256((size_t)M * N * 4);
-    // split-K partials of the tensor-core GEMM (the f32 product when the output is e4m3)
-    ws += align256(w4::gptq_prefill_split_bytes(M, N, K, group_size, c_dtype == W4_E4M3 ? W4_F32 : c_dtype));
+    ws += align256(gptq_split_bytes(M, N, K, group_size, c_dtype));
     return ws;
 }
 
@@ -169,10 +183,15 @@ int w4_gptq_gemm(const void *a, int a_dtype, const int32_t *qweight, const int32
     int rc = w4::check_gptq_gemm(a, a_dtype, qweight, scales, c, c_dtype, row_scale, M, N, K, group_size);
     if (rc) return rc;
     const size_t need = w4_gptq_workspace_bytes(M, N, K, group_size, perm != nullptr, c_dtype);
-    W4_REQUIRE(workspace_bytes >= need && (need == 0 || workspace), W4_ERR_INVALID,
-               "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+    const size_t split = align256(gptq_split_bytes(M, N, K, group_size, c_dtype));
+    // At decode sizes the K-split partials are optional: without them the GEMM runs unsplit.
+    const size_t least = M <= 16 ? need - split : need;
+    W4_REQUIRE(workspace_bytes >= least && workspace && aligned(workspace, 256), W4_ERR_INVALID,
+               "a 256-byte aligned workspace of %zu bytes is needed (%zu given), its first %d bytes zero",
+               need, workspace_bytes, W4_WORKSPACE_SYNC_BYTES);
     cudaStream_t st = S(stream);
-    char *ws = static_cast<char *>(workspace);
+    char *sync = static_cast<char *>(workspace);
+    char *ws = sync + W4_WORKSPACE_SYNC_BYTES;
     const void *a_eff = a;
     if (perm) {
         uint16_t *ap = reinterpret_cast<uint16_t *>(ws);
@@ -181,18 +200,16 @@ int w4_gptq_gemm(const void *a, int a_dtype, const int32_t *qweight, const int32
         if (rc) return rc;
         a_eff = ap;
     }
-    const size_t split = align256(
-        w4::gptq_prefill_split_bytes(M, N, K, group_size, c_dtype == W4_E4M3 ? W4_F32 : c_dtype));
+    void *out = c;
     if (c_dtype == W4_E4M3) {
-        float *y = reinterpret_cast<float *>(ws);
+        out = ws;
         ws += align256((size_t)M * N * 4);
-        rc = w4::gptq_gemv(a_eff, a_dtype, qweight, qzeros, scales, y, W4_F32, M, N, K, group_size,
-                           zero_offset, split ? ws : nullptr, split, st);
-        if (rc) return rc;
-        return w4::rowscale_fp8(y, W4_F32, static_cast<uint8_t *>(c), row_scale, M, N, st);
     }
-    return w4::gptq_gemv(a_eff, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, group_size,
-                         zero_offset, split ? ws : nullptr, split, st);
+    const size_t have = workspace_bytes - (size_t)(ws - sync);
+    rc = w4::gptq_gemv(a_eff, a_dtype, qweight, qzeros, scales, out, c_dtype == W4_E4M3 ? W4_F32 : c_dtype, M, N,
+                       K, group_size, zero_offset, sync, split ? ws : nullptr, split < have ? split : have, st);
+    if (rc || c_dtype != W4_E4M3) return rc;
+    return w4::rowscale_fp8(static_cast<const float *>(out), W4_F32, static_cast<uint8_t *>(c), row_scale, M, N, st);
 }
 
 int w4_gptq_gemm_s4a(const uint8_t *a_s4, const uint8_t *b_s4, const float *a_scale,
@@ -240,8 +257,8 @@ int w4_nvfp4_quant_act(const uint16_t *a, int M, int K, const float *a_global, u
 }
 
 size_t w4_nvfp4_workspace_bytes(int M, int N, int K, int act_mode, int c_dtype) {
-    size_t ws = 0;
     if (M <= 0 || N <= 0 || K <= 0) return 0;
+    size_t ws = W4_WORKSPACE_SYNC_BYTES;
     if (act_mode == W4_ACT_NVFP4) ws += w4::nvfp4_prefill_workspace(M, N, K);
     if (c_dtype == W4_E4M3) ws += align256((size_t)M * N * 4);
     // split-K partials of the W4A16 tensor-core GEMM (the f32 product when the output is e4m3)
@@ -273,16 +290,18 @@ int w4_nvfp4_gemm(const void *a, const uint8_t *w, int layout, const void *scale
                "rearranged scale atoms are read by the NVFP4-activation GEMM only");
     W4_REQUIRE(aligned(a, 16) && aligned(w, 16), W4_ERR_INVALID, "a and w must be 16-byte aligned");
     const size_t need = w4_nvfp4_workspace_bytes(M, N, K, act_mode, c_dtype);
-    W4_REQUIRE(workspace_bytes >= need && (need == 0 || workspace), W4_ERR_INVALID,
-               "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+    W4_REQUIRE(workspace_bytes >= need && workspace && aligned(workspace, 256), W4_ERR_INVALID,
+               "a 256-byte aligned workspace of %zu bytes is needed (%zu given), its first %d bytes zero",
+               need, workspace_bytes, W4_WORKSPACE_SYNC_BYTES);
     cudaStream_t st = S(stream);
+    char *const wsbase = static_cast<char *>(workspace) + W4_WORKSPACE_SYNC_BYTES;
     if (act_mode == W4_ACT_NVFP4) {
         // block-scaled tensor-core GEMM on NVFP4 activations (nvfp4_prefill.cu)
         W4_REQUIRE(scale_dtype == W4_E4M3 || scale_dtype == W4_E4M3_ATOMS, W4_ERR_UNSUPPORTED,
                    "NVFP4 activations need E4M3 weight block scales (the MMA scales are UE4M3)");
         W4_REQUIRE(K % 256 == 0 && N % 128 == 0, W4_ERR_UNSUPPORTED,
                    "NVFP4 activations need K %% 256 == 0 and N %% 128 == 0 (K=%d N=%d)", K, N);
-        char *wsb = static_cast<char *>(workspace);
+        char *wsb = wsbase;
         void *out = c;
         int odt = c_dtype;
         if (c_dtype == W4_E4M3) {
@@ -301,7 +320,7 @@ int w4_nvfp4_gemm(const void *a, const uint8_t *w, int layout, const void *scale
     }
     // W4A16: the tensor-core GEMM from kFp4PrefillMinM tokens on (E4M3 block scales),
     // else the decode kernels
-    char *wsb = static_cast<char *>(workspace);
+    char *wsb = wsbase;
     void *out = c;
     int odt = c_dtype;
     if (c_dtype == W4_E4M3) {
@@ -341,7 +360,7 @@ int w4_rmsnorm_quant_nvfp4(const void *x, int x_dtype, const void *gamma, float 
 
 size_t w4_nvfp4_gemm_q_workspace_bytes(int M, int N, int K, int scale_dtype, int c_dtype) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
-    size_t ws = w4::nvfp4_prefill_q_workspace(M, N, K, scale_dtype == W4_E4M3);
+    size_t ws = W4_WORKSPACE_SYNC_BYTES + w4::nvfp4_prefill_q_workspace(M, N, K, scale_dtype == W4_E4M3);
     if (c_dtype == W4_E4M3) ws += align256((size_t)M * N * 4);
     return ws;
 }
@@ -368,10 +387,11 @@ int w4_nvfp4_gemm_q(const uint8_t *a_codes, const uint8_t *a_sf_atoms, const flo
                    (scale_dtype != W4_E4M3_ATOMS || aligned(scale, 16)),
                W4_ERR_INVALID, "a_codes, a_sf_atoms, w and scale atoms must be 16-byte aligned");
     const size_t need = w4_nvfp4_gemm_q_workspace_bytes(M, N, K, scale_dtype, c_dtype);
-    W4_REQUIRE(workspace_bytes >= need && (need == 0 || workspace), W4_ERR_INVALID,
-               "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+    W4_REQUIRE(workspace_bytes >= need && workspace && aligned(workspace, 256), W4_ERR_INVALID,
+               "a 256-byte aligned workspace of %zu bytes is needed (%zu given), its first %d bytes zero",
+               need, workspace_bytes, W4_WORKSPACE_SYNC_BYTES);
     cudaStream_t st = S(stream);
-    char *wsb = static_cast<char *>(workspace);
+    char *wsb = static_cast<char *>(workspace) + W4_WORKSPACE_SYNC_BYTES;
     void *out = c;
     int odt = c_dtype;
     if (c_dtype == W4_E4M3) {

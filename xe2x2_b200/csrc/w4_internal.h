@@ -14,14 +14,25 @@ int gptq_repack_act_order(const int32_t *qweight, const int32_t *g_idx, int K, i
 int gather_cols(const uint16_t *a, const int32_t *perm, int M, int K, uint16_t *out,
                 cudaStream_t st);
 // Any M: the tensor-core GEMM for M >= kPrefillMinM when it takes the shape, else
-// the decode kernels.  ws / ws_bytes: scratch for split-K partials (may be null).
+// the decode kernels.  sync: the workspace's zeroed sync area (may be null); ws /
+// ws_bytes: scratch for split-K partials (may be null: no K split).
 int gptq_gemv(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
               const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs,
-              int zero_offset, void *ws, size_t ws_bytes, cudaStream_t st);
+              int zero_offset, void *sync, void *ws, size_t ws_bytes, cudaStream_t st);
 int gptq_gemv_tma(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
                   const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
                   cudaStream_t st);
 int take_wait_status();
+// gptq_decode.cu: the shared-ring decode GEMM (M <= 16); -1 = shape not handled there.
+// sync: zeroed tile counters (W4_WORKSPACE_SYNC_BYTES); ws: K-split partials of
+// gptq_decode_split_bytes() bytes.  Without them the GEMM runs unsplit.
+int gptq_gemv_decode(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
+                     const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
+                     void *sync, void *ws, size_t ws_bytes, cudaStream_t st);
+size_t gptq_decode_split_bytes(int M, int N, int K, int gs);
+int take_decode_wait_status();
+// w4_api.cu: count a decode call that ran a register-streamed fallback kernel
+void note_decode_fallback();
 
 // Row-parallel decode GEMM with the all-reduce in its epilogue (gptq_tma.cu), over
 // the peer buffers of a tensor-parallel communicator (tp_peer.cu lays them out):

@@ -55,7 +55,11 @@ def _contig(t, name):
 
 
 class _Workspace:
-    """Per-device scratch buffer grown on demand (callers of the C ABI pass it in)."""
+    """Per-(device, stream) scratch buffer grown on demand (callers of the C ABI pass it in).
+
+    Allocated zero-filled: every libw4 workspace starts with a sync area that must be zero
+    before first use and that every call leaves zero (include/w4.h).
+    """
 
     def __init__(self):
         self._buf = {}
@@ -68,7 +72,7 @@ class _Workspace:
         with self._lock:
             buf = self._buf.get(key)
             if buf is None or buf.numel() < nbytes:
-                buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+                buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
                 self._buf[key] = buf
         return buf, buf.numel()
 

@@ -272,7 +272,9 @@ class TPLayerSet:
             else:
                 shard = shard_rows(qw, qz, sc, rank, world, group_size)
             del qw, qz, sc
-            self.layers[p.name] = TPLinear(comm, p.mode, *shard, group_size=group_size)
+            # at world 1 a row-parallel shard is the whole matrix and nothing is summed
+            mode = p.mode if world > 1 else "column"
+            self.layers[p.name] = TPLinear(comm, mode, *shard, group_size=group_size)
 
     def inputs(self, M, dtype=torch.bfloat16, seed=7):
         """Activations for every projection's shard: {name: [M, K_rank]}."""
@@ -295,4 +297,13 @@ class TPLayerSet:
         tot = 0
         for lay in self.layers.values():
             tot += lay.qweight.numel() * 4 + lay.scales.numel() * 2 + (0 if lay.qzeros is None else lay.qzeros.numel() * 4)
+        return tot
+
+    def bytes(self, M, group_size=128):
+        """Algorithmic bytes of one step of the whole (unsharded) layer: every weight once and the
+        bf16 activations in and outputs out once (replicated reads across ranks not counted)."""
+        tot = 0
+        for p in self.projs:
+            ngrp = p.K // group_size
+            tot += p.K // 8 * p.N * 4 + ngrp * p.N * 2 + ngrp * p.N // 8 * 4 + M * (p.K + p.N) * 2
         return tot
