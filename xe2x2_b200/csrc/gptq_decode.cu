@@ -162,6 +162,10 @@ gptq_decode_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_cons
     const int P = act_pitch(max_st);
 
     if (warp == CW && lane == 0) {
+        // the descriptors' first use would otherwise wait for their fetch
+        prefetch_tensormap(&qw_map);
+        prefetch_tensormap(&sc_map);
+        if (has_z) prefetch_tensormap(&zr_map);
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], CW);
@@ -408,16 +412,14 @@ gptq_decode_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_cons
                 *reinterpret_cast<float4 *>(part + ((size_t)blockIdx.z * M + tok0 + tr) * N + n0 + colw) =
                     make_float4(facc[0][nt][i], facc[0][nt][i + 2], facc[1][nt][i], facc[1][nt][i + 2]);
         }
-    // Publish: the CTA barrier makes every consumer's partials visible to thread 0, whose
-    // device-scope fence then orders them (cumulatively) before its count; after the count a
-    // second fence orders the other CTAs' partials before this CTA's reads (the last one).
+    // Publish: the CTA barrier orders every consumer's partials before thread 0's count, whose
+    // release (cumulative) publishes them at device scope; its acquire orders the other CTAs'
+    // partials before this CTA's reads (the last one), which the second barrier passes on.
     asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
     int *flag = reinterpret_cast<int *>(base + L.flag);
     if (threadIdx.x == 0) {
         const unsigned int tile = blockIdx.x * gridDim.y + blockIdx.y;
-        __threadfence();
-        *flag = atomicInc(&cnt[tile], (unsigned int)(ks - 1)) == (unsigned int)(ks - 1);  // wraps to 0
-        __threadfence();
+        *flag = atom_inc_acq_rel(&cnt[tile], (unsigned int)(ks - 1)) == (unsigned int)(ks - 1);  // wraps to 0
     }
     asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
     if (!*flag) return;
@@ -460,8 +462,6 @@ bool env_choice(DecChoice &c) {
 
 constexpr int kSmemPerSm = 228 * 1024;  // shared memory of one SM
 constexpr int kSmemPerCta = 227 * 1024;
-
-int sg_of(int gs) { return gs % 128 == 0 ? 1 : 128 / gs; }
 
 // Ring depth: stages until the CTAs an SM holds share its shared memory, within [3, kMaxStages].
 int ring_depth(int cw, int sg, int max_st, int rows, int per_sm) {

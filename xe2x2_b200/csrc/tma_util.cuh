@@ -98,6 +98,18 @@ __device__ __forceinline__ void bulk_load_1d(void *dst, const void *src, uint32_
 // Programmatic dependent launch: let the next grid on the stream start its
 // prologue now / wait until every grid this one depends on has completed and
 // its memory is visible (no-ops when the launch carries no such dependency).
+// Fetch a tensor map into the TMA unit's descriptor cache ahead of its first copy.
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+// atomicInc with acquire-release semantics at device scope: the writes ordered before it (by
+// program order or a CTA barrier) are published with the count, and the writes other threads
+// published with their counts are visible after it.
+__device__ __forceinline__ unsigned int atom_inc_acq_rel(unsigned int *p, unsigned int limit) {
+    unsigned int old;
+    asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(limit) : "memory");
+    return old;
+}
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 // Thread-block clusters: a full barrier over every thread of every CTA of the
