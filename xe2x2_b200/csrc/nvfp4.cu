@@ -657,11 +657,12 @@ static int launch_nvfp4_gemv_t(const uint16_t *a, const uint8_t *w, const void *
 
 int nvfp4_gemv(const uint16_t *a, const uint8_t *w, int layout, const void *scale,
                int scale_dtype, const float *global_scale, void *c, int c_dtype, int M, int N,
-               int K, cudaStream_t st) {
+               int K, void *sync, void *ws, size_t ws_bytes, cudaStream_t st) {
     (void)layout;  // NK only; validated by the caller
-    // TMA-streamed kernel (nvfp4_tma.cu) first; the register-streamed one below
-    // covers shapes it does not take.
-    const int rc = nvfp4_gemv_tma(a, w, scale, scale_dtype, global_scale, c, c_dtype, M, N, K, st);
+    // the TMA-ring kernel (nvfp4_decode.cu) first; the register-streamed one below covers
+    // pointers it does not take
+    const int rc = nvfp4_gemv_decode(a, w, scale, scale_dtype, global_scale, c, c_dtype, M, N, K, sync, ws,
+                                     ws_bytes, st);
     if (rc >= 0) return rc;
     note_decode_fallback();
     if (scale_dtype == W4_E4M3) {

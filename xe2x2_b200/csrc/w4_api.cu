@@ -89,7 +89,7 @@ int w4_check_device_status(void) {
     w4::set_error("");
     const int r1 = w4::take_wait_status();
     const int r2 = w4::take_prefill_wait_status();
-    const int r3 = w4::take_fp4_wait_status();
+    const int r3 = w4::take_fp4d_wait_status();
     const int r4 = w4::take_fp4_prefill_wait_status();
     const int r5 = w4::take_tp_wait_status();
     const int r6 = w4::take_tp_fused_wait_status();
@@ -261,9 +261,13 @@ size_t w4_nvfp4_workspace_bytes(int M, int N, int K, int act_mode, int c_dtype) 
     size_t ws = W4_WORKSPACE_SYNC_BYTES;
     if (act_mode == W4_ACT_NVFP4) ws += w4::nvfp4_prefill_workspace(M, N, K);
     if (c_dtype == W4_E4M3) ws += align256((size_t)M * N * 4);
-    // split-K partials of the W4A16 tensor-core GEMM (the f32 product when the output is e4m3)
-    if (act_mode == W4_ACT_W4A16)
-        ws += align256(w4::nvfp4_w4a16_prefill_split_bytes(M, N, K, c_dtype == W4_E4M3 ? W4_F32 : c_dtype));
+    // split-K partials of the W4A16 tensor-core GEMM or of the decode GEMM, whichever the shape
+    // takes (after the f32 product when the output is e4m3)
+    if (act_mode == W4_ACT_W4A16) {
+        const size_t pf = w4::nvfp4_w4a16_prefill_split_bytes(M, N, K, c_dtype == W4_E4M3 ? W4_F32 : c_dtype);
+        const size_t dec = w4::nvfp4_decode_split_bytes(M, N, K);
+        ws += align256(pf > dec ? pf : dec);
+    }
     return ws;
 }
 
@@ -336,7 +340,8 @@ int w4_nvfp4_gemm(const void *a, const uint8_t *w, int layout, const void *scale
     }
     if (rc == -1)
         rc = w4::nvfp4_gemv(static_cast<const uint16_t *>(a), w, layout, scale, scale_dtype, global_scale, out, odt,
-                            M, N, K, st);
+                            M, N, K, workspace, wsb, workspace_bytes - (size_t)(wsb - static_cast<char *>(workspace)),
+                            st);
     if (rc || c_dtype != W4_E4M3) return rc;
     return w4::rowscale_fp8(out, W4_F32, static_cast<uint8_t *>(c), row_scale, M, N, st);
 }

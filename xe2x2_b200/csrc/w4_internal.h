@@ -81,9 +81,12 @@ int nvfp4_quant_act_atoms(const uint16_t *a, int M, int K, const float *a_global
                           uint8_t *sf_atoms, cudaStream_t st);
 int nvfp4_lut_s8a(const int8_t *a, const uint8_t *packed, const float *a_s, const float *b_s,
                   uint16_t *c, int rows, int cols, int dk, cudaStream_t st);
-int nvfp4_gemv_tma(const uint16_t *a, const uint8_t *w, const void *scale, int scale_dtype,
-                   const float *global_scale, void *c, int c_dtype, int M, int N, int K, cudaStream_t st);
-int take_fp4_wait_status();
+// nvfp4_decode.cu (shared TMA ring; K split through the workspace): -1 = not handled there
+size_t nvfp4_decode_split_bytes(int M, int N, int K);
+int nvfp4_gemv_decode(const uint16_t *a, const uint8_t *w, const void *scale, int scale_dtype,
+                      const float *global_scale, void *c, int c_dtype, int M, int N, int K, void *sync, void *ws,
+                      size_t ws_bytes, cudaStream_t st);
+int take_fp4d_wait_status();
 // nvfp4_prefill.cu (tcgen05 block-scaled); -1 = shape not handled there
 size_t nvfp4_prefill_workspace(int M, int N, int K);
 int nvfp4_prefill(const uint16_t *a, const float *a_global, const uint8_t *w_nk, const uint8_t *w_sf,
@@ -91,9 +94,11 @@ int nvfp4_prefill(const uint16_t *a, const float *a_global, const uint8_t *w_nk,
                   void *workspace, cudaStream_t st);
 int nvfp4_sf_atoms(const uint8_t *src, int rows, int nkb, long rs, long ks, uint8_t *dst, cudaStream_t st);
 int take_fp4_prefill_wait_status();
+// sync / ws / ws_bytes: the workspace's sync area and the space for K-split partials (null:
+// no K split)
 int nvfp4_gemv(const uint16_t *a, const uint8_t *w, int layout, const void *scale,
                int scale_dtype, const float *global_scale, void *c, int c_dtype, int M, int N,
-               int K, cudaStream_t st);
+               int K, void *sync, void *ws, size_t ws_bytes, cudaStream_t st);
 
 // epilogue.cu
 int rmsnorm_quant_s8(const uint16_t *x, int8_t *q, float *scale, int M, int K, float eps,
