@@ -50,3 +50,44 @@ def test_rowscale_fp8_bit_exact(cuda, dtype):
     q_ref, s_ref = O.rowscale_fp8(np_(y.float()))
     assert np.array_equal(np_(q.view(torch.uint8)), q_ref)
     assert np.array_equal(np_(s), s_ref)
+
+
+def _sync_area_zero(dev):
+    from xe2x2_b200 import _lib as L
+    buf, _ = ops._WS.get(dev, 1)
+    return bool((buf[:L.W4_WORKSPACE_SYNC_BYTES] == 0).all())
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 17408, 5120), (5, 4096, 4096), (16, 5120, 2176)])
+def test_gptq_fp8_output_fused_row_max(cuda, M, N, K):
+    """Decode sizes: the GEMM folds the row maxima into the workspace and the cast reads its f32
+    product once.  The fp8 codes and row scales equal the two-pass cast of the same call's f32
+    output bit for bit, twice in a row, and the sync area is zero again afterwards."""
+    from xe2x2_b200 import synth
+    qw, qz, sc, _ = synth.gptq_weights(K, N, 128, asym=True, seed=M, device=cuda)
+    a = synth.activations(M, K, torch.bfloat16, seed=M + 1, device=cuda)
+    y = ops.gptq_gemm(a, qw, qz, sc, 128, 1, out_dtype=torch.float32)
+    q_ref, s_ref = O.rowscale_fp8(np_(y))
+    for _ in range(2):
+        q, s = ops.gptq_gemm(a, qw, qz, sc, 128, 1, out_dtype=torch.float8_e4m3fn)
+        torch.cuda.synchronize()
+        assert np.array_equal(np_(q.view(torch.uint8)), q_ref)
+        assert np.array_equal(np_(s), s_ref)
+        assert _sync_area_zero(cuda)
+
+
+@pytest.mark.parametrize("M", [1, 8])
+def test_nvfp4_fp8_output_fused_row_max(cuda, M):
+    """The same for the NVFP4 W4A16 decode GEMM."""
+    from xe2x2_b200 import synth
+    K, N = 5120, 5120
+    w, scale, gscale = synth.nvfp4_weights(K, N, seed=M, device=cuda)
+    x = synth.activations(M, K, torch.bfloat16, seed=M + 2, device=cuda)
+    y = ops.nvfp4_gemm(x, w, scale, gscale, torch.float32)
+    q_ref, s_ref = O.rowscale_fp8(np_(y))
+    for _ in range(2):
+        q, s = ops.nvfp4_gemm(x, w, scale, gscale, torch.float8_e4m3fn)
+        torch.cuda.synchronize()
+        assert np.array_equal(np_(q.view(torch.uint8)), q_ref)
+        assert np.array_equal(np_(s), s_ref)
+        assert _sync_area_zero(cuda)

@@ -7,6 +7,7 @@
 // order with IEEE division / square root, so codes can differ from the host
 // only where the parallel sum of squares rounds differently (|dq| <= 1, the
 // reference's own acceptance bound, rmsnorm_epilogue.cpp:193-204).
+#include "tma_util.cuh"
 #include "w4_common.cuh"
 #include "w4_internal.h"
 
@@ -101,6 +102,48 @@ rowscale_fp8_kernel(const void *__restrict__ y, uint8_t *__restrict__ q,
     if (threadIdx.x == 0) row_scale[row] = s;
     for (int j = threadIdx.x; j < N; j += blockDim.x)
         q[base + j] = (uint8_t)f_to_e4m3(__fdiv_rn(load_as_f<T>(y, base + j), s));
+}
+
+// The cast when a decode GEMM has already folded the row maxima of |y| into rowmax (fp32 bits):
+// CTA (chunk, row) casts 8 values per thread of its 2048-value chunk, with the row's scale
+// computed as above; chunk 0 stores it.  Each CTA counts itself on rowcnt[row] after reading
+// the maximum (acquire-release), and the last one zeroes rowmax[row] for the next call (the
+// counter wraps to zero).
+constexpr int kCastChunk = 8 * kRowThreads;
+__global__ void __launch_bounds__(kRowThreads)
+rowscale_fp8_amax_kernel(const float *__restrict__ y, unsigned int *__restrict__ rowmax,
+                         unsigned int *__restrict__ rowcnt, uint8_t *__restrict__ q,
+                         float *__restrict__ row_scale, int N) {
+    __shared__ float s_sh;
+    const int row = blockIdx.y;
+    if (threadIdx.x == 0) {
+        const float amax = __uint_as_float(*reinterpret_cast<volatile unsigned int *>(&rowmax[row]));
+        float s = __fdiv_rn(amax, 448.f);
+        if (s <= 0.f) s = 1.f;
+        s_sh = s;
+        if (blockIdx.x == 0) row_scale[row] = s;
+        if (atom_inc_acq_rel(&rowcnt[row], gridDim.x - 1) == gridDim.x - 1) rowmax[row] = 0u;
+    }
+    __syncthreads();
+    const float s = s_sh;
+    const int j = blockIdx.x * kCastChunk + threadIdx.x * 8;
+    if (j >= N) return;
+    const float4 a = __ldcs(reinterpret_cast<const float4 *>(y + (size_t)row * N + j));
+    const float4 b = __ldcs(reinterpret_cast<const float4 *>(y + (size_t)row * N + j + 4));
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w[i >> 2] |= f_to_e4m3(__fdiv_rn(v[i], s)) << (8 * (i & 3));
+    *reinterpret_cast<uint2 *>(q + (size_t)row * N + j) = make_uint2(w[0], w[1]);
+}
+
+int rowscale_fp8_amax(const float *y, unsigned int *rowmax, unsigned int *rowcnt, uint8_t *q, float *row_scale,
+                      int M, int N, cudaStream_t st) {
+    if (M > 16 || N % 8 || !aligned(y, 16) || !aligned(q, 8)) return -1;
+    const dim3 grid((N + kCastChunk - 1) / kCastChunk, M);
+    rowscale_fp8_amax_kernel<<<grid, kRowThreads, 0, st>>>(y, rowmax, rowcnt, q, row_scale, N);
+    W4_LAUNCH_CHECK();
+    return W4_OK;
 }
 
 int rowscale_fp8(const void *y, int y_dtype, uint8_t *q, float *row_scale, int M, int N,

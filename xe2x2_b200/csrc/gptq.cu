@@ -383,7 +383,7 @@ int gptq_gemv(const void *a, int a_dtype, const int32_t *qweight, const int32_t 
         if (rp >= 0) return rp;
     }
     const int rc = gptq_gemv_decode(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, sync,
-                                    ws, ws_bytes, st);
+                                    ws, ws_bytes, nullptr, st);
     if (rc >= 0) return rc;
     note_decode_fallback();
     if (a_dtype == W4_BF16)

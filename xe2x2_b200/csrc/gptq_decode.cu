@@ -69,8 +69,8 @@ __host__ __device__ constexpr int al128(int x) { return (x + 127) & ~127; }
 __host__ __device__ inline int act_pitch(int max_stages) { return max_stages * 256 + 64; }
 
 // Shared-memory layout of one CTA (byte offsets from a 1024-aligned base), the same on host
-// and device: S weight stages | S scale stages | S zero stages | 2S + 1 barriers and a flag |
-// per-unit terms [units][16 rows] (float4) | activations [rows][P] and one zero row.
+// and device: S weight stages | S scale stages | S zero stages | 2S + 1 barriers, a flag and 16
+// row maxima | per-unit terms [units][16 rows] (float4) | activations [rows][P] and one zero row.
 struct Lay {
     int w_stage, sc_stage, zr_stage, sc, zr, bars, flag, corr, act, total;
     __host__ __device__ Lay(int CW, int SG, int S, int max_st, int rows) {
@@ -82,7 +82,7 @@ struct Lay {
         zr = sc + S * sc_stage;
         bars = zr + S * zr_stage;
         flag = bars + (2 * S + 1) * 8;
-        corr = al128(flag + 4);
+        corr = al128(flag + 4 + 16 * 4);
         act = al128(corr + max_st * SG * 16 * 16);
         total = act + (rows + 1) * act_pitch(max_st);  // the last row stays zero
         (void)BN;
@@ -140,7 +140,8 @@ __global__ void __maxnreg__(dec_regs<NT>())
 gptq_decode_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_constant__ CUtensorMap sc_map,
                    const __grid_constant__ CUtensorMap zr_map, const uint16_t *__restrict__ A, void *__restrict__ C,
                    int c_dtype, int M, int N, int K, int has_z, int zero_offset, int nst, int max_st, int gs, int S,
-                   int bf16, int pre, float *__restrict__ part, unsigned int *__restrict__ cnt) {
+                   int bf16, int pre, float *__restrict__ part, unsigned int *__restrict__ cnt,
+                   unsigned int *__restrict__ rowmax) {
     constexpr int SG = 4 / GSTEPS;
     constexpr int BN = 32 * CW;
     extern __shared__ uint8_t smem_dyn[];
@@ -280,6 +281,8 @@ gptq_decode_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_cons
     }
     for (int o = threadIdx.x; o < ns * (kStageK / 8); o += CW * 32)
         *reinterpret_cast<uint4 *>(act + rows_alloc * P + o * 16) = make_uint4(0, 0, 0, 0);  // the zero row
+    unsigned int *rmax = reinterpret_cast<unsigned int *>(base + L.flag + 4);  // this CTA's row maxima
+    if (rowmax && threadIdx.x < 16) rmax[threadIdx.x] = 0u;
     asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");  // consumers only
 
     const int cw = warp;
@@ -396,9 +399,12 @@ gptq_decode_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_cons
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const int tr = nt * 8 + 2 * t + (i & 1);
-                    if (tr < rows)
+                    if (tr < rows) {
                         store_out(C, c_dtype, (size_t)(tok0 + tr) * N + n0 + colw + 2 * mt + (i >> 1), facc[mt][nt][i]);
+                        if (rowmax) fold_rowmax(rmax, tr, facc[mt][nt][i]);
+                    }
                 }
+        if (rowmax) publish_rowmax<CW>(rmax, rowmax + tok0, rows);
         return;
     }
     // K split: this CTA's partial tile -> part[z][token][column] (16-byte stores of four
@@ -435,7 +441,9 @@ gptq_decode_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_cons
         store_out(C, c_dtype, o + 1, v.y);
         store_out(C, c_dtype, o + 2, v.z);
         store_out(C, c_dtype, o + 3, v.w);
+        if (rowmax) fold_rowmax(rmax, tr, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
     }
+    if (rowmax) publish_rowmax<CW>(rmax, rowmax + tok0, rows);
 }
 
 }  // namespace dec
@@ -514,7 +522,7 @@ DecChoice choose(int M, int N, int K, int gs, int NT) {
 template <int CW, int NT, int GSTEPS>
 static int launch_dec_t(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
                         const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
-                        DecChoice ch, unsigned int *cnt, float *part, cudaStream_t st) {
+                        DecChoice ch, unsigned int *cnt, float *part, unsigned int *rowmax, cudaStream_t st) {
     constexpr int SG = 4 / GSTEPS;
     constexpr int BN = 32 * CW;
     const int nst = (K + dec::kStageK - 1) / dec::kStageK;
@@ -565,35 +573,35 @@ static int launch_dec_t(const void *a, int a_dtype, const int32_t *qweight, cons
     dim3 grid(mblocks, N / BN, ks), block(32 * (CW + 1));
     W4_CUDA_TRY(launch_decode(kern, grid, block, smem, st, 1u, qw_map, sc_map, zr_map,
                               static_cast<const uint16_t *>(a), c, c_dtype, M, N, K, has_z, zero_offset, nst, max_st,
-                              gs, S, (int)(a_dtype == W4_BF16), pre, part, cnt));
+                              gs, S, (int)(a_dtype == W4_BF16), pre, part, cnt, rowmax));
     return W4_OK;
 }
 
 template <int CW, int NT>
 static int launch_dec_g(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
                         const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
-                        DecChoice ch, unsigned int *cnt, float *part, cudaStream_t st) {
+                        DecChoice ch, unsigned int *cnt, float *part, unsigned int *rowmax, cudaStream_t st) {
     if (gs % 128 == 0)
         return launch_dec_t<CW, NT, 4>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch,
-                                       cnt, part, st);
+                                       cnt, part, rowmax, st);
     if (gs == 64)
         return launch_dec_t<CW, NT, 2>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch,
-                                       cnt, part, st);
+                                       cnt, part, rowmax, st);
     if (gs == 32)
         return launch_dec_t<CW, NT, 1>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch,
-                                       cnt, part, st);
+                                       cnt, part, rowmax, st);
     return -1;
 }
 
 template <int NT>
 static int launch_dec_nt(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
                          const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
-                         DecChoice ch, unsigned int *cnt, float *part, cudaStream_t st) {
+                         DecChoice ch, unsigned int *cnt, float *part, unsigned int *rowmax, cudaStream_t st) {
     switch (ch.cw) {
-        case 8: return launch_dec_g<8, NT>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch, cnt, part, st);
-        case 4: return launch_dec_g<4, NT>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch, cnt, part, st);
-        case 2: return launch_dec_g<2, NT>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch, cnt, part, st);
-        case 1: return launch_dec_g<1, NT>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch, cnt, part, st);
+        case 8: return launch_dec_g<8, NT>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch, cnt, part, rowmax, st);
+        case 4: return launch_dec_g<4, NT>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch, cnt, part, rowmax, st);
+        case 2: return launch_dec_g<2, NT>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch, cnt, part, rowmax, st);
+        case 1: return launch_dec_g<1, NT>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch, cnt, part, rowmax, st);
         default: return -1;
     }
 }
@@ -613,7 +621,7 @@ size_t gptq_decode_split_bytes(int M, int N, int K, int gs) {
 
 int gptq_gemv_decode(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
                      const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
-                     void *sync, void *ws, size_t ws_bytes, cudaStream_t st) {
+                     void *sync, void *ws, size_t ws_bytes, unsigned int *rowmax, cudaStream_t st) {
     if (!decode_shape_ok(M, N, K, gs)) return -1;
     if (!aligned(qweight, 16) || !aligned(scales, 16) || (qzeros && !aligned(qzeros, 16)) || !aligned(a, 16)) return -1;
     const int NT = M <= 8 ? 1 : 2;
@@ -623,13 +631,13 @@ int gptq_gemv_decode(const void *a, int a_dtype, const int32_t *qweight, const i
     const long tiles = (long)(N / (32 * ch.cw)) * ((M + 8 * NT - 1) / (8 * NT));
     // The K split needs the workspace: fp32 partials and one counter per tile in the sync area.
     if (ch.ks > 1 && (!sync || !ws || !aligned(ws, 16) || ws_bytes < (size_t)ch.ks * M * N * 4 ||
-                      tiles > (long)(W4_WORKSPACE_SYNC_BYTES / sizeof(unsigned int))))
+                      tiles > (long)kSyncTileCounters))
         ch.ks = 1;
     unsigned int *cnt = static_cast<unsigned int *>(sync);
     float *part = static_cast<float *>(ws);
     if (NT == 1)
-        return launch_dec_nt<1>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch, cnt, part, st);
-    return launch_dec_nt<2>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch, cnt, part, st);
+        return launch_dec_nt<1>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch, cnt, part, rowmax, st);
+    return launch_dec_nt<2>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch, cnt, part, rowmax, st);
 }
 
 int take_decode_wait_status() {

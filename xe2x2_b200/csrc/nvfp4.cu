@@ -662,7 +662,7 @@ int nvfp4_gemv(const uint16_t *a, const uint8_t *w, int layout, const void *scal
     // the TMA-ring kernel (nvfp4_decode.cu) first; the register-streamed one below covers
     // pointers it does not take
     const int rc = nvfp4_gemv_decode(a, w, scale, scale_dtype, global_scale, c, c_dtype, M, N, K, sync, ws,
-                                     ws_bytes, st);
+                                     ws_bytes, nullptr, st);
     if (rc >= 0) return rc;
     note_decode_fallback();
     if (scale_dtype == W4_E4M3) {

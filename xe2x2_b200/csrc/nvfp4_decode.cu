@@ -61,8 +61,8 @@ __host__ __device__ constexpr int al128(int x) { return (x + 127) & ~127; }
 __host__ __device__ inline int act_pitch(int max_st) { return max_st * 512 + 64; }
 
 // Shared-memory layout of one CTA (byte offsets from a 1024-aligned base), the same on host and
-// device: S weight stages (CW boxes of 4 KB) | S scale stages (16 x BN E4M3) | 2S + 1 barriers
-// and a flag | 2^-e [units][16 rows] | activations [rows][P] and one zero row.
+// device: S weight stages (CW boxes of 4 KB) | S scale stages (16 x BN E4M3) | 2S + 1 barriers,
+// a flag and 16 row maxima | 2^-e [units][16 rows] | activations [rows][P] and one zero row.
 struct Lay {
     int w_stage, s_stage, sc, bars, flag, inv, act, total;
     __host__ __device__ Lay(int CW, int S, int max_st, int rows) {
@@ -71,7 +71,7 @@ struct Lay {
         sc = S * w_stage;
         bars = sc + S * s_stage;
         flag = bars + (2 * S + 1) * 8;
-        inv = al128(flag + 4);
+        inv = al128(flag + 4 + 16 * 4);
         act = al128(inv + max_st * 2 * 16 * 4);
         total = act + (rows + 1) * act_pitch(max_st);
     }
@@ -130,7 +130,7 @@ __global__ void __maxnreg__((fp4d_regs<NT>()))
 nvfp4_decode_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap sc_map,
                     const uint16_t *__restrict__ A, const float *__restrict__ global_scale, void *__restrict__ C,
                     int c_dtype, int M, int N, int K, int nst, int max_st, int S, int pre,
-                    float *__restrict__ part, unsigned int *__restrict__ cnt) {
+                    float *__restrict__ part, unsigned int *__restrict__ cnt, unsigned int *__restrict__ rowmax) {
     constexpr int BN = 32 * CW;
     extern __shared__ uint8_t smem_dyn[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
@@ -251,6 +251,8 @@ nvfp4_decode_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
         for (int o = threadIdx.x; o < ns * (KS / 8); o += CW * 32)
             *reinterpret_cast<uint4 *>(act + rows_alloc * P + o * 16) = make_uint4(0, 0, 0, 0);  // the zero row
     }
+    unsigned int *rmax = reinterpret_cast<unsigned int *>(base + L.flag + 4);  // this CTA's row maxima
+    if (rowmax && threadIdx.x < 16) rmax[threadIdx.x] = 0u;
     asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");  // consumers only
 
     const int cw = warp;
@@ -361,9 +363,13 @@ nvfp4_decode_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const int tr = nt * 8 + 2 * t + (i & 1);
-                    if (tr < rows)
-                        store_out(C, c_dtype, (size_t)(tok0 + tr) * N + n0 + colw + 2 * mt + (i >> 1), facc[mt][nt][i] * gsc);
+                    if (tr < rows) {
+                        const float v = facc[mt][nt][i] * gsc;
+                        store_out(C, c_dtype, (size_t)(tok0 + tr) * N + n0 + colw + 2 * mt + (i >> 1), v);
+                        if (rowmax) fold_rowmax(rmax, tr, v);
+                    }
                 }
+        if (rowmax) publish_rowmax<CW>(rmax, rowmax + tok0, rows);
         return;
     }
     // K split: this CTA's partial tile -> part[z][token][column] (8-byte stores of two columns),
@@ -398,11 +404,14 @@ nvfp4_decode_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
             const float4 u = __ldcg(reinterpret_cast<const float4 *>(part + (size_t)z * M * N + o));
             v.x += u.x, v.y += u.y, v.z += u.z, v.w += u.w;
         }
-        store_out(C, c_dtype, o, v.x * gsc);
-        store_out(C, c_dtype, o + 1, v.y * gsc);
-        store_out(C, c_dtype, o + 2, v.z * gsc);
-        store_out(C, c_dtype, o + 3, v.w * gsc);
+        v.x *= gsc, v.y *= gsc, v.z *= gsc, v.w *= gsc;
+        store_out(C, c_dtype, o, v.x);
+        store_out(C, c_dtype, o + 1, v.y);
+        store_out(C, c_dtype, o + 2, v.z);
+        store_out(C, c_dtype, o + 3, v.w);
+        if (rowmax) fold_rowmax(rmax, tr, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
     }
+    if (rowmax) publish_rowmax<CW>(rmax, rowmax + tok0, rows);
 }
 
 }  // namespace fp4d
@@ -473,7 +482,7 @@ Fp4Choice fp4_choose(int M, int N, int K, int NT) {
 template <int CW, int NT>
 static int launch_fp4d_t(const uint16_t *a, const uint8_t *w, const void *scale, const float *global_scale, void *c,
                          int c_dtype, int M, int N, int K, Fp4Choice ch, unsigned int *cnt, float *part,
-                         cudaStream_t st) {
+                         unsigned int *rowmax, cudaStream_t st) {
     constexpr int BN = 32 * CW;
     const int nst = (K + fp4d::KS - 1) / fp4d::KS;
     const int ks = ch.ks > nst ? nst : ch.ks;
@@ -517,19 +526,19 @@ static int launch_fp4d_t(const uint16_t *a, const uint8_t *w, const void *scale,
     const int pre = launch_overlap() == W4_OVERLAP_STATIC_WEIGHTS;
     dim3 grid(mblocks, N / BN, ks), block(32 * (CW + 1));
     W4_CUDA_TRY(launch_decode(kern, grid, block, smem, st, 1u, w_map, sc_map, a, global_scale, c, c_dtype, M, N, K,
-                              nst, max_st, S, pre, part, cnt));
+                              nst, max_st, S, pre, part, cnt, rowmax));
     return W4_OK;
 }
 
 template <int NT>
 static int launch_fp4d_nt(const uint16_t *a, const uint8_t *w, const void *scale, const float *global_scale,
                           void *c, int c_dtype, int M, int N, int K, Fp4Choice ch, unsigned int *cnt, float *part,
-                          cudaStream_t st) {
+                          unsigned int *rowmax, cudaStream_t st) {
     switch (ch.cw) {
-        case 8: return launch_fp4d_t<8, NT>(a, w, scale, global_scale, c, c_dtype, M, N, K, ch, cnt, part, st);
-        case 4: return launch_fp4d_t<4, NT>(a, w, scale, global_scale, c, c_dtype, M, N, K, ch, cnt, part, st);
-        case 2: return launch_fp4d_t<2, NT>(a, w, scale, global_scale, c, c_dtype, M, N, K, ch, cnt, part, st);
-        case 1: return launch_fp4d_t<1, NT>(a, w, scale, global_scale, c, c_dtype, M, N, K, ch, cnt, part, st);
+        case 8: return launch_fp4d_t<8, NT>(a, w, scale, global_scale, c, c_dtype, M, N, K, ch, cnt, part, rowmax, st);
+        case 4: return launch_fp4d_t<4, NT>(a, w, scale, global_scale, c, c_dtype, M, N, K, ch, cnt, part, rowmax, st);
+        case 2: return launch_fp4d_t<2, NT>(a, w, scale, global_scale, c, c_dtype, M, N, K, ch, cnt, part, rowmax, st);
+        case 1: return launch_fp4d_t<1, NT>(a, w, scale, global_scale, c, c_dtype, M, N, K, ch, cnt, part, rowmax, st);
         default: return -1;
     }
 }
@@ -548,7 +557,7 @@ size_t nvfp4_decode_split_bytes(int M, int N, int K) {
 // W4_OK / a W4 error, or -1 when the shape or tensor maps are not handled here.
 int nvfp4_gemv_decode(const uint16_t *a, const uint8_t *w, const void *scale, int scale_dtype,
                       const float *global_scale, void *c, int c_dtype, int M, int N, int K, void *sync, void *ws,
-                      size_t ws_bytes, cudaStream_t st) {
+                      size_t ws_bytes, unsigned int *rowmax, cudaStream_t st) {
     if (!fp4_decode_shape_ok(M, N, K)) return -1;
     // E4M3 block scales only: a bf16 scale times an e2m1 code need not be an f16
     if (scale_dtype != W4_E4M3 || !aligned(a, 16) || !aligned(w, 16) || !aligned(scale, 16)) return -1;
@@ -559,12 +568,12 @@ int nvfp4_gemv_decode(const uint16_t *a, const uint8_t *w, const void *scale, in
     const long tiles = (long)(N / (32 * ch.cw)) * ((M + 8 * NT - 1) / (8 * NT));
     // The K split needs the workspace: fp32 partials and one counter per tile in the sync area.
     if (ch.ks > 1 && (!sync || !ws || !aligned(ws, 16) || ws_bytes < (size_t)ch.ks * M * N * 4 ||
-                      tiles > (long)(W4_WORKSPACE_SYNC_BYTES / sizeof(unsigned int))))
+                      tiles > (long)kSyncTileCounters))
         ch.ks = 1;
     unsigned int *cnt = static_cast<unsigned int *>(sync);
     float *part = static_cast<float *>(ws);
-    return NT == 1 ? launch_fp4d_nt<1>(a, w, scale, global_scale, c, c_dtype, M, N, K, ch, cnt, part, st)
-                   : launch_fp4d_nt<2>(a, w, scale, global_scale, c, c_dtype, M, N, K, ch, cnt, part, st);
+    return NT == 1 ? launch_fp4d_nt<1>(a, w, scale, global_scale, c, c_dtype, M, N, K, ch, cnt, part, rowmax, st)
+                   : launch_fp4d_nt<2>(a, w, scale, global_scale, c, c_dtype, M, N, K, ch, cnt, part, rowmax, st);
 }
 
 int take_fp4d_wait_status() {

@@ -110,6 +110,17 @@ __device__ __forceinline__ unsigned int atom_inc_acq_rel(unsigned int *p, unsign
     asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(limit) : "memory");
     return old;
 }
+// Row maxima of a decode GEMM's output tile: each value folds |v| into the CTA's shared row
+// maxima (fp32 bits compare like the non-negative floats they are), then after the consumers'
+// barrier one thread per row folds the CTA's maximum into the global one.
+__device__ __forceinline__ void fold_rowmax(unsigned int *rmax, int r, float v) {
+    atomicMax(&rmax[r], __float_as_uint(fabsf(v)));
+}
+template <int CW>
+__device__ __forceinline__ void publish_rowmax(const unsigned int *rmax, unsigned int *rowmax, int rows) {
+    asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
+    if ((int)threadIdx.x < rows) atomicMax(&rowmax[threadIdx.x], rmax[threadIdx.x]);
+}
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 // Thread-block clusters: a full barrier over every thread of every CTA of the

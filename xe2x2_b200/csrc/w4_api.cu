@@ -206,6 +206,18 @@ int w4_gptq_gemm(const void *a, int a_dtype, const int32_t *qweight, const int32
         ws += align256((size_t)M * N * 4);
     }
     const size_t have = workspace_bytes - (size_t)(ws - sync);
+    if (c_dtype == W4_E4M3 && M <= 16 && N % 8 == 0 && aligned(c, 8)) {
+        // decode: the GEMM folds the row maxima of its f32 product into the sync area, so the
+        // cast reads the product once
+        unsigned int *sw = reinterpret_cast<unsigned int *>(sync);
+        rc = w4::gptq_gemv_decode(a_eff, a_dtype, qweight, qzeros, scales, out, W4_F32, M, N, K, group_size,
+                                  zero_offset, sync, split ? ws : nullptr, split < have ? split : have,
+                                  sw + w4::kSyncRowMax, st);
+        if (rc == W4_OK)
+            return w4::rowscale_fp8_amax(static_cast<const float *>(out), sw + w4::kSyncRowMax, sw + w4::kSyncRowCnt,
+                                         static_cast<uint8_t *>(c), row_scale, M, N, st);
+        if (rc != -1) return rc;
+    }
     rc = w4::gptq_gemv(a_eff, a_dtype, qweight, qzeros, scales, out, c_dtype == W4_E4M3 ? W4_F32 : c_dtype, M, N,
                        K, group_size, zero_offset, sync, split ? ws : nullptr, split < have ? split : have, st);
     if (rc || c_dtype != W4_E4M3) return rc;
@@ -333,6 +345,18 @@ int w4_nvfp4_gemm(const void *a, const uint8_t *w, int layout, const void *scale
         wsb += align256((size_t)M * N * 4);
     }
     rc = -1;
+    const size_t have = workspace_bytes - (size_t)(wsb - static_cast<char *>(workspace));
+    if (c_dtype == W4_E4M3 && M < w4::kFp4PrefillMinM && N % 8 == 0 && aligned(c, 8)) {
+        // decode: the GEMM folds the row maxima of its f32 product into the sync area, so the
+        // cast reads the product once
+        unsigned int *sw = static_cast<unsigned int *>(workspace);
+        rc = w4::nvfp4_gemv_decode(static_cast<const uint16_t *>(a), w, scale, scale_dtype, global_scale, out, odt,
+                                   M, N, K, workspace, wsb, have, sw + w4::kSyncRowMax, st);
+        if (rc == W4_OK)
+            return w4::rowscale_fp8_amax(static_cast<const float *>(out), sw + w4::kSyncRowMax, sw + w4::kSyncRowCnt,
+                                         static_cast<uint8_t *>(c), row_scale, M, N, st);
+        if (rc != -1) return rc;
+    }
     if (scale_dtype == W4_E4M3) {
         const size_t split = w4::nvfp4_w4a16_prefill_split_bytes(M, N, K, odt);
         rc = w4::nvfp4_w4a16_prefill(static_cast<const uint16_t *>(a), w, static_cast<const uint8_t *>(scale),
@@ -340,8 +364,7 @@ int w4_nvfp4_gemm(const void *a, const uint8_t *w, int layout, const void *scale
     }
     if (rc == -1)
         rc = w4::nvfp4_gemv(static_cast<const uint16_t *>(a), w, layout, scale, scale_dtype, global_scale, out, odt,
-                            M, N, K, workspace, wsb, workspace_bytes - (size_t)(wsb - static_cast<char *>(workspace)),
-                            st);
+                            M, N, K, workspace, wsb, have, st);
     if (rc || c_dtype != W4_E4M3) return rc;
     return w4::rowscale_fp8(out, W4_F32, static_cast<uint8_t *>(c), row_scale, M, N, st);
 }

@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "w4.h"
+
 namespace w4 {
 
 // gptq.cu
@@ -23,12 +25,19 @@ int gptq_gemv_tma(const void *a, int a_dtype, const int32_t *qweight, const int3
                   const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
                   cudaStream_t st);
 int take_wait_status();
+// The workspace sync area (W4_WORKSPACE_SYNC_BYTES, zero between calls) as 32-bit words: tile
+// counters from word 0, then 16 row maxima (fp32 bits of |y|) and 16 row counters at the end.
+constexpr int kSyncWords = W4_WORKSPACE_SYNC_BYTES / 4;
+constexpr int kSyncTileCounters = kSyncWords - 32;
+constexpr int kSyncRowMax = kSyncWords - 32;
+constexpr int kSyncRowCnt = kSyncWords - 16;
 // gptq_decode.cu: the shared-ring decode GEMM (M <= 16); -1 = shape not handled there.
 // sync: zeroed tile counters (W4_WORKSPACE_SYNC_BYTES); ws: K-split partials of
-// gptq_decode_split_bytes() bytes.  Without them the GEMM runs unsplit.
+// gptq_decode_split_bytes() bytes.  Without them the GEMM runs unsplit.  rowmax (optional): the
+// row maxima of |C| are folded into it with atomicMax on their fp32 bits.
 int gptq_gemv_decode(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
                      const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
-                     void *sync, void *ws, size_t ws_bytes, cudaStream_t st);
+                     void *sync, void *ws, size_t ws_bytes, unsigned int *rowmax, cudaStream_t st);
 size_t gptq_decode_split_bytes(int M, int N, int K, int gs);
 int take_decode_wait_status();
 // w4_api.cu: count a decode call that ran a register-streamed fallback kernel
@@ -85,7 +94,7 @@ int nvfp4_lut_s8a(const int8_t *a, const uint8_t *packed, const float *a_s, cons
 size_t nvfp4_decode_split_bytes(int M, int N, int K);
 int nvfp4_gemv_decode(const uint16_t *a, const uint8_t *w, const void *scale, int scale_dtype,
                       const float *global_scale, void *c, int c_dtype, int M, int N, int K, void *sync, void *ws,
-                      size_t ws_bytes, cudaStream_t st);
+                      size_t ws_bytes, unsigned int *rowmax, cudaStream_t st);
 int take_fp4d_wait_status();
 // nvfp4_prefill.cu (tcgen05 block-scaled); -1 = shape not handled there
 size_t nvfp4_prefill_workspace(int M, int N, int K);
@@ -116,5 +125,9 @@ size_t nvfp4_prefill_q_workspace(int M, int N, int K, bool scale_atoms_needed);
 int splitk_reduce(const float *partial, int splits, long mn, void *c, int c_dtype, cudaStream_t st);
 int rowscale_fp8(const void *y, int y_dtype, uint8_t *q, float *row_scale, int M, int N,
                  cudaStream_t st);
+// The same cast (bit for bit) from f32 y whose row maxima a decode GEMM folded into rowmax (fp32
+// bits, M <= 16); the last CTA of each row zeroes rowmax[row] again, counting on rowcnt[row].
+int rowscale_fp8_amax(const float *y, unsigned int *rowmax, unsigned int *rowcnt, uint8_t *q, float *row_scale,
+                      int M, int N, cudaStream_t st);
 
 }  // namespace w4
