@@ -138,9 +138,9 @@ def _case_fused_row_parallel(rank, world):
                 comm.set_fused_epilogue(False)
                 u32 = lay(xs, out_dtype=torch.float32)
                 comm.wait()
-                # fp32 partials summed in rank order either way; the un-fused GEMM may split K
-                # over a CTA cluster, which changes the order of the fp32 partial sums
-                assert _rel(f32, u32) < 1e-6, (K, N, M)
+                # exact products either way; the fused and the un-fused GEMMs sum them in fp32 in
+                # different orders (the un-fused one per 128-k unit and over a K split)
+                assert _rel(f32, u32) < 1e-5, (K, N, M)
                 assert _rel(f32, full) < 1e-5
                 assert _rel(b16, full) < 1e-2
                 assert _rel(q8.float() * rs[:, None], full) < 4e-2
