@@ -187,6 +187,30 @@ int w4_gptq_gemm_fp8_noalloc(const void *a, int a_dtype, const int32_t *qweight,
  * a_s4 u8 [rows, dk/2] (pack_a, low nibble = even k), b_s4 u8 [dk/2, cols]
  * (pack_b), a_scale f32 [rows], b_scale f16 [dk/128, cols], c f16 [rows, cols].
  * Bit-exact with the reference host oracle (dpas_s4_gptq_sc.cpp:273-288). */
+/* Grouped (MoE) GEMMs: one launch over num_experts experts (1..64).  Expert e's weights are
+ * slice e of stacked tensors and its tokens are rows [offsets[e], offsets[e+1]) of a and c
+ * (host array of num_experts + 1 ints, offsets[0] == 0, nondecreasing; tokens sorted by
+ * expert; empty experts allowed).  The reference runs the routed experts of a MoE layer as
+ * separate GEMMs chained on one queue (kernels/esimd_dpas/moe_group_s8_m1.cpp:1-7; expert shapes
+ * hidden 2688, expert 1856, kernels/nemotron/README.md).  The decode GEMM streams each expert's
+ * weights once per 16 tokens of that expert, so it is meant for decode-sized groups.
+ * GPTQ: qweight [E][K/8][N], qzeros [E][K/gs][N/8] or NULL, scales [E][K/gs][N]; arguments
+ * otherwise as w4_gptq_gemm (no act_order).  c_dtype f16, bf16, f32 or e4m3 (row_scale then
+ * holds one scale per row of c).  The workspace follows the rules of w4_gptq_gemm. */
+size_t w4_gptq_gemm_grouped_workspace_bytes(const int32_t *offsets, int num_experts, int N, int K,
+                                            int group_size, int c_dtype);
+int w4_gptq_gemm_grouped(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
+                         const uint16_t *scales, const int32_t *offsets, int num_experts, void *c,
+                         int c_dtype, float *row_scale, int N, int K, int group_size, int zero_offset,
+                         void *workspace, size_t workspace_bytes, void *stream);
+/* NVFP4 W4A16: w [E][N][K/2] (K-contiguous codes), E4M3 block scales [E][K/16][N], tensor scales
+ * global_scale[E] (fp32, device), bf16 activations; K a multiple of 64, N of 32. */
+size_t w4_nvfp4_gemm_grouped_workspace_bytes(const int32_t *offsets, int num_experts, int N, int K,
+                                             int c_dtype);
+int w4_nvfp4_gemm_grouped(const void *a, const uint8_t *w, const uint8_t *scale, const float *global_scale,
+                          const int32_t *offsets, int num_experts, void *c, int c_dtype, float *row_scale,
+                          int N, int K, void *workspace, size_t workspace_bytes, void *stream);
+
 int w4_gptq_gemm_s4a(const uint8_t *a_s4, const uint8_t *b_s4, const float *a_scale,
                      const uint16_t *b_scale, uint16_t *c, int rows, int cols, int dk,
                      void *stream);

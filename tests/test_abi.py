@@ -152,3 +152,21 @@ def test_python_wrappers_refuse_cpu_tensors_and_missing_scales():
     w = torch.zeros(64, 32, dtype=torch.uint8)
     with pytest.raises(ValueError):
         ops.NVFP4Linear(w, torch.zeros(8, 32, dtype=torch.uint8), torch.ones(1), None, L.W4_ACT_NVFP4)
+
+
+def test_grouped_gemm_checks_offsets_without_gpu():
+    import ctypes
+    lib = L.lib()
+    f = _fake()
+    for off in ((1, 2, 4), (0, 3, 2)):
+        arr = (ctypes.c_int32 * 3)(*off)
+        assert lib.w4_gptq_gemm_grouped_workspace_bytes(arr, 2, 64, 256, 128, L.W4_BF16) == 0
+        rc = lib.w4_gptq_gemm_grouped(f, L.W4_BF16, f, None, f, arr, 2, f, L.W4_BF16, None, 64, 256, 128, 1, f,
+                                      1 << 20, None)
+        assert rc == L.W4_ERR_INVALID and b"offsets" in lib.w4_last_error()
+        rc = lib.w4_nvfp4_gemm_grouped(f, f, f, f, arr, 2, f, L.W4_BF16, None, 64, 256, f, 1 << 20, None)
+        assert rc == L.W4_ERR_INVALID
+    ok = (ctypes.c_int32 * 9)(0, 3, 3, 4, 11, 13, 29, 34, 35)
+    assert lib.w4_gptq_gemm_grouped_workspace_bytes(ok, 8, 1856, 2688, 128, L.W4_BF16) >= L.W4_WORKSPACE_SYNC_BYTES
+    assert lib.w4_nvfp4_gemm_grouped_workspace_bytes(ok, 8, 2688, 1856, L.W4_E4M3) >= \
+        L.W4_WORKSPACE_SYNC_BYTES + 35 * 2688 * 4

@@ -48,6 +48,10 @@ _SIGS = {
     "w4_gptq_repack_act_order": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
     "w4_gptq_workspace_bytes": (_Z, [_I, _I, _I, _I, _I, _I]),
     "w4_gptq_gemm": (_I, [_P, _I, _P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _P, _Z, _P]),
+    "w4_gptq_gemm_grouped_workspace_bytes": (_Z, [_P, _I, _I, _I, _I, _I]),
+    "w4_gptq_gemm_grouped": (_I, [_P, _I, _P, _P, _P, _P, _I, _P, _I, _P, _I, _I, _I, _I, _P, _Z, _P]),
+    "w4_nvfp4_gemm_grouped_workspace_bytes": (_Z, [_P, _I, _I, _I, _I]),
+    "w4_nvfp4_gemm_grouped": (_I, [_P, _P, _P, _P, _P, _I, _P, _I, _P, _I, _I, _P, _Z, _P]),
     "w4_gptq_gemm_s4a": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),
     "w4_gptq_gemm_fp8_noalloc": (_I, [_P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "w4_nvfp4_dequant": (_I, [_P, _I, _P, _I, _P, _I, _I, _P, _P]),

@@ -131,7 +131,8 @@ __device__ __forceinline__ uint32_t pack_h2(__half lo, __half hi) {
 // 4 / GSTEPS units (scale rows) per stage (one row for gs >= 128, read as row stage * 128 / gs).
 // nst: 128-k stages of K, split over the ks CTAs along grid z; max_st: the most stages any CTA of
 // the split holds; S: ring depth.  bf16: activations are bf16 (else f16).  part / cnt (ks > 1):
-// fp32 partials [ks][M][N] and the tile counters (zero on entry, left zero).
+// fp32 partials [ks][M][N] and the tile counters (zero on entry, left zero).  grp: the token rows
+// of each expert (the maps' z coordinate); M: all rows; rows_alloc: token rows a CTA holds.
 // Register cap: 80 per thread with one token tile (five 160-thread CTAs per SM), 128 with two.
 template <int NT> constexpr int dec_regs() { return NT == 1 ? 80 : 128; }
 
@@ -141,12 +142,11 @@ gptq_decode_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_cons
                    const __grid_constant__ CUtensorMap zr_map, const uint16_t *__restrict__ A, void *__restrict__ C,
                    int c_dtype, int M, int N, int K, int has_z, int zero_offset, int nst, int max_st, int gs, int S,
                    int bf16, int pre, float *__restrict__ part, unsigned int *__restrict__ cnt,
-                   unsigned int *__restrict__ rowmax) {
+                   unsigned int *__restrict__ rowmax, const __grid_constant__ ExpertRows grp, int rows_alloc) {
     constexpr int SG = 4 / GSTEPS;
     constexpr int BN = 32 * CW;
     extern __shared__ uint8_t smem_dyn[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
-    const int rows_alloc = min(8 * NT, M);  // every CTA holds the same count (the token blocks of M)
     const int ks = (int)gridDim.z;
     const Lay L(CW, SG, S, max_st, rows_alloc);
     uint64_t *full = reinterpret_cast<uint64_t *>(base + L.bars);
@@ -156,8 +156,9 @@ gptq_decode_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_cons
     uint8_t *act = base + L.act;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int n0 = blockIdx.y * BN;
-    const int tok0 = blockIdx.x * 8 * NT;
-    const int rows = min(8 * NT, M - tok0);  // real token rows of this CTA
+    const int ex = expert_of_block(grp, blockIdx.x);
+    const int tok0 = grp.row0[ex] + ((int)blockIdx.x - grp.blk0[ex]) * 8 * NT;
+    const int rows = min(8 * NT, grp.row0[ex + 1] - tok0);  // real token rows of this CTA
     const int sb = (int)(blockIdx.z * (unsigned)nst / (unsigned)ks);
     const int ns = (int)((blockIdx.z + 1) * (unsigned)nst / (unsigned)ks) - sb;  // stages of this CTA
     const int P = act_pitch(max_st);
@@ -186,9 +187,10 @@ gptq_decode_kernel(const __grid_constant__ CUtensorMap qw_map, const __grid_cons
                 mbar_arrive_expect_tx(&full[s], tx);
 #pragma unroll
                 for (int c = 0; c < CW; ++c)
-                    tma_load_2d(base + s * L.w_stage + c * kRows * 128, &qw_map, n0 + 32 * c, st * kRows, &full[s]);
-                tma_load_2d(base + L.sc + s * L.sc_stage, &sc_map, n0, srow, &full[s]);
-                if (has_z) tma_load_2d(base + L.zr + s * L.zr_stage, &zr_map, n0 / 8, srow, &full[s]);
+                    tma_load_3d(base + s * L.w_stage + c * kRows * 128, &qw_map, n0 + 32 * c, st * kRows, ex,
+                                &full[s]);
+                tma_load_3d(base + L.sc + s * L.sc_stage, &sc_map, n0, srow, ex, &full[s]);
+                if (has_z) tma_load_3d(base + L.zr + s * L.zr_stage, &zr_map, n0 / 8, srow, ex, &full[s]);
                 s = s + 1 == S ? 0 : s + 1;
             };
             // pre: the weights of the first ring fill are requested before the previous kernel on
@@ -495,13 +497,13 @@ int ctas_per_sm(int cw, int NT, int sg, int max_st, int rows) {
 // Tile width and K split.  The grid should be about one wave of CTAs with equal work, so HBM
 // bandwidth is shared evenly: take the widest column tile whose tiles, split over at most 8 CTAs
 // along K, reach the target CTA count (1.8 CTAs per SM with one token tile, 0.9 with two, whose
-// CTAs hold twice the registers), then the smallest K split that reaches it.
-DecChoice choose(int M, int N, int K, int gs, int NT) {
+// CTAs hold twice the registers), then the smallest K split that reaches it.  mblocks: token
+// blocks of the call (over all experts).
+DecChoice choose(int mblocks, int N, int K, int NT) {
     DecChoice c{1, 1, 0};
     if (env_choice(c) && N % (32 * c.cw) == 0) return c;
     const int nsm = num_sms();
     const int nst = (K + dec::kStageK - 1) / dec::kStageK;
-    const int mblocks = (M + 8 * NT - 1) / (8 * NT);
     const int ks_cap = nst / 2 < 1 ? 1 : (nst / 2 > 8 ? 8 : nst / 2);
     const long target = NT == 1 ? (long)(1.8 * nsm) : (long)(0.9 * nsm);
     const int cws[4] = {8, 4, 2, 1};
@@ -517,19 +519,32 @@ DecChoice choose(int M, int N, int K, int gs, int NT) {
     return c;
 }
 
+// One decode GEMM call: E stacked weight matrices, grp.n expert row groups (1 for a plain GEMM).
+struct DecCall {
+    const void *a;
+    int a_dtype;
+    const int32_t *qweight, *qzeros;
+    const uint16_t *scales;
+    void *c;
+    int c_dtype, M, N, K, gs, zero_offset, E, NT, rows_alloc;
+    ExpertRows grp;
+    unsigned int *cnt, *rowmax;
+    float *part;
+};
+
 }  // namespace
 
 template <int CW, int NT, int GSTEPS>
-static int launch_dec_t(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
-                        const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
-                        DecChoice ch, unsigned int *cnt, float *part, unsigned int *rowmax, cudaStream_t st) {
+static int launch_dec_t(const DecCall &q, DecChoice ch, cudaStream_t st) {
     constexpr int SG = 4 / GSTEPS;
     constexpr int BN = 32 * CW;
+    const int N = q.N, K = q.K, gs = q.gs;
     const int nst = (K + dec::kStageK - 1) / dec::kStageK;
     const int ks = ch.ks > nst ? nst : ch.ks;
     const int max_st = (nst + ks - 1) / ks;
-    const int mblocks = (M + 8 * NT - 1) / (8 * NT);
-    const int rows = M < 8 * NT ? M : 8 * NT;
+    const int mblocks = q.grp.blk0[q.grp.n];
+    const int rows = q.rows_alloc;
+    if (mblocks == 0) return W4_OK;  // no token rows
     int S = ch.S;
     if (S == 0) {
         // the CTAs an SM will hold: its limit, or fewer when the grid is smaller than a wave
@@ -542,16 +557,17 @@ static int launch_dec_t(const void *a, int a_dtype, const int32_t *qweight, cons
     }
     const size_t smem = 1024 + (size_t)dec::Lay(CW, SG, S, max_st, rows).total;
     if (smem > (size_t)kSmemPerCta) return -1;
+    const uint64_t E = (uint64_t)q.E, ng = (uint64_t)(K / gs);
     CUtensorMap qw_map, sc_map, zr_map;
-    if (!make_map_2d(&qw_map, CU_TENSOR_MAP_DATA_TYPE_INT32, qweight, N, K / 8, (uint64_t)N * 4, 32, dec::kRows,
-                     CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map_2d(&sc_map, CU_TENSOR_MAP_DATA_TYPE_UINT16, scales, N, K / gs, (uint64_t)N * 2, BN, SG,
+    if (!make_map_3d(&qw_map, CU_TENSOR_MAP_DATA_TYPE_INT32, q.qweight, N, K / 8, E, (uint64_t)N * 4,
+                     (uint64_t)(K / 8) * N * 4, 32, dec::kRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map_3d(&sc_map, CU_TENSOR_MAP_DATA_TYPE_UINT16, q.scales, N, ng, E, (uint64_t)N * 2, ng * N * 2, BN, SG,
                      CU_TENSOR_MAP_SWIZZLE_NONE))
         return -1;
-    const int has_z = qzeros != nullptr;
+    const int has_z = q.qzeros != nullptr;
     if (has_z) {
-        if (!make_map_2d(&zr_map, CU_TENSOR_MAP_DATA_TYPE_INT32, qzeros, N / 8, K / gs, (uint64_t)N / 2, BN / 8, SG,
-                         CU_TENSOR_MAP_SWIZZLE_NONE))
+        if (!make_map_3d(&zr_map, CU_TENSOR_MAP_DATA_TYPE_INT32, q.qzeros, N / 8, ng, E, (uint64_t)N / 2,
+                         ng * N / 2, BN / 8, SG, CU_TENSOR_MAP_SWIZZLE_NONE))
             return -1;
     } else {
         zr_map = sc_map;  // unused
@@ -572,72 +588,111 @@ static int launch_dec_t(const void *a, int a_dtype, const int32_t *qweight, cons
     const int pre = launch_overlap() == W4_OVERLAP_STATIC_WEIGHTS;
     dim3 grid(mblocks, N / BN, ks), block(32 * (CW + 1));
     W4_CUDA_TRY(launch_decode(kern, grid, block, smem, st, 1u, qw_map, sc_map, zr_map,
-                              static_cast<const uint16_t *>(a), c, c_dtype, M, N, K, has_z, zero_offset, nst, max_st,
-                              gs, S, (int)(a_dtype == W4_BF16), pre, part, cnt, rowmax));
+                              static_cast<const uint16_t *>(q.a), q.c, q.c_dtype, q.M, N, K, has_z, q.zero_offset, nst,
+                              max_st, gs, S, (int)(q.a_dtype == W4_BF16), pre, q.part, q.cnt, q.rowmax, q.grp,
+                              q.rows_alloc));
     return W4_OK;
 }
 
 template <int CW, int NT>
-static int launch_dec_g(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
-                        const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
-                        DecChoice ch, unsigned int *cnt, float *part, unsigned int *rowmax, cudaStream_t st) {
-    if (gs % 128 == 0)
-        return launch_dec_t<CW, NT, 4>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch,
-                                       cnt, part, rowmax, st);
-    if (gs == 64)
-        return launch_dec_t<CW, NT, 2>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch,
-                                       cnt, part, rowmax, st);
-    if (gs == 32)
-        return launch_dec_t<CW, NT, 1>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch,
-                                       cnt, part, rowmax, st);
+static int launch_dec_g(const DecCall &q, DecChoice ch, cudaStream_t st) {
+    if (q.gs % 128 == 0) return launch_dec_t<CW, NT, 4>(q, ch, st);
+    if (q.gs == 64) return launch_dec_t<CW, NT, 2>(q, ch, st);
+    if (q.gs == 32) return launch_dec_t<CW, NT, 1>(q, ch, st);
     return -1;
 }
 
 template <int NT>
-static int launch_dec_nt(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
-                         const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
-                         DecChoice ch, unsigned int *cnt, float *part, unsigned int *rowmax, cudaStream_t st) {
+static int launch_dec_nt(const DecCall &q, DecChoice ch, cudaStream_t st) {
     switch (ch.cw) {
-        case 8: return launch_dec_g<8, NT>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch, cnt, part, rowmax, st);
-        case 4: return launch_dec_g<4, NT>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch, cnt, part, rowmax, st);
-        case 2: return launch_dec_g<2, NT>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch, cnt, part, rowmax, st);
-        case 1: return launch_dec_g<1, NT>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch, cnt, part, rowmax, st);
+        case 8: return launch_dec_g<8, NT>(q, ch, st);
+        case 4: return launch_dec_g<4, NT>(q, ch, st);
+        case 2: return launch_dec_g<2, NT>(q, ch, st);
+        case 1: return launch_dec_g<1, NT>(q, ch, st);
         default: return -1;
     }
 }
 
-static bool decode_shape_ok(int M, int N, int K, int gs) {
-    return M >= 1 && M <= 16 && N % 32 == 0 && K % 8 == 0 && (gs % 128 == 0 || gs == 64 || gs == 32);
+static bool decode_shape_ok(int N, int K, int gs) {
+    return N % 32 == 0 && K % 8 == 0 && K % gs == 0 && (gs % 128 == 0 || gs == 64 || gs == 32);
+}
+
+// The most rows of any expert of a call, and the checks of its offsets (off[0] = 0, nondecreasing).
+static int max_rows(const int *off, int n) {
+    if (!off || n < 1 || n > kMaxExperts || off[0] != 0) return -1;
+    int m = 0;
+    for (int e = 0; e < n; ++e) {
+        if (off[e + 1] < off[e]) return -1;
+        m = off[e + 1] - off[e] > m ? off[e + 1] - off[e] : m;
+    }
+    return m;
+}
+
+// The K-split partials a call takes (0: unsplit), for experts with row offsets off[0..n].
+static size_t split_bytes_for(const int *off, int n, int N, int K, int gs) {
+    const int mr = max_rows(off, n);
+    if (mr < 0 || !decode_shape_ok(N, K, gs)) return 0;
+    const int NT = mr <= 8 ? 1 : 2;
+    ExpertRows g;
+    if (!expert_rows(g, off, n, 8 * NT)) return 0;
+    const DecChoice ch = choose(g.blk0[n], N, K, NT);
+    const int nst = (K + dec::kStageK - 1) / dec::kStageK;
+    const int ks = ch.ks > nst ? nst : ch.ks;
+    return ks > 1 ? (size_t)ks * off[n] * N * 4 : 0;
 }
 
 size_t gptq_decode_split_bytes(int M, int N, int K, int gs) {
-    if (!decode_shape_ok(M, N, K, gs)) return 0;
-    const int NT = M <= 8 ? 1 : 2;
-    const DecChoice ch = choose(M, N, K, gs, NT);
-    const int nst = (K + dec::kStageK - 1) / dec::kStageK;
-    const int ks = ch.ks > nst ? nst : ch.ks;
-    return ks > 1 ? (size_t)ks * M * N * 4 : 0;
+    if (M < 1 || M > 16) return 0;
+    const int off[2] = {0, M};
+    return split_bytes_for(off, 1, N, K, gs);
+}
+
+size_t gptq_decode_grouped_split_bytes(const int *off, int n, int N, int K, int gs) {
+    return split_bytes_for(off, n, N, K, gs);
+}
+
+static int run_decode(DecCall &q, const int *off, int n, void *sync, void *ws, size_t ws_bytes, cudaStream_t st) {
+    const int mr = max_rows(off, n);
+    if (mr < 0 || !decode_shape_ok(q.N, q.K, q.gs)) return -1;
+    if (!aligned(q.qweight, 16) || !aligned(q.scales, 16) || (q.qzeros && !aligned(q.qzeros, 16)) || !aligned(q.a, 16))
+        return -1;
+    q.NT = mr <= 8 ? 1 : 2;
+    q.rows_alloc = mr < 8 * q.NT ? mr : 8 * q.NT;
+    q.M = off[n];
+    if (!expert_rows(q.grp, off, n, 8 * q.NT)) return -1;
+    if (q.M == 0) return W4_OK;
+    DecChoice ch = choose(q.grp.blk0[n], q.N, q.K, q.NT);
+    const int nst = (q.K + dec::kStageK - 1) / dec::kStageK;
+    if (ch.ks > nst) ch.ks = nst;
+    const long tiles = (long)(q.N / (32 * ch.cw)) * q.grp.blk0[n];
+    // The K split needs the workspace: fp32 partials and one counter per tile in the sync area.
+    if (ch.ks > 1 && (!sync || !ws || !aligned(ws, 16) || ws_bytes < (size_t)ch.ks * q.M * q.N * 4 ||
+                      tiles > (long)kSyncTileCounters))
+        ch.ks = 1;
+    q.cnt = static_cast<unsigned int *>(sync);
+    q.part = static_cast<float *>(ws);
+    if (q.NT == 1) return launch_dec_nt<1>(q, ch, st);
+    return launch_dec_nt<2>(q, ch, st);
 }
 
 int gptq_gemv_decode(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
                      const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
                      void *sync, void *ws, size_t ws_bytes, unsigned int *rowmax, cudaStream_t st) {
-    if (!decode_shape_ok(M, N, K, gs)) return -1;
-    if (!aligned(qweight, 16) || !aligned(scales, 16) || (qzeros && !aligned(qzeros, 16)) || !aligned(a, 16)) return -1;
-    const int NT = M <= 8 ? 1 : 2;
-    DecChoice ch = choose(M, N, K, gs, NT);
-    const int nst = (K + dec::kStageK - 1) / dec::kStageK;
-    if (ch.ks > nst) ch.ks = nst;
-    const long tiles = (long)(N / (32 * ch.cw)) * ((M + 8 * NT - 1) / (8 * NT));
-    // The K split needs the workspace: fp32 partials and one counter per tile in the sync area.
-    if (ch.ks > 1 && (!sync || !ws || !aligned(ws, 16) || ws_bytes < (size_t)ch.ks * M * N * 4 ||
-                      tiles > (long)kSyncTileCounters))
-        ch.ks = 1;
-    unsigned int *cnt = static_cast<unsigned int *>(sync);
-    float *part = static_cast<float *>(ws);
-    if (NT == 1)
-        return launch_dec_nt<1>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch, cnt, part, rowmax, st);
-    return launch_dec_nt<2>(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ch, cnt, part, rowmax, st);
+    if (M < 1 || M > 16) return -1;
+    DecCall q{};
+    q.a = a, q.a_dtype = a_dtype, q.qweight = qweight, q.qzeros = qzeros, q.scales = scales, q.c = c;
+    q.c_dtype = c_dtype, q.N = N, q.K = K, q.gs = gs, q.zero_offset = zero_offset, q.E = 1, q.rowmax = rowmax;
+    const int off[2] = {0, M};
+    return run_decode(q, off, 1, sync, ws, ws_bytes, st);
+}
+
+int gptq_gemv_decode_grouped(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
+                             const uint16_t *scales, const int *off, int n, void *c, int c_dtype, int N, int K, int gs,
+                             int zero_offset, void *sync, void *ws, size_t ws_bytes, cudaStream_t st) {
+    DecCall q{};
+    q.a = a, q.a_dtype = a_dtype, q.qweight = qweight, q.qzeros = qzeros, q.scales = scales, q.c = c;
+    q.c_dtype = c_dtype, q.N = N, q.K = K, q.gs = gs, q.zero_offset = zero_offset, q.E = n, q.rowmax = nullptr;
+    return run_decode(q, off, n, sync, ws, ws_bytes, st);
 }
 
 int take_decode_wait_status() {

@@ -129,12 +129,12 @@ template <int CW, int NT>
 __global__ void __maxnreg__((fp4d_regs<NT>()))
 nvfp4_decode_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap sc_map,
                     const uint16_t *__restrict__ A, const float *__restrict__ global_scale, void *__restrict__ C,
-                    int c_dtype, int M, int N, int K, int nst, int max_st, int S, int pre,
+                    int c_dtype, int M, int N, int K, int nst, int max_st, int S, int pre, int rows_alloc,
+                    const __grid_constant__ ExpertRows grp,
                     float *__restrict__ part, unsigned int *__restrict__ cnt, unsigned int *__restrict__ rowmax) {
     constexpr int BN = 32 * CW;
     extern __shared__ uint8_t smem_dyn[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
-    const int rows_alloc = min(8 * NT, M);  // every CTA holds the same count
     const Lay L(CW, S, max_st, rows_alloc);
     uint64_t *full = reinterpret_cast<uint64_t *>(base + L.bars);
     uint64_t *empty = full + S;
@@ -142,8 +142,9 @@ nvfp4_decode_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
     float *inv = reinterpret_cast<float *>(base + L.inv);
     uint8_t *act = base + L.act;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int tok0 = blockIdx.x * 8 * NT;
-    const int rows = min(8 * NT, M - tok0);  // real token rows of this CTA
+    const int ex = expert_of_block(grp, blockIdx.x);
+    const int tok0 = grp.row0[ex] + ((int)blockIdx.x - grp.blk0[ex]) * 8 * NT;
+    const int rows = min(8 * NT, grp.row0[ex + 1] - tok0);  // real token rows of this CTA
     const int n0 = blockIdx.y * BN;
     const int ks = (int)gridDim.z;
     const int sb = (int)(blockIdx.z * (unsigned)nst / (unsigned)ks);
@@ -172,8 +173,9 @@ nvfp4_decode_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
                 mbar_arrive_expect_tx(&full[s], tx);
 #pragma unroll
                 for (int c = 0; c < CW; ++c)
-                    tma_load_2d(base + s * L.w_stage + c * 32 * 128, &w_map, st * (KS / 2), n0 + 32 * c, &full[s]);
-                tma_load_2d(base + L.sc + s * L.s_stage, &sc_map, n0, st * (KS / 16), &full[s]);
+                    tma_load_3d(base + s * L.w_stage + c * 32 * 128, &w_map, st * (KS / 2), n0 + 32 * c, ex,
+                                &full[s]);
+                tma_load_3d(base + L.sc + s * L.s_stage, &sc_map, n0, st * (KS / 16), ex, &full[s]);
                 if (++s == S) {
                     s = 0;
                     ++wraps;
@@ -354,7 +356,7 @@ nvfp4_decode_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
     grid_dep_launch();  // late trigger: the next grid's CTAs take the slots this one frees
 
     // ---- output: lane element (mt, nt, i) is column colw + 2mt + (i >> 1), token 8nt + 2t + (i & 1)
-    const float gsc = global_scale ? *global_scale : 1.0f;
+    const float gsc = global_scale ? global_scale[ex] : 1.0f;
     if (ks == 1) {
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt)
@@ -455,13 +457,13 @@ int fp4_ctas_per_sm(int cw, int NT, int max_st, int rows) {
 
 // Tile width and K split: the grid should be about one wave of CTAs with equal work.  Take the
 // widest column tile whose tiles, split over at most 8 CTAs along K (at least two stages each),
-// reach 1.8 CTAs per SM, then the smallest K split that reaches it.
-Fp4Choice fp4_choose(int M, int N, int K, int NT) {
+// reach 1.8 CTAs per SM, then the smallest K split that reaches it.  mblocks: token blocks of the
+// call (over all experts).
+Fp4Choice fp4_choose(int mblocks, int N, int K) {
     Fp4Choice c{1, 1, 0};
     if (env_fp4_choice(c) && N % (32 * c.cw) == 0) return c;
     const int nsm = num_sms();
     const int nst = (K + fp4d::KS - 1) / fp4d::KS;
-    const int mblocks = (M + 8 * NT - 1) / (8 * NT);
     const int ks_cap = nst / 2 < 1 ? 1 : (nst / 2 > 8 ? 8 : nst / 2);
     const long target = (long)(1.8 * nsm);
     const int cws[4] = {8, 4, 2, 1};
@@ -477,18 +479,31 @@ Fp4Choice fp4_choose(int M, int N, int K, int NT) {
     return c;
 }
 
+// One decode GEMM call: E stacked weight matrices, grp.n expert row groups (1 for a plain GEMM).
+struct Fp4Call {
+    const uint16_t *a;
+    const uint8_t *w;
+    const void *scale;
+    const float *global_scale;  // one per expert
+    void *c;
+    int c_dtype, M, N, K, E, NT, rows_alloc;
+    ExpertRows grp;
+    unsigned int *cnt, *rowmax;
+    float *part;
+};
+
 }  // namespace
 
 template <int CW, int NT>
-static int launch_fp4d_t(const uint16_t *a, const uint8_t *w, const void *scale, const float *global_scale, void *c,
-                         int c_dtype, int M, int N, int K, Fp4Choice ch, unsigned int *cnt, float *part,
-                         unsigned int *rowmax, cudaStream_t st) {
+static int launch_fp4d_t(const Fp4Call &q, Fp4Choice ch, cudaStream_t st) {
     constexpr int BN = 32 * CW;
+    const int N = q.N, K = q.K;
     const int nst = (K + fp4d::KS - 1) / fp4d::KS;
     const int ks = ch.ks > nst ? nst : ch.ks;
     const int max_st = (nst + ks - 1) / ks;
-    const int mblocks = (M + 8 * NT - 1) / (8 * NT);
-    const int rows = M < 8 * NT ? M : 8 * NT;
+    const int mblocks = q.grp.blk0[q.grp.n];
+    const int rows = q.rows_alloc;
+    if (mblocks == 0) return W4_OK;  // no token rows
     int S = ch.S;
     if (S == 0) {
         // the CTAs an SM will hold: its limit, or fewer when the grid is smaller than a wave
@@ -504,11 +519,12 @@ static int launch_fp4d_t(const uint16_t *a, const uint8_t *w, const void *scale,
     }
     const size_t smem = 1024 + (size_t)fp4d::Lay(CW, S, max_st, rows).total;
     if (smem > (size_t)kSmemPerCta) return -1;
+    const uint64_t E = (uint64_t)q.E;
     CUtensorMap w_map, sc_map;
-    if (!make_map_2d(&w_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)K / 2, N, (uint64_t)K / 2, fp4d::KS / 2, 32,
-                     CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map_2d(&sc_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, scale, N, K / 16, (uint64_t)N, BN, 16,
-                     CU_TENSOR_MAP_SWIZZLE_NONE))
+    if (!make_map_3d(&w_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, q.w, (uint64_t)K / 2, N, E, (uint64_t)K / 2,
+                     (uint64_t)N * K / 2, fp4d::KS / 2, 32, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map_3d(&sc_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, q.scale, N, K / 16, E, (uint64_t)N, (uint64_t)N * (K / 16),
+                     BN, 16, CU_TENSOR_MAP_SWIZZLE_NONE))
         return -1;
     auto kern = fp4d::nvfp4_decode_kernel<CW, NT>;
     {
@@ -525,55 +541,101 @@ static int launch_fp4d_t(const uint16_t *a, const uint8_t *w, const void *scale,
     }
     const int pre = launch_overlap() == W4_OVERLAP_STATIC_WEIGHTS;
     dim3 grid(mblocks, N / BN, ks), block(32 * (CW + 1));
-    W4_CUDA_TRY(launch_decode(kern, grid, block, smem, st, 1u, w_map, sc_map, a, global_scale, c, c_dtype, M, N, K,
-                              nst, max_st, S, pre, part, cnt, rowmax));
+    W4_CUDA_TRY(launch_decode(kern, grid, block, smem, st, 1u, w_map, sc_map, q.a, q.global_scale, q.c, q.c_dtype, q.M,
+                              N, K, nst, max_st, S, pre, q.rows_alloc, q.grp, q.part, q.cnt, q.rowmax));
     return W4_OK;
 }
 
 template <int NT>
-static int launch_fp4d_nt(const uint16_t *a, const uint8_t *w, const void *scale, const float *global_scale,
-                          void *c, int c_dtype, int M, int N, int K, Fp4Choice ch, unsigned int *cnt, float *part,
-                          unsigned int *rowmax, cudaStream_t st) {
+static int launch_fp4d_nt(const Fp4Call &q, Fp4Choice ch, cudaStream_t st) {
     switch (ch.cw) {
-        case 8: return launch_fp4d_t<8, NT>(a, w, scale, global_scale, c, c_dtype, M, N, K, ch, cnt, part, rowmax, st);
-        case 4: return launch_fp4d_t<4, NT>(a, w, scale, global_scale, c, c_dtype, M, N, K, ch, cnt, part, rowmax, st);
-        case 2: return launch_fp4d_t<2, NT>(a, w, scale, global_scale, c, c_dtype, M, N, K, ch, cnt, part, rowmax, st);
-        case 1: return launch_fp4d_t<1, NT>(a, w, scale, global_scale, c, c_dtype, M, N, K, ch, cnt, part, rowmax, st);
+        case 8: return launch_fp4d_t<8, NT>(q, ch, st);
+        case 4: return launch_fp4d_t<4, NT>(q, ch, st);
+        case 2: return launch_fp4d_t<2, NT>(q, ch, st);
+        case 1: return launch_fp4d_t<1, NT>(q, ch, st);
         default: return -1;
     }
 }
 
-static bool fp4_decode_shape_ok(int M, int N, int K) { return M >= 1 && N % 32 == 0 && K % 128 == 0; }
+// K a multiple of 64: whole 16-k scale blocks and 16-byte activation copies; a partial last stage
+// reads zero codes, scales and activations.
+static bool fp4_decode_shape_ok(int N, int K) { return N % 32 == 0 && K % 64 == 0; }
 
-size_t nvfp4_decode_split_bytes(int M, int N, int K) {
-    if (!fp4_decode_shape_ok(M, N, K)) return 0;
-    const int NT = M <= 8 ? 1 : 2;
-    const Fp4Choice ch = fp4_choose(M, N, K, NT);
+static int fp4_max_rows(const int *off, int n) {
+    if (!off || n < 1 || n > kMaxExperts || off[0] != 0) return -1;
+    int m = 0;
+    for (int e = 0; e < n; ++e) {
+        if (off[e + 1] < off[e]) return -1;
+        m = off[e + 1] - off[e] > m ? off[e + 1] - off[e] : m;
+    }
+    return m;
+}
+
+static size_t fp4_split_bytes_for(const int *off, int n, int N, int K) {
+    const int mr = fp4_max_rows(off, n);
+    if (mr < 0 || !fp4_decode_shape_ok(N, K)) return 0;
+    const int NT = mr <= 8 ? 1 : 2;
+    ExpertRows g;
+    if (!expert_rows(g, off, n, 8 * NT)) return 0;
+    const Fp4Choice ch = fp4_choose(g.blk0[n], N, K);
     const int nst = (K + fp4d::KS - 1) / fp4d::KS;
     const int ks = ch.ks > nst ? nst : ch.ks;
-    return ks > 1 ? (size_t)ks * M * N * 4 : 0;
+    return ks > 1 ? (size_t)ks * off[n] * N * 4 : 0;
+}
+
+size_t nvfp4_decode_split_bytes(int M, int N, int K) {
+    if (M < 1) return 0;
+    const int off[2] = {0, M};
+    return fp4_split_bytes_for(off, 1, N, K);
+}
+
+size_t nvfp4_decode_grouped_split_bytes(const int *off, int n, int N, int K) {
+    return fp4_split_bytes_for(off, n, N, K);
+}
+
+static int run_fp4_decode(Fp4Call &q, const int *off, int n, int scale_dtype, void *sync, void *ws, size_t ws_bytes,
+                          cudaStream_t st) {
+    const int mr = fp4_max_rows(off, n);
+    if (mr < 0 || !fp4_decode_shape_ok(q.N, q.K)) return -1;
+    // E4M3 block scales only: a bf16 scale times an e2m1 code need not be an f16
+    if (scale_dtype != W4_E4M3 || !aligned(q.a, 16) || !aligned(q.w, 16) || !aligned(q.scale, 16)) return -1;
+    q.NT = mr <= 8 ? 1 : 2;
+    q.rows_alloc = mr < 8 * q.NT ? mr : 8 * q.NT;
+    q.M = off[n];
+    if (!expert_rows(q.grp, off, n, 8 * q.NT)) return -1;
+    if (q.M == 0) return W4_OK;
+    Fp4Choice ch = fp4_choose(q.grp.blk0[n], q.N, q.K);
+    const int nst = (q.K + fp4d::KS - 1) / fp4d::KS;
+    if (ch.ks > nst) ch.ks = nst;
+    const long tiles = (long)(q.N / (32 * ch.cw)) * q.grp.blk0[n];
+    // The K split needs the workspace: fp32 partials and one counter per tile in the sync area.
+    if (ch.ks > 1 && (!sync || !ws || !aligned(ws, 16) || ws_bytes < (size_t)ch.ks * q.M * q.N * 4 ||
+                      tiles > (long)kSyncTileCounters))
+        ch.ks = 1;
+    q.cnt = static_cast<unsigned int *>(sync);
+    q.part = static_cast<float *>(ws);
+    return q.NT == 1 ? launch_fp4d_nt<1>(q, ch, st) : launch_fp4d_nt<2>(q, ch, st);
 }
 
 // W4_OK / a W4 error, or -1 when the shape or tensor maps are not handled here.
 int nvfp4_gemv_decode(const uint16_t *a, const uint8_t *w, const void *scale, int scale_dtype,
                       const float *global_scale, void *c, int c_dtype, int M, int N, int K, void *sync, void *ws,
                       size_t ws_bytes, unsigned int *rowmax, cudaStream_t st) {
-    if (!fp4_decode_shape_ok(M, N, K)) return -1;
-    // E4M3 block scales only: a bf16 scale times an e2m1 code need not be an f16
-    if (scale_dtype != W4_E4M3 || !aligned(a, 16) || !aligned(w, 16) || !aligned(scale, 16)) return -1;
-    const int NT = M <= 8 ? 1 : 2;
-    Fp4Choice ch = fp4_choose(M, N, K, NT);
-    const int nst = (K + fp4d::KS - 1) / fp4d::KS;
-    if (ch.ks > nst) ch.ks = nst;
-    const long tiles = (long)(N / (32 * ch.cw)) * ((M + 8 * NT - 1) / (8 * NT));
-    // The K split needs the workspace: fp32 partials and one counter per tile in the sync area.
-    if (ch.ks > 1 && (!sync || !ws || !aligned(ws, 16) || ws_bytes < (size_t)ch.ks * M * N * 4 ||
-                      tiles > (long)kSyncTileCounters))
-        ch.ks = 1;
-    unsigned int *cnt = static_cast<unsigned int *>(sync);
-    float *part = static_cast<float *>(ws);
-    return NT == 1 ? launch_fp4d_nt<1>(a, w, scale, global_scale, c, c_dtype, M, N, K, ch, cnt, part, rowmax, st)
-                   : launch_fp4d_nt<2>(a, w, scale, global_scale, c, c_dtype, M, N, K, ch, cnt, part, rowmax, st);
+    if (M < 1) return -1;
+    Fp4Call q{};
+    q.a = a, q.w = w, q.scale = scale, q.global_scale = global_scale, q.c = c, q.c_dtype = c_dtype;
+    q.N = N, q.K = K, q.E = 1, q.rowmax = rowmax;
+    const int off[2] = {0, M};
+    return run_fp4_decode(q, off, 1, scale_dtype, sync, ws, ws_bytes, st);
+}
+
+int nvfp4_gemv_decode_grouped(const uint16_t *a, const uint8_t *w, const void *scale, int scale_dtype,
+                              const float *global_scale, const int *off, int n, void *c, int c_dtype, int N, int K,
+                              void *sync, void *ws, size_t ws_bytes, cudaStream_t st) {
+    Fp4Call q{};
+    q.a = a, q.w = w, q.scale = scale, q.global_scale = global_scale, q.c = c, q.c_dtype = c_dtype;
+    q.N = N, q.K = K, q.E = n, q.rowmax = nullptr;
+    return run_fp4_decode(q, off, n, scale_dtype, sync, ws, ws_bytes, st);
 }
 
 int take_fp4d_wait_status() {

@@ -11,6 +11,7 @@
 #include <utility>
 
 #include "w4_common.cuh"
+#include "w4_internal.h"
 
 namespace w4 {
 
@@ -190,6 +191,43 @@ inline cudaError_t launch_decode(void (*kern)(KArgs...), dim3 grid, dim3 block, 
     cfg.attrs = at;
     cfg.numAttrs = n;
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+// 3-D tiled map of [d2][d1][d0] elements (d0 innermost; byte strides s1 of d1 and s2 of d2), box
+// {b0, b1, 1}: the decode GEMMs read stacked per-expert matrices with the expert as z.
+inline bool make_map_3d(CUtensorMap *map, CUtensorMapDataType dt, const void *ptr, uint64_t d0, uint64_t d1,
+                        uint64_t d2, uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, CUtensorMapSwizzle swz) {
+    PFN_cuTensorMapEncodeTiled fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[3] = {d0, d1, d2};
+    const cuuint64_t strides[2] = {s1, s2};
+    const cuuint32_t box[3] = {b0, b1, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, dt, 3, const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The token rows of a decode GEMM call as expert groups: expert e owns rows [row0[e], row0[e+1])
+// of A and C and token blocks [blk0[e], blk0[e+1]) of grid x.  One group for a plain GEMM.
+struct ExpertRows {
+    int n;
+    int blk0[kMaxExperts + 1];
+    int row0[kMaxExperts + 1];
+};
+__device__ __forceinline__ int expert_of_block(const ExpertRows &g, int b) {
+    int e = 0;
+    while (e + 1 < g.n && g.blk0[e + 1] <= b) ++e;
+    return e;
+}
+// Host: the table for experts with row offsets off[0..n] (off[0] = 0, nondecreasing) and token
+// blocks of `per` rows; false if n is out of range.
+inline bool expert_rows(ExpertRows &g, const int *off, int n, int per) {
+    if (n < 1 || n > kMaxExperts) return false;
+    g.n = n;
+    g.blk0[0] = 0;
+    for (int e = 0; e <= n; ++e) g.row0[e] = off[e];
+    for (int e = 0; e < n; ++e) g.blk0[e + 1] = g.blk0[e] + (off[e + 1] - off[e] + per - 1) / per;
+    return true;
 }
 
 inline bool make_map_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *ptr, uint64_t d0, uint64_t d1,

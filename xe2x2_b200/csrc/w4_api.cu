@@ -224,6 +224,109 @@ int w4_gptq_gemm(const void *a, int a_dtype, const int32_t *qweight, const int32
     return w4::rowscale_fp8(static_cast<const float *>(out), W4_F32, static_cast<uint8_t *>(c), row_scale, M, N, st);
 }
 
+// ------------------------------------------------------------------ grouped (MoE)
+static int check_offsets(const int32_t *off, int n, int *rows) {
+    W4_REQUIRE(off && n >= 1 && n <= w4::kMaxExperts, W4_ERR_INVALID, "offsets and 1..%d experts are required",
+               w4::kMaxExperts);
+    W4_REQUIRE(off[0] == 0, W4_ERR_INVALID, "offsets[0] must be 0");
+    for (int e = 0; e < n; ++e)
+        W4_REQUIRE(off[e + 1] >= off[e], W4_ERR_INVALID, "offsets must be nondecreasing (expert %d)", e);
+    *rows = off[n];
+    return W4_OK;
+}
+
+size_t w4_gptq_gemm_grouped_workspace_bytes(const int32_t *offsets, int num_experts, int N, int K, int group_size,
+                                            int c_dtype) {
+    int rows = 0;
+    if (check_offsets(offsets, num_experts, &rows) || N <= 0 || K <= 0 || group_size <= 0) return 0;
+    size_t ws = W4_WORKSPACE_SYNC_BYTES;
+    if (c_dtype == W4_E4M3) ws += align256((size_t)rows * N * 4);
+    return ws + align256(w4::gptq_decode_grouped_split_bytes(offsets, num_experts, N, K, group_size));
+}
+
+int w4_gptq_gemm_grouped(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
+                         const uint16_t *scales, const int32_t *offsets, int num_experts, void *c, int c_dtype,
+                         float *row_scale, int N, int K, int group_size, int zero_offset, void *workspace,
+                         size_t workspace_bytes, void *stream) {
+    w4::set_error("");
+    int rows = 0;
+    int rc = check_offsets(offsets, num_experts, &rows);
+    if (rc) return rc;
+    rc = w4::check_gptq_gemm(a, a_dtype, qweight, scales, c, c_dtype, row_scale, rows > 0 ? rows : 1, N, K,
+                             group_size);
+    if (rc) return rc;
+    const size_t need = w4_gptq_gemm_grouped_workspace_bytes(offsets, num_experts, N, K, group_size, c_dtype);
+    W4_REQUIRE(workspace_bytes >= need && workspace && aligned(workspace, 256), W4_ERR_INVALID,
+               "a 256-byte aligned workspace of %zu bytes is needed (%zu given), its first %d bytes zero", need,
+               workspace_bytes, W4_WORKSPACE_SYNC_BYTES);
+    if (rows == 0) return W4_OK;
+    cudaStream_t st = S(stream);
+    char *sync = static_cast<char *>(workspace);
+    char *ws = sync + W4_WORKSPACE_SYNC_BYTES;
+    void *out = c;
+    if (c_dtype == W4_E4M3) {
+        out = ws;
+        ws += align256((size_t)rows * N * 4);
+    }
+    rc = w4::gptq_gemv_decode_grouped(a, a_dtype, qweight, qzeros, scales, offsets, num_experts, out,
+                                      c_dtype == W4_E4M3 ? W4_F32 : c_dtype, N, K, group_size, zero_offset, sync, ws,
+                                      workspace_bytes - (size_t)(ws - sync), st);
+    if (rc == -1) {
+        w4::set_error("grouped GPTQ GEMM: shape not handled (N %% 32, K %% 8, group size 32, 64 or a multiple of "
+                      "128, 16-byte aligned tensors)");
+        return W4_ERR_UNSUPPORTED;
+    }
+    if (rc || c_dtype != W4_E4M3) return rc;
+    return w4::rowscale_fp8(out, W4_F32, static_cast<uint8_t *>(c), row_scale, rows, N, st);
+}
+
+size_t w4_nvfp4_gemm_grouped_workspace_bytes(const int32_t *offsets, int num_experts, int N, int K, int c_dtype) {
+    int rows = 0;
+    if (check_offsets(offsets, num_experts, &rows) || N <= 0 || K <= 0) return 0;
+    size_t ws = W4_WORKSPACE_SYNC_BYTES;
+    if (c_dtype == W4_E4M3) ws += align256((size_t)rows * N * 4);
+    return ws + align256(w4::nvfp4_decode_grouped_split_bytes(offsets, num_experts, N, K));
+}
+
+int w4_nvfp4_gemm_grouped(const void *a, const uint8_t *w, const uint8_t *scale, const float *global_scale,
+                          const int32_t *offsets, int num_experts, void *c, int c_dtype, float *row_scale, int N, int K,
+                          void *workspace, size_t workspace_bytes, void *stream) {
+    w4::set_error("");
+    int rows = 0;
+    int rc = check_offsets(offsets, num_experts, &rows);
+    if (rc) return rc;
+    W4_REQUIRE(a && w && scale && global_scale && c, W4_ERR_INVALID, "a, w, scale, global_scale and c are required");
+    W4_REQUIRE(N > 0 && K > 0 && N % 32 == 0 && K % 64 == 0, W4_ERR_UNSUPPORTED,
+               "need N %% 32 == 0 and K %% 64 == 0 (N=%d K=%d)", N, K);
+    W4_REQUIRE(c_dtype == W4_F16 || c_dtype == W4_BF16 || c_dtype == W4_F32 || c_dtype == W4_E4M3, W4_ERR_INVALID,
+               "c_dtype must be f16, bf16, f32 or e4m3");
+    W4_REQUIRE(c_dtype != W4_E4M3 || row_scale, W4_ERR_INVALID, "e4m3 output needs row_scale");
+    W4_REQUIRE(aligned(a, 16) && aligned(w, 16) && aligned(scale, 16), W4_ERR_INVALID,
+               "a, w and scale must be 16-byte aligned");
+    const size_t need = w4_nvfp4_gemm_grouped_workspace_bytes(offsets, num_experts, N, K, c_dtype);
+    W4_REQUIRE(workspace_bytes >= need && workspace && aligned(workspace, 256), W4_ERR_INVALID,
+               "a 256-byte aligned workspace of %zu bytes is needed (%zu given), its first %d bytes zero", need,
+               workspace_bytes, W4_WORKSPACE_SYNC_BYTES);
+    if (rows == 0) return W4_OK;
+    cudaStream_t st = S(stream);
+    char *sync = static_cast<char *>(workspace);
+    char *ws = sync + W4_WORKSPACE_SYNC_BYTES;
+    void *out = c;
+    if (c_dtype == W4_E4M3) {
+        out = ws;
+        ws += align256((size_t)rows * N * 4);
+    }
+    rc = w4::nvfp4_gemv_decode_grouped(static_cast<const uint16_t *>(a), w, scale, W4_E4M3, global_scale, offsets,
+                                       num_experts, out, c_dtype == W4_E4M3 ? W4_F32 : c_dtype, N, K, sync, ws,
+                                       workspace_bytes - (size_t)(ws - sync), st);
+    if (rc == -1) {
+        w4::set_error("grouped NVFP4 GEMM: shape not handled by the decode kernel");
+        return W4_ERR_UNSUPPORTED;
+    }
+    if (rc || c_dtype != W4_E4M3) return rc;
+    return w4::rowscale_fp8(out, W4_F32, static_cast<uint8_t *>(c), row_scale, rows, N, st);
+}
+
 int w4_gptq_gemm_s4a(const uint8_t *a_s4, const uint8_t *b_s4, const float *a_scale,
                      const uint16_t *b_scale, uint16_t *c, int rows, int cols, int dk,
                      void *stream) {

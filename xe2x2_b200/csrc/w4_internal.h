@@ -27,6 +27,7 @@ int gptq_gemv_tma(const void *a, int a_dtype, const int32_t *qweight, const int3
 int take_wait_status();
 // The workspace sync area (W4_WORKSPACE_SYNC_BYTES, zero between calls) as 32-bit words: tile
 // counters from word 0, then 16 row maxima (fp32 bits of |y|) and 16 row counters at the end.
+constexpr int kMaxExperts = 64;  // expert groups of one grouped (MoE) GEMM call
 constexpr int kSyncWords = W4_WORKSPACE_SYNC_BYTES / 4;
 constexpr int kSyncTileCounters = kSyncWords - 32;
 constexpr int kSyncRowMax = kSyncWords - 32;
@@ -39,6 +40,12 @@ int gptq_gemv_decode(const void *a, int a_dtype, const int32_t *qweight, const i
                      const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
                      void *sync, void *ws, size_t ws_bytes, unsigned int *rowmax, cudaStream_t st);
 size_t gptq_decode_split_bytes(int M, int N, int K, int gs);
+// Grouped (MoE) form: expert e's weights are slice e of stacked [E][...] tensors and its token
+// rows are [off[e], off[e+1]) of a and c (host offsets, off[0] = 0, at most 64 experts).
+int gptq_gemv_decode_grouped(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
+                             const uint16_t *scales, const int *off, int n, void *c, int c_dtype, int N, int K, int gs,
+                             int zero_offset, void *sync, void *ws, size_t ws_bytes, cudaStream_t st);
+size_t gptq_decode_grouped_split_bytes(const int *off, int n, int N, int K, int gs);
 int take_decode_wait_status();
 // w4_api.cu: count a decode call that ran a register-streamed fallback kernel
 void note_decode_fallback();
@@ -96,6 +103,10 @@ int nvfp4_gemv_decode(const uint16_t *a, const uint8_t *w, const void *scale, in
                       const float *global_scale, void *c, int c_dtype, int M, int N, int K, void *sync, void *ws,
                       size_t ws_bytes, unsigned int *rowmax, cudaStream_t st);
 int take_fp4d_wait_status();
+int nvfp4_gemv_decode_grouped(const uint16_t *a, const uint8_t *w, const void *scale, int scale_dtype,
+                              const float *global_scale, const int *off, int n, void *c, int c_dtype, int N, int K,
+                              void *sync, void *ws, size_t ws_bytes, cudaStream_t st);
+size_t nvfp4_decode_grouped_split_bytes(const int *off, int n, int N, int K);
 // nvfp4_prefill.cu (tcgen05 block-scaled); -1 = shape not handled there
 size_t nvfp4_prefill_workspace(int M, int N, int K);
 int nvfp4_prefill(const uint16_t *a, const float *a_global, const uint8_t *w_nk, const uint8_t *w_sf,

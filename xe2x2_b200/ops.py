@@ -385,6 +385,57 @@ def rowscale_fp8(y):
 _registered = False
 
 
+# ===================================================================== grouped (MoE)
+def _offsets(offsets, E):
+    off = [int(x) for x in (offsets.tolist() if torch.is_tensor(offsets) else offsets)]
+    if len(off) != E + 1:
+        raise ValueError(f"offsets must hold num_experts + 1 = {E + 1} entries, got {len(off)}")
+    return (ctypes.c_int32 * len(off))(*off), off[-1]
+
+
+def gptq_gemm_grouped(a, qweight, qzeros, scales, offsets, group_size=128, zero_offset=1, out_dtype=None):
+    """Grouped (MoE) GPTQ GEMM in one launch: expert e multiplies rows [offsets[e], offsets[e+1])
+    of ``a`` (tokens sorted by expert) by its slice of the stacked weights qweight [E, K/8, N],
+    qzeros [E, K/gs, N/8] or None, scales [E, K/gs, N].  ``offsets``: E + 1 host ints from 0.
+    Returns [rows, N] (and the row scales for an fp8 output)."""
+    _need_cuda(a, qweight, qzeros, scales)
+    for t, n in ((a, "a"), (qweight, "qweight"), (qzeros, "qzeros"), (scales, "scales")):
+        _contig(t, n)
+    E, K8, N = qweight.shape
+    K = K8 * 8
+    off, rows = _offsets(offsets, E)
+    if a.shape != (rows, K):
+        raise ValueError(f"a must be [{rows}, {K}], got {tuple(a.shape)}")
+    out_dtype = out_dtype or a.dtype
+    c = torch.empty((rows, N), dtype=out_dtype, device=a.device)
+    rs = torch.empty(rows, dtype=torch.float32, device=a.device) if out_dtype == torch.float8_e4m3fn else None
+    need = L.lib().w4_gptq_gemm_grouped_workspace_bytes(off, E, N, K, group_size, _DT[out_dtype])
+    ws, wsb = _WS.get(a.device, need)
+    L.call("w4_gptq_gemm_grouped", _p(a), _DT[a.dtype], _p(qweight), _p(qzeros), _p(scales), off, E, _p(c),
+           _DT[out_dtype], _p(rs), N, K, group_size, zero_offset, _p(ws), wsb, _stream(a.device))
+    return (c, rs) if rs is not None else c
+
+
+def nvfp4_gemm_grouped(x, w_nk, scale, global_scale, offsets, out_dtype=torch.bfloat16):
+    """Grouped (MoE) NVFP4 W4A16 GEMM in one launch: w_nk u8 [E, N, K/2] (K-contiguous codes),
+    E4M3 block scales [E, K/16, N], tensor scales f32 [E]; bf16 activations sorted by expert."""
+    _need_cuda(x, w_nk, scale, global_scale)
+    for t, n in ((x, "x"), (w_nk, "w_nk"), (scale, "scale"), (global_scale, "global_scale")):
+        _contig(t, n)
+    E, N, K2 = w_nk.shape
+    K = K2 * 2
+    off, rows = _offsets(offsets, E)
+    if x.shape != (rows, K) or x.dtype != torch.bfloat16:
+        raise ValueError(f"x must be bf16 [{rows}, {K}]")
+    c = torch.empty((rows, N), dtype=out_dtype, device=x.device)
+    rs = torch.empty(rows, dtype=torch.float32, device=x.device) if out_dtype == torch.float8_e4m3fn else None
+    need = L.lib().w4_nvfp4_gemm_grouped_workspace_bytes(off, E, N, K, _DT[out_dtype])
+    ws, wsb = _WS.get(x.device, need)
+    L.call("w4_nvfp4_gemm_grouped", _p(x), _p(w_nk), _p(scale), _p(global_scale), off, E, _p(c), _DT[out_dtype],
+           _p(rs), N, K, _p(ws), wsb, _stream(x.device))
+    return (c, rs) if rs is not None else c
+
+
 def register_torch_ops():
     """Expose the reference operator names as ``torch.ops.w4.*`` (CUDA only)."""
     global _registered
