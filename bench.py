@@ -9,8 +9,9 @@ copies of the M-sweep (3 * 4 * R GEMMs), replayed from CUDA graphs.  Metric: alg
 bytes (qweight + scales + qzeros + A + C, each once) per second.  The same line carries
 ``per_config``: configs 1, 3 and 4 (GPTQ M=16 4096^2 f16; NVFP4 5120^2 M=1..8192 with bf16
 or NVFP4 activations; GPTQ act_order prefill M=2048/8192), each timed on the device with its
-roofline fraction and the CPU oracle timed beside it on a bounded sample, and ``tp1``: the
-config 5 layer set at TP=1.
+roofline fraction and the CPU oracle timed beside it on a bounded sample; ``moe``: the grouped
+(MoE) GEMMs over 8 experts of hidden 2688 x expert 1856; and ``tp1``: the config 5 layer set at
+TP=1.
 
 Several GPUs (``--gpus N`` under torchrun): BASELINE config 5 -- one 27B-class layer's GPTQ
 projections (QKV and gate|up column-parallel, o and down row-parallel with the all-reduce of
@@ -51,8 +52,8 @@ METRIC = json.load(open(os.path.join(ROOT, "BASELINE.json")))["metric"]
 WORKLOAD = ("config2: GPTQ int4 W4A16 decode sweep, M in {1,4,8,16}, K=5120, N=17408, group 128, "
             "asymmetric packed zeros (v1 +1), bf16 activations and output, fp32 accumulate")
 # dram__bytes_read.sum + dram__bytes_write.sum of one config 2 decode launch at M=1 (ncu capture of the
-# decode kernel; equal to the algorithmic 46.35 MB within 0.1 %).
-TRAFFIC_PER_LAUNCH = 46_357_760
+# decode kernel: 46,365,952 read + 13,312 written; the algorithmic bytes are 46.35 MB).
+TRAFFIC_PER_LAUNCH = 46_379_264
 
 
 def alg_bytes(M: int, n_cols: int = N, k: int = K) -> int:
@@ -365,7 +366,52 @@ def per_config(dev, pk, cpu: bool) -> dict:
     res["config4"] = c4
     del lins
     torch.cuda.empty_cache()
+    res["moe"] = moe_record(dev, pk, l2)
     return res
+
+
+MOE_COUNTS = {"decode_top6": [1, 1, 0, 1, 1, 1, 0, 1], "batch32_top6": [24, 31, 0, 17, 40, 29, 33, 18]}
+
+
+def moe_record(dev, pk, l2) -> dict:
+    """Grouped (MoE) GEMMs, one launch over 8 experts of hidden 2688 x expert 1856 (the
+    reference's Lightning MoE shapes): GPTQ g128 and NVFP4, up (K=2688, N=1856) and down (K=1856,
+    N=2688, GPTQ g64), ragged token counts.  Bytes: the weights of the experts with tokens."""
+    import torch
+
+    from xe2x2_b200 import ops, synth
+    H, X, E = 2688, 1856, 8
+    out = {"shape": "8 experts, hidden 2688 x expert 1856", "counts": MOE_COUNTS}
+    for proj, K, N, gs in (("up", H, X, 128), ("down", X, H, 64)):
+        wb1 = K // 8 * N * 4 + K // gs * N * 2 + K // gs * N // 8 * 4
+        R = copies_for(wb1 * E, l2)
+        gq = []
+        for r in range(R):
+            ws = [synth.gptq_weights(K, N, gs, asym=True, seed=100 * r + e, device=dev)[:3] for e in range(E)]
+            gq.append(tuple(torch.stack([w[i] for w in ws]).contiguous() for i in range(3)))
+        fb1 = N * K // 2 + K // 16 * N
+        fq = []
+        for r in range(copies_for(fb1 * E, l2)):
+            ws = [synth.nvfp4_weights(K, N, seed=100 * r + e, device=dev) for e in range(E)]
+            fq.append((torch.stack([w[0].t() for w in ws]).contiguous(), torch.stack([w[1] for w in ws]).contiguous(),
+                       torch.cat([w[2] for w in ws]).contiguous()))
+        for name, cnt in MOE_COUNTS.items():
+            off = [0]
+            for c in cnt:
+                off.append(off[-1] + c)
+            active = sum(1 for c in cnt if c)
+            a = synth.activations(off[-1], K, torch.bfloat16, seed=1, device=dev)
+            us = time_graph(lambda r: ops.gptq_gemm_grouped(a, *gq[r % len(gq)], off, gs, 1), max(2 * len(gq), 20))
+            nb = active * wb1 + off[-1] * (K + N) * 2
+            out[f"gptq_{proj}_{name}"] = {"us": round(us, 2), "GB/s": round(nb / us / 1e3, 1),
+                                          "frac": round(nb / us / 1e3 / pk["hbm"], 4)}
+            us = time_graph(lambda r: ops.nvfp4_gemm_grouped(a, *fq[r % len(fq)], off), max(2 * len(fq), 20))
+            nb = active * fb1 + off[-1] * (K + N) * 2
+            out[f"nvfp4_{proj}_{name}"] = {"us": round(us, 2), "GB/s": round(nb / us / 1e3, 1),
+                                           "frac": round(nb / us / 1e3 / pk["hbm"], 4)}
+        del gq, fq
+        torch.cuda.empty_cache()
+    return out
 
 
 # ----------------------------------------------------------------------------- GPU side: config 2

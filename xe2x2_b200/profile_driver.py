@@ -2,6 +2,7 @@
 
     python -m xe2x2_b200.profile_driver --kernel gptq --M 16 --K 5120 --N 17408 --iters 4
     python -m xe2x2_b200.profile_driver --kernel nvfp4 --M 1,16 --K 5120 --N 5120 --time
+    python -m xe2x2_b200.profile_driver --kernel gptq_grouped --counts 1,1,0,1,1,1,0,1 --K 2688 --N 1856
 
 Without --time it runs ``--iters`` launches back to back (a small, fixed number of
 launches for an ncu capture).  With --time it reports the median per-launch
@@ -74,8 +75,10 @@ def nvfp4_bytes(M, K, N):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", choices=["gptq", "nvfp4", "producer"], default="gptq",
-                    help="producer: the fused RMSNorm -> NVFP4 activation kernel on [M, K]")
+    ap.add_argument("--kernel", choices=["gptq", "nvfp4", "producer", "gptq_grouped", "nvfp4_grouped"],
+                    default="gptq", help="producer: the fused RMSNorm -> NVFP4 activation kernel on [M, K]; "
+                    "*_grouped: one grouped (MoE) launch over len(--counts) experts")
+    ap.add_argument("--counts", default="1,1,0,1,1,1,0,1", help="tokens per expert of a grouped launch")
     ap.add_argument("--M", default="16", help="comma-separated token counts")
     ap.add_argument("--K", type=int, default=5120)
     ap.add_argument("--N", type=int, default=17408)
@@ -90,6 +93,8 @@ def main(argv=None):
     dt = torch.bfloat16 if args.dtype == "bf16" else torch.float16
     K, N = args.K, args.N
     wbytes = gptq_bytes(0, K, N, args.gs) if args.kernel == "gptq" else nvfp4_bytes(0, K, N)
+    if args.kernel.endswith("_grouped"):
+        return grouped(args, dev, dt)
     if args.kernel == "producer":
         wbytes = 1 << 40  # no weights: one copy
     l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 << 20) or (126 << 20)
@@ -131,6 +136,41 @@ def main(argv=None):
                         "GB/s": round(nb / us / 1e3, 1), "TFLOP/s": round(2 * M * N * K / us / 1e6, 2)})
     for r in results:
         print(json.dumps(r))
+    print("ok")
+
+
+def grouped(args, dev, dt):
+    """Grouped (MoE) launches: experts of K x N with --counts tokens each, stacked weights."""
+    K, N = args.K, args.N
+    cnt = [int(c) for c in args.counts.split(",")]
+    E = len(cnt)
+    off = [0]
+    for c in cnt:
+        off.append(off[-1] + c)
+    a = synth.activations(off[-1], K, dt if args.kernel == "gptq_grouped" else torch.bfloat16, seed=1, device=dev)
+    if args.kernel == "gptq_grouped":
+        ws = [synth.gptq_weights(K, N, args.gs, asym=True, seed=e, device=dev)[:3] for e in range(E)]
+        qw, qz, sc = (torch.stack([w[i] for w in ws]).contiguous() for i in range(3))
+
+        def run(i):
+            return ops.gptq_gemm_grouped(a, qw, qz, sc, off, args.gs, 1)
+        nb = sum(1 for c in cnt if c) * gptq_bytes(0, K, N, args.gs)
+    else:
+        ws = [synth.nvfp4_weights(K, N, seed=e, device=dev) for e in range(E)]
+        w_nk = torch.stack([w[0].t() for w in ws]).contiguous()
+        scale = torch.stack([w[1] for w in ws]).contiguous()
+        gsc = torch.cat([w[2] for w in ws]).contiguous()
+
+        def run(i):
+            return ops.nvfp4_gemm_grouped(a, w_nk, scale, gsc, off)
+        nb = sum(1 for c in cnt if c) * nvfp4_bytes(0, K, N)
+    for i in range(args.iters):
+        run(i)
+    torch.cuda.synchronize()
+    if args.time:
+        us = time_graph(run, max(args.iters, 20))
+        print(json.dumps({"kernel": args.kernel, "counts": cnt, "K": K, "N": N, "graph_us": round(us, 3),
+                          "GB/s": round(nb / us / 1e3, 1), "note": "weights of one stack (L2-warm if small)"}))
     print("ok")
 
 
