@@ -172,21 +172,18 @@ int w4_gptq_gemm(const void *a, int a_dtype, const int32_t *qweight, const int32
  * the f32 intermediate lives in a static device array inside the library
  * (4 MiB per device, held until exit) instead of a workspace: M*N must be
  * <= 1,048,576 or the call returns W4_ERR_UNSUPPORTED.  The first call on a
- * device looks the array's address up; make it before any stream capture.
- * All calls share the array: calls that overlap on the GPU race. */
+ * device looks the array's address up; make it before any stream capture.  The
+ * address is cached per device for the life of the process: after
+ * cudaDeviceReset on a device, do not call this on that device again.
+ * All calls share the array: calls that overlap on the GPU race.  With no
+ * workspace the GEMM never splits K, so results equal w4_gptq_gemm's only to
+ * fp32 summation order (that entry point splits K over CTAs when the output
+ * tiles are few, and from M = 17 runs the tensor-core GEMM). */
 int w4_gptq_gemm_fp8_noalloc(const void *a, int a_dtype, const int32_t *qweight,
                              const int32_t *qzeros, const uint16_t *scales, uint8_t *q_out,
                              float *row_scale, int M, int N, int K, int group_size,
                              int zero_offset, void *stream);
 
-/* The reference kernel's own contract, same arguments in the same order as
- * launch(q, ad, bd, asd, sd, cd, rows, cols, dk) of
- * kernels/esimd_dpas/dpas_s4_gptq_sc.cpp:146-149:
- *   C[r,c] = half( sum_g float(s32_g) * a_scale[r] * float(b_scale[g,c]) ),
- *   s32_g  = sum_{k in g} A_s4[r,k] * B_s4[k,c]   (group size 128, exact)
- * a_s4 u8 [rows, dk/2] (pack_a, low nibble = even k), b_s4 u8 [dk/2, cols]
- * (pack_b), a_scale f32 [rows], b_scale f16 [dk/128, cols], c f16 [rows, cols].
- * Bit-exact with the reference host oracle (dpas_s4_gptq_sc.cpp:273-288). */
 /* Grouped (MoE) GEMMs: one launch over num_experts experts (1..64).  Expert e's weights are
  * slice e of stacked tensors and its tokens are rows [offsets[e], offsets[e+1]) of a and c
  * (host array of num_experts + 1 ints, offsets[0] == 0, nondecreasing; tokens sorted by
@@ -211,6 +208,14 @@ int w4_nvfp4_gemm_grouped(const void *a, const uint8_t *w, const uint8_t *scale,
                           const int32_t *offsets, int num_experts, void *c, int c_dtype, float *row_scale,
                           int N, int K, void *workspace, size_t workspace_bytes, void *stream);
 
+/* The reference kernel's own contract, same arguments in the same order as
+ * launch(q, ad, bd, asd, sd, cd, rows, cols, dk) of
+ * kernels/esimd_dpas/dpas_s4_gptq_sc.cpp:146-149:
+ *   C[r,c] = half( sum_g float(s32_g) * a_scale[r] * float(b_scale[g,c]) ),
+ *   s32_g  = sum_{k in g} A_s4[r,k] * B_s4[k,c]   (group size 128, exact)
+ * a_s4 u8 [rows, dk/2] (pack_a, low nibble = even k), b_s4 u8 [dk/2, cols]
+ * (pack_b), a_scale f32 [rows], b_scale f16 [dk/128, cols], c f16 [rows, cols].
+ * Bit-exact with the reference host oracle (dpas_s4_gptq_sc.cpp:273-288). */
 int w4_gptq_gemm_s4a(const uint8_t *a_s4, const uint8_t *b_s4, const float *a_scale,
                      const uint16_t *b_scale, uint16_t *c, int rows, int cols, int dk,
                      void *stream);

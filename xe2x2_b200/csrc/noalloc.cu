@@ -12,8 +12,10 @@
 //
 // The array's name is only a host-side stand-in for device memory; its real
 // device address is looked up once per device with cudaGetSymbolAddress (on
-// the first call made with that device current) and cached.  Make that first
-// call before any stream capture.  Every call shares the one array, so calls
+// the first call made with that device current) and cached for the life of the
+// process; after cudaDeviceReset the cached address is stale, so do not call
+// this again on a device that was reset.  Make the first call before any stream
+// capture.  Every call shares the one array, so calls
 // that overlap on the GPU (different streams, or threads) race on it: order
 // them.  The GEMM overwrites all M*N scratch elements before the cast reads
 // them, so nothing has to be cleared between calls.
