@@ -604,7 +604,8 @@ def run_decode(args) -> None:
                     "sweeps": e2e_steps_done, "ms_per_sweep": round(ms_e2e / e2e_steps_done, 5)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm"], "unit": "GB/s",
                          "frac": round(achieved / pk["hbm"], 4), "traffic": TRAFFIC_PER_LAUNCH,
-                         "kernel": "w4::dec::gptq_decode_kernel", "peak_source": pk["source"] + " hbm_gbs (copy)",
+                         "kernel": "w4::dec::gptq_decode_kernel (M = 1, 4, 8), w4::gptq_gemv_kernel (M = 16)",
+                         "peak_source": pk["source"] + " hbm_gbs (copy)",
                          "per_m": per_m},
             "gpu_launches": gemms_per_step * args.steps,
             "decode_fallbacks": fallbacks,

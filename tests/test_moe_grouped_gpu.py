@@ -48,7 +48,8 @@ def test_gptq_grouped_matches_oracle(cuda, counts, proj, K, N, gs):
 
 def test_gptq_grouped_equals_per_expert_calls_and_fp8(cuda):
     """The grouped launch gives each expert what a plain call on its slice gives (to fp32
-    summation order), and the fp8 output is the row-scaled cast of the f32 product."""
+    summation order: a plain call may run another decode kernel, with another order of the
+    exact products' fp32 sums), and the fp8 output is the row-scaled cast of the f32 product."""
     cnt = COUNTS["decode"]
     E, off = len(cnt), _offsets(cnt)
     K, N, gs = HIDDEN, EXPERT, 128
@@ -60,7 +61,7 @@ def test_gptq_grouped_equals_per_expert_calls_and_fp8(cuda):
             continue
         one = ops.gptq_gemm(a[off[e]:off[e + 1]].contiguous(), qw[e], qz[e], sc[e], gs, 1, out_dtype=torch.float32)
         rel = float((one - y[off[e]:off[e + 1]]).norm() / one.norm())
-        assert rel < 1e-5, (e, rel)
+        assert rel < 5e-5, (e, rel)
     q, s = ops.gptq_gemm_grouped(a, qw, qz, sc, off, gs, 1, out_dtype=torch.float8_e4m3fn)
     q_ref, s_ref = O.rowscale_fp8(np_(y))
     assert np.array_equal(np_(q.view(torch.uint8)), q_ref)

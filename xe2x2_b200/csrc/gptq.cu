@@ -8,6 +8,7 @@
 // except the optional act_order row permutation.
 #include <cooperative_groups.h>
 
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -371,16 +372,37 @@ static int launch_gemv(const void *a, const int32_t *qweight, const int32_t *qze
     return launch_gemv_nt<T, 2>(ap, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
 }
 
+// Where the register-batched kernel is the faster decode design (measured on B200 against the
+// shared-ring TMA kernel over the BASELINE shapes and their tensor-parallel shards): with two
+// token tiles (9..16 tokens) its 16 warps per CTA, each with its own batch of independent 16-byte
+// loads, hide the doubled MMA work better, except on mid-sized layers that are neither wide nor
+// small (5120 x 5120 ties, 8704 x 5120 loses); with one tile it wins only on small layers from
+// 5 tokens.  W4_GPTQ_DECODE (a tuning override of the TMA kernel) turns this choice off.
+bool prefer_register_gemv(int M, int N, int K) {
+    if (std::getenv("W4_GPTQ_DECODE")) return false;
+    const long long nk = (long long)N * K;
+    if (M > 8) return nk < 24LL * 1024 * 1024 || N >= 12288;
+    return M >= 5 && nk < 12LL * 1024 * 1024;
+}
+
 int gptq_gemv(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
               const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs,
               int zero_offset, void *sync, void *ws, size_t ws_bytes, cudaStream_t st) {
     // Prefill-sized token counts: the tcgen05 GEMM (gptq_prefill.cu).  Decode: the
-    // shared-ring TMA kernel (gptq_decode.cu); the register-batched kernel below runs only
-    // for shapes it does not take, and every such call is counted (w4_decode_fallback_count).
+    // register-batched kernel above where it is the faster design (prefer_register_gemv), else
+    // the shared-ring TMA kernel (gptq_decode.cu); the register-batched kernel also runs for
+    // shapes the TMA kernel does not take, and every such call is counted
+    // (w4_decode_fallback_count).
     if (M >= kPrefillMinM) {
         const int rp = gptq_prefill(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ws,
                                     ws_bytes, st);
         if (rp >= 0) return rp;
+    }
+    if (M < kPrefillMinM && prefer_register_gemv(M, N, K) && aligned(a, 16) && aligned(qweight, 16) &&
+        aligned(scales, 8)) {
+        if (a_dtype == W4_BF16)
+            return launch_gemv<__nv_bfloat16>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
+        return launch_gemv<__half>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, st);
     }
     const int rc = gptq_gemv_decode(a, a_dtype, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, sync,
                                     ws, ws_bytes, nullptr, st);

@@ -458,7 +458,11 @@ struct DecChoice {
 };
 
 // Optional tile override for tuning sweeps: W4_GPTQ_DECODE="cw,ks[,S]" (cw in {1,2,4,8}, ks 1..8,
-// S ring stages 2..8).
+// S ring stages 2..8), or "reg" to decline every call (the register-streamed kernel runs).
+bool env_decline() {
+    const char *e = std::getenv("W4_GPTQ_DECODE");
+    return e && e[0] == 'r';
+}
 bool env_choice(DecChoice &c) {
     const char *e = std::getenv("W4_GPTQ_DECODE");
     if (!e) return false;
@@ -652,6 +656,7 @@ size_t gptq_decode_grouped_split_bytes(const int *off, int n, int N, int K, int 
 }
 
 static int run_decode(DecCall &q, const int *off, int n, void *sync, void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (env_decline()) return -1;
     const int mr = max_rows(off, n);
     if (mr < 0 || !decode_shape_ok(q.N, q.K, q.gs)) return -1;
     if (!aligned(q.qweight, 16) || !aligned(q.scales, 16) || (q.qzeros && !aligned(q.qzeros, 16)) || !aligned(q.a, 16))

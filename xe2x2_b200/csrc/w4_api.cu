@@ -206,7 +206,7 @@ int w4_gptq_gemm(const void *a, int a_dtype, const int32_t *qweight, const int32
         ws += align256((size_t)M * N * 4);
     }
     const size_t have = workspace_bytes - (size_t)(ws - sync);
-    if (c_dtype == W4_E4M3 && M <= 16 && N % 8 == 0 && aligned(c, 8)) {
+    if (c_dtype == W4_E4M3 && M <= 16 && N % 8 == 0 && aligned(c, 8) && !w4::prefer_register_gemv(M, N, K)) {
         // decode: the GEMM folds the row maxima of its f32 product into the sync area, so the
         // cast reads the product once
         unsigned int *sw = reinterpret_cast<unsigned int *>(sync);

@@ -40,6 +40,8 @@ int gptq_gemv_decode(const void *a, int a_dtype, const int32_t *qweight, const i
                      const uint16_t *scales, void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset,
                      void *sync, void *ws, size_t ws_bytes, unsigned int *rowmax, cudaStream_t st);
 size_t gptq_decode_split_bytes(int M, int N, int K, int gs);
+// gptq.cu: decode shapes that run the register-batched kernel by design (faster there)
+bool prefer_register_gemv(int M, int N, int K);
 // Grouped (MoE) form: expert e's weights are slice e of stacked [E][...] tensors and its token
 // rows are [off[e], off[e+1]) of a and c (host offsets, off[0] = 0, at most 64 experts).
 int gptq_gemv_decode_grouped(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
