@@ -455,23 +455,24 @@ int fp4_ctas_per_sm(int cw, int NT, int max_st, int rows) {
     return r < 1 ? 1 : (r > 32 ? 32 : r);
 }
 
-// Tile width and K split: the grid should be about one wave of CTAs with equal work.  Take the
-// widest column tile whose tiles, split over at most 8 CTAs along K (at least two stages each),
-// reach 1.8 CTAs per SM, then the smallest K split that reaches it.  mblocks: token blocks of the
+// Tile width and K split.  The 128-column tile (four consumer warps) is taken whenever N allows
+// it (measured faster than 256, 64 and 32 columns at every decode shape, small shards included),
+// then the smallest K split, at most 8 and at most one CTA per 256-k stage, that reaches 1.3 CTAs
+// per SM.  Measured on 5120 x 5120, 5120 x 17408, 640 x 5120, 2176 x 5120 and 1408 x 4096 at one
+// and eight rows, the best split always gave 1.35 to 1.9 CTAs per SM; beyond one wave (three
+// 160-thread CTAs of this kernel per SM) the call slows by a third.  mblocks: token blocks of the
 // call (over all experts).
 Fp4Choice fp4_choose(int mblocks, int N, int K) {
     Fp4Choice c{1, 1, 0};
     if (env_fp4_choice(c) && N % (32 * c.cw) == 0) return c;
     const int nsm = num_sms();
     const int nst = (K + fp4d::KS - 1) / fp4d::KS;
-    const int ks_cap = nst / 2 < 1 ? 1 : (nst / 2 > 8 ? 8 : nst / 2);
-    const long target = (long)(1.8 * nsm);
-    const int cws[4] = {8, 4, 2, 1};
-    for (int i = 0; i < 4; ++i) {
-        const int cw = cws[i];
+    const int ks_cap = nst > 8 ? 8 : nst;
+    const long target = (long)(1.3 * nsm);
+    const int cws[4] = {4, 8, 2, 1};
+    for (int cw : cws) {
         if (N % (32 * cw)) continue;
         const long tiles = (long)(N / (32 * cw)) * mblocks;
-        if (i < 3 && tiles * ks_cap < target) continue;  // too few tiles: a narrower one
         int ks = 1;
         while (ks < ks_cap && tiles * ks < target) ++ks;
         return {cw, ks, 0};
@@ -595,6 +596,8 @@ size_t nvfp4_decode_grouped_split_bytes(const int *off, int n, int N, int K) {
 
 static int run_fp4_decode(Fp4Call &q, const int *off, int n, int scale_dtype, void *sync, void *ws, size_t ws_bytes,
                           cudaStream_t st) {
+    const char *env = std::getenv("W4_NVFP4_DECODE");
+    if (env && env[0] == 'r') return -1;  // tuning override "reg": the register-streamed kernel runs
     const int mr = fp4_max_rows(off, n);
     if (mr < 0 || !fp4_decode_shape_ok(q.N, q.K)) return -1;
     // E4M3 block scales only: a bf16 scale times an e2m1 code need not be an f16
