@@ -499,23 +499,27 @@ int ctas_per_sm(int cw, int NT, int sg, int max_st, int rows) {
 }
 
 // Tile width and K split.  The grid should be about one wave of CTAs with equal work, so HBM
-// bandwidth is shared evenly: take the widest column tile whose tiles, split over at most 8 CTAs
-// along K, reach the target CTA count (1.8 CTAs per SM with one token tile, 0.9 with two, whose
-// CTAs hold twice the registers), then the smallest K split that reaches it.  mblocks: token
-// blocks of the call (over all experts).
+// bandwidth is shared evenly: the target is 1.8 CTAs per SM with one token tile, 0.9 with two,
+// whose CTAs hold twice the registers.  The K split is at most 8 and at most one CTA per 128-k
+// stage.  A 256-column tile is taken when its tiles, split, reach the target; else a 128-column
+// tile when they reach a quarter of it; else 64, else 32 columns (narrow shards such as 896
+// columns run fastest on 64-column tiles).  Then the smallest K split that reaches the target.
+// Measured on 17408, 5120, 4352 and 896 columns with K from 640 to 8704.  mblocks: token blocks
+// of the call (over all experts).
 DecChoice choose(int mblocks, int N, int K, int NT) {
     DecChoice c{1, 1, 0};
     if (env_choice(c) && N % (32 * c.cw) == 0) return c;
     const int nsm = num_sms();
     const int nst = (K + dec::kStageK - 1) / dec::kStageK;
-    const int ks_cap = nst / 2 < 1 ? 1 : (nst / 2 > 8 ? 8 : nst / 2);
+    const int ks_cap = nst > 8 ? 8 : nst;
     const long target = NT == 1 ? (long)(1.8 * nsm) : (long)(0.9 * nsm);
     const int cws[4] = {8, 4, 2, 1};
+    const long need[4] = {target, target / 4, 0, 0};
     for (int i = 0; i < 4; ++i) {
         const int cw = cws[i];
         if (N % (32 * cw)) continue;
         const long tiles = (long)(N / (32 * cw)) * mblocks;
-        if (i < 3 && tiles * ks_cap < target) continue;  // too few tiles: a narrower one
+        if (tiles * ks_cap < need[i]) continue;  // too few tiles: a narrower one
         int ks = 1;
         while (ks < ks_cap && tiles * ks < target) ++ks;
         return {cw, ks, 0};
