@@ -21,7 +21,8 @@ instead (weak scaling, no collective).
 
 Output: one JSON line on rank 0 with ``value`` (device time, inputs resident in HBM),
 ``e2e`` (the public API with every step's activations copied in from pinned host memory and
-its outputs copied out), ``roofline`` for the dominant kernel, ``cpu_baseline`` (the C oracle
+its outputs copied out), ``roofline`` for the dominant kernel (with ``read_ceiling``: the read
+bandwidth a plain one-launch read of the same bytes attains, timed the same way), ``cpu_baseline`` (the C oracle
 on the host cores) and ``clocks`` (nvidia-smi during the timed region).
 
 ``--impl reference`` times the reference's CPU path instead (the plain-C restatement of its
@@ -507,6 +508,19 @@ def run_decode(args) -> None:
     tot_us = sum(per_m[str(M)]["us"] for M in MS)
     achieved = tot_b / tot_us / 1e3
 
+    # ---------------- the read bandwidth one launch of this size attains (w4_read_probe), timed
+    # the same way over as many buffers of one M = 1 launch's bytes: the practical ceiling of a
+    # GEMM launch that reads its operands once (launch ramp and tail included)
+    rb = alg_bytes(1) // 16 * 16
+    probe_bufs = [torch.zeros(rb, dtype=torch.uint8, device=dev) for _ in range(R)]
+    sink = torch.zeros(1, dtype=torch.int32, device=dev)
+    probe_us = time_graph(lambda r: L.call("w4_read_probe", ops._p(probe_bufs[r % R]), rb, ops._p(sink),
+                                           ops._stream(dev)), max(30, 2 * R))
+    del probe_bufs
+    read_ceiling = {"bytes": rb, "us": round(probe_us, 3), "GB/s": round(rb / probe_us / 1e3, 1),
+                    "frac_of_peak": round(rb / probe_us / 1e3 / pk["hbm"], 4),
+                    "m1_frac_of_ceiling": round(probe_us / per_m["1"]["us"], 4)}
+
     # ---------------- end to end through the public API (pinned host in, host out)
     # Each step's inputs (the four activation blocks) travel from pinned host memory in one copy
     # and its four outputs come back in one, as a serving loop runs them: copies on their own
@@ -606,7 +620,7 @@ def run_decode(args) -> None:
                          "frac": round(achieved / pk["hbm"], 4), "traffic": TRAFFIC_PER_LAUNCH,
                          "kernel": "w4::dec::gptq_decode_kernel (M = 1, 4, 8), w4::gptq_gemv_kernel (M = 16)",
                          "peak_source": pk["source"] + " hbm_gbs (copy)",
-                         "per_m": per_m},
+                         "per_m": per_m, "read_ceiling": read_ceiling},
             "gpu_launches": gemms_per_step * args.steps,
             "decode_fallbacks": fallbacks,
             "clocks": clk,

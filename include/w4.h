@@ -118,6 +118,16 @@ int w4_get_launch_overlap(void);
  * count stays 0 on the shapes they measure.  No counterpart in the reference. */
 unsigned long long w4_decode_fallback_count(void);
 
+/* Measurement helper; no counterpart in the reference.  One launch that reads
+ * `bytes` (a positive multiple of 16) of device memory at `buf` (16-byte
+ * aligned) with 16-byte loads at full occupancy and writes `sink` (4 bytes of
+ * device memory) only if the XOR of every word equals a fixed sentinel.  Timed
+ * back to back over buffers larger than L2, it gives the read bandwidth that a
+ * single kernel of that size attains on this GPU, launch ramp and tail
+ * included: the practical ceiling of a decode GEMM that reads its operands
+ * once.  Argument errors are synchronous (W4_ERR_INVALID). */
+int w4_read_probe(const void *buf, size_t bytes, unsigned int *sink, void *stream);
+
 /* ===================================================================== */
 /* GPTQ int4                                                              */
 /* ===================================================================== */

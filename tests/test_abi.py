@@ -170,3 +170,12 @@ def test_grouped_gemm_checks_offsets_without_gpu():
     assert lib.w4_gptq_gemm_grouped_workspace_bytes(ok, 8, 1856, 2688, 128, L.W4_BF16) >= L.W4_WORKSPACE_SYNC_BYTES
     assert lib.w4_nvfp4_gemm_grouped_workspace_bytes(ok, 8, 2688, 1856, L.W4_E4M3) >= \
         L.W4_WORKSPACE_SYNC_BYTES + 35 * 2688 * 4
+
+
+def test_read_probe_rejects_bad_arguments_without_gpu():
+    lib = L.lib()
+    f = _fake()
+    assert lib.w4_read_probe(None, 1024, f, None) == L.W4_ERR_INVALID
+    assert lib.w4_read_probe(f, 1000, f, None) == L.W4_ERR_INVALID  # not a multiple of 16
+    assert lib.w4_read_probe(_fake(0x10008), 1024, f, None) == L.W4_ERR_INVALID  # misaligned
+    assert b"aligned" in lib.w4_last_error()

@@ -27,6 +27,9 @@ def _oracle(a, qw, qz, sc, K, N, gs, zo=1, g_idx=None):
     (200, 2048, 512, 128, False, torch.float16, torch.float16),   # symmetric, f16 path
     (300, 1024, 768, 128, True, torch.bfloat16, torch.float32),   # three M tiles, mixed tile widths
     (64, 4096, 256, 256, True, torch.float16, torch.float32),     # group 256
+    (64, 2688, 1856, 128, True, torch.bfloat16, torch.float32),   # N % 128 != 0: ragged last tile
+    (40, 1856, 2688, 64, True, torch.bfloat16, torch.bfloat16),   # 2688 = 10.5 x 256
+    (24, 1024, 96, 128, True, torch.bfloat16, torch.float32),     # N below one tile
 ])
 def test_prefill_shapes(cuda, M, K, N, gs, asym, dtype, out):
     qw, qz, sc, _ = synth.gptq_weights(K, N, gs, asym=asym, seed=M + N, device=cuda)

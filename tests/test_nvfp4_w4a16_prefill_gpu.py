@@ -27,6 +27,8 @@ def _oracle(x, w, scale, gscale):
     (128, 1024, 384),    # 128-wide tiles (N % 256 != 0)
     (300, 2048, 512),    # three 128-row tiles: two A tiles per CTA
     (32, 8192, 256),     # few output tiles: K split across CTAs
+    (40, 2688, 1856),    # N % 128 != 0: ragged last tile
+    (24, 1920, 2688),    # 2688 = 10.5 x 256
 ])
 def test_w4a16_prefill_matches_oracle(cuda, M, K, N):
     w, scale, gscale = synth.nvfp4_weights(K, N, seed=M + K, device=cuda)

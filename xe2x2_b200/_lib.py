@@ -44,6 +44,7 @@ _SIGS = {
     "w4_set_launch_overlap": (_I, [_I]),
     "w4_get_launch_overlap": (_I, []),
     "w4_decode_fallback_count": (ctypes.c_ulonglong, []),
+    "w4_read_probe": (_I, [_P, _Z, _P, _P]),
     "w4_gptq_dequant": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "w4_gptq_repack_act_order": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
     "w4_gptq_workspace_bytes": (_Z, [_I, _I, _I, _I, _I, _I]),

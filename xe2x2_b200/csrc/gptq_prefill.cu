@@ -6,9 +6,15 @@
 // of kernels/esimd_dpas/dpas_s4_gptq_db48.cpp:148-246 (same formula, s32
 // groups there, W4A16 here per the checkpoint layout).
 //
-// One CTA computes a 128 x BN tile of C (BN = 256, or 128 when N is not a
-// multiple of 256) with the fp32 accumulator in tensor memory (TMEM, BN
-// columns x 128 lanes).  Eighteen warps, specialised:
+// One CTA computes a 128 x BN tile of C (BN = 256 or 128) with the fp32
+// accumulator in tensor memory (TMEM, BN columns x 128 lanes).  N need only be
+// a multiple of 32: the last column tile reads past N through the tensor maps'
+// zero fill (zero codes, scales and zeros dequantise to 0) and stores only the
+// 32-column chunks below N.  Grouped (MoE) GEMMs run the same kernel: the
+// weights are E stacked matrices read through 3-D tensor maps (expert = z),
+// each CTA's 128-row tile belongs to one expert (ExpertRows), and it stores
+// only that expert's rows; a plain GEMM is the one-expert case.  Eighteen
+// warps, specialised:
 //   warp 0     TMA producer: per 64-deep k-block, the A tile (128 x 64 bf16,
 //              128-byte swizzled) and the raw weight pieces (qweight 8 x BN
 //              int32, the group's scale row and packed zero row) into ring
@@ -34,6 +40,8 @@
 // Every mbarrier wait is bounded (tma_util.cuh): on expiry the CTA stops its
 // loops, the MMA thread still signals completion, TMEM is freed, and
 // w4_check_device_status() reports W4_ERR_TIMEOUT.  No copy uses multicast.
+#include <cstdio>
+#include <cstdlib>
 #include <type_traits>
 
 #include <cuda_fp8.h>
@@ -182,7 +190,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap qw_map,
                     const __grid_constant__ CUtensorMap sc_map, const __grid_constant__ CUtensorMap zr_map,
                     int has_z, void *__restrict__ C, int c_dtype, int M, int N, int K, int gs, int zero_offset,
-                    int kb_per_split, float *__restrict__ partial, const float *__restrict__ w_global) {
+                    int kb_per_split, float *__restrict__ partial, const float *__restrict__ w_global,
+                    const __grid_constant__ ExpertRows grp) {
     static_assert(!FP4 || std::is_same<T, __nv_bfloat16>::value, "NVFP4 weights meet bf16 activations");
     using Lay = Layout<BN, MT, FP4>;
     constexpr int S = Lay::S;
@@ -196,7 +205,10 @@ gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + Lay::MISC_OFF);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + Lay::MISC_OFF + 4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * BM * MT, n0 = blockIdx.y * BN;
+    // this CTA's rows: tile blockIdx.x - blk0[ex] of expert ex, rows [m0, m_end) stored
+    const int ex = expert_of_block(grp, blockIdx.x);
+    const int m0 = grp.row0[ex] + ((int)blockIdx.x - grp.blk0[ex]) * BM * MT, m_end = grp.row0[ex + 1];
+    const int n0 = blockIdx.y * BN;
     // split-K: this CTA reduces k-blocks [kb0, kb0 + nk) and, when split, writes an
     // fp32 partial tile that a second kernel sums
     const int kb0 = blockIdx.z * kb_per_split;
@@ -224,6 +236,9 @@ gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
+            // A: the whole BM * MT-row tile (rows of the next expert or past M included: they meet
+            // only accumulator rows that are never stored).  Loading only the 32-row boxes that
+            // hold this tile's rows measured 12 % slower on the MoE shapes.
             const uint32_t tx = Lay::A_BYTES + Lay::QW_BYTES + Lay::SC_BYTES + (has_z ? BN / 2 : 0);
             for (int i = 0; i < nk; ++i) {
                 const int s = i % S;
@@ -233,12 +248,12 @@ gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
                 mbar_arrive_expect_tx(&full[s], tx);
                 tma_load_2d(sm + Lay::A_OFF + s * Lay::A_BYTES, &a_map, kb * BK, m0, &full[s]);
                 if constexpr (FP4) {
-                    tma_load_2d(sm + Lay::QW_OFF + s * Lay::QW_BYTES, &qw_map, kb * (BK / 2), n0, &full[s]);
-                    tma_load_2d(sm + Lay::SC_OFF + s * Lay::SC_BYTES, &sc_map, n0, kb * (BK / 16), &full[s]);
+                    tma_load_3d(sm + Lay::QW_OFF + s * Lay::QW_BYTES, &qw_map, kb * (BK / 2), n0, ex, &full[s]);
+                    tma_load_3d(sm + Lay::SC_OFF + s * Lay::SC_BYTES, &sc_map, n0, kb * (BK / 16), ex, &full[s]);
                 } else {
-                    tma_load_2d(sm + Lay::QW_OFF + s * Lay::QW_BYTES, &qw_map, n0, kb * (BK / 8), &full[s]);
-                    tma_load_2d(sm + Lay::SC_OFF + s * Lay::SC_BYTES, &sc_map, n0, g, &full[s]);
-                    if (has_z) tma_load_2d(sm + Lay::ZR_OFF + s * Lay::ZR_SLOT, &zr_map, n0 / 8, g, &full[s]);
+                    tma_load_3d(sm + Lay::QW_OFF + s * Lay::QW_BYTES, &qw_map, n0, kb * (BK / 8), ex, &full[s]);
+                    tma_load_3d(sm + Lay::SC_OFF + s * Lay::SC_BYTES, &sc_map, n0, g, ex, &full[s]);
+                    if (has_z) tma_load_3d(sm + Lay::ZR_OFF + s * Lay::ZR_SLOT, &zr_map, n0 / 8, g, ex, &full[s]);
                 }
             }
         }
@@ -345,7 +360,7 @@ gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
             (void)ok;
             tc_fence_after();
             const int q = warp & 3;
-            const float gsc = w_global ? *w_global : 1.0f;  // NVFP4 tensor scale
+            const float gsc = w_global ? w_global[ex] : 1.0f;  // NVFP4 tensor scale of this expert
 #pragma unroll 1
             for (int cc = 0; cc < MT * BN; cc += 32) {
                 const int mh = cc / BN, c0 = cc % BN;
@@ -356,7 +371,7 @@ gptq_prefill_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
 #pragma unroll
                     for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * gsc);
                 }
-                if (row < M) {
+                if (row < m_end && n0 + c0 < N) {  // N % 32 == 0: a chunk is wholly inside or outside
                     const size_t base = (size_t)row * N + n0 + c0;
                     if (partial) {
                         float4 *dst = reinterpret_cast<float4 *>(partial + (size_t)blockIdx.z * M * N + base);
@@ -425,92 +440,91 @@ __global__ void splitk_reduce_kernel(const float *__restrict__ partial, int spli
     }
 }
 
+// Shared memory of one prefill kernel instantiation (the template argument), opted in once per
+// device.
+template <auto kern>
+static int prepare(size_t smem) {
+    static std::mutex mu;
+    static bool set_dev[128] = {};
+    int dev = 0;
+    W4_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 128 && !set_dev[dev]) {
+        W4_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        set_dev[dev] = true;
+    }
+    return W4_OK;
+}
+
+// GPTQ weights: E stacked [K/8, N] qweight, [K/gs, N] scales, [K/gs, N/8] qzeros (or none).
 template <typename T, int BN, int MT>
 static int launch(const void *a, const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales, void *c,
-                  int c_dtype, int M, int N, int K, int gs, int zero_offset, int ksplit, float *partial,
-                  cudaStream_t st) {
+                  int c_dtype, const ExpertRows &g, int E, int M, int N, int K, int gs, int zero_offset, int ksplit,
+                  float *partial, cudaStream_t st) {
     using Lay = Layout<BN, MT>;
     const CUtensorMapDataType adt =
         std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const uint64_t ng = (uint64_t)(K / gs);
     CUtensorMap a_map, qw_map, sc_map, zr_map;
     if (!make_map_2d(&a_map, adt, a, K, M, (uint64_t)K * 2, BK, BM * MT, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map_2d(&qw_map, CU_TENSOR_MAP_DATA_TYPE_INT32, qweight, N, K / 8, (uint64_t)N * 4, BN, BK / 8,
-                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_map_2d(&sc_map, CU_TENSOR_MAP_DATA_TYPE_UINT16, scales, N, K / gs, (uint64_t)N * 2, BN, 1,
+        !make_map_3d(&qw_map, CU_TENSOR_MAP_DATA_TYPE_INT32, qweight, N, K / 8, E, (uint64_t)N * 4,
+                     (uint64_t)(K / 8) * N * 4, BN, BK / 8, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map_3d(&sc_map, CU_TENSOR_MAP_DATA_TYPE_UINT16, scales, N, ng, E, (uint64_t)N * 2, ng * N * 2, BN, 1,
                      CU_TENSOR_MAP_SWIZZLE_NONE))
         return -1;
     const int has_z = qzeros != nullptr;
     if (has_z) {
-        if (!make_map_2d(&zr_map, CU_TENSOR_MAP_DATA_TYPE_INT32, qzeros, N / 8, K / gs, (uint64_t)N / 2, BN / 8, 1,
-                         CU_TENSOR_MAP_SWIZZLE_NONE))
+        if (!make_map_3d(&zr_map, CU_TENSOR_MAP_DATA_TYPE_INT32, qzeros, N / 8, ng, E, (uint64_t)N / 2, ng * N / 2,
+                         BN / 8, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
             return -1;
     } else {
         zr_map = sc_map;  // unused
     }
-    auto kern = gptq_prefill_kernel<T, BN, MT, false>;
+    constexpr auto kern = gptq_prefill_kernel<T, BN, MT, false>;
     const size_t smem = Lay::TOTAL + 1024;
-    {
-        static std::mutex mu;
-        static bool set_dev[128] = {};
-        int dev = 0;
-        W4_CUDA_TRY(cudaGetDevice(&dev));
-        std::lock_guard<std::mutex> lk(mu);
-        if (dev < 128 && !set_dev[dev]) {
-            W4_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            set_dev[dev] = true;
-        }
-    }
+    if (const int rc = prepare<kern>(smem)) return rc;
     const int nk = K / BK;
     const int kb_per_split = (nk + ksplit - 1) / ksplit;
     ksplit = (nk + kb_per_split - 1) / kb_per_split;  // every split gets at least one k-block
-    dim3 grid((M + BM * MT - 1) / (BM * MT), N / BN, ksplit), block(kThreads);
+    dim3 grid((unsigned)g.blk0[g.n], (unsigned)((N + BN - 1) / BN), (unsigned)ksplit), block(kThreads);
     kern<<<grid, block, smem, st>>>(a_map, qw_map, sc_map, zr_map, has_z, c, c_dtype, M, N, K, gs, zero_offset,
-                                    kb_per_split, ksplit > 1 ? partial : nullptr, nullptr);
+                                    kb_per_split, ksplit > 1 ? partial : nullptr, nullptr, g);
     W4_LAUNCH_CHECK();
     if (ksplit > 1) {
-        const long mn = (long)M * N;  // N % 128 == 0: whole float4 groups
+        const long mn = (long)M * N;  // N % 32 == 0: whole float4 groups
         splitk_reduce_kernel<<<(unsigned)((mn / 4 + 255) / 256), 256, 0, st>>>(partial, ksplit, mn, c, c_dtype);
         W4_LAUNCH_CHECK();
     }
     return W4_OK;
 }
 
-// NVFP4 weights (codes [N, K/2] K-contiguous, E4M3 block scales [K/16, N], fp32
-// tensor scale) with bf16 activations.
+// NVFP4 weights: E stacked codes [N, K/2] (K-contiguous), E4M3 block scales [K/16, N] and one
+// fp32 tensor scale per expert, with bf16 activations.
 template <int BN, int MT>
 static int launch_fp4(const uint16_t *a, const uint8_t *w_nk, const uint8_t *scale, const float *w_global, void *c,
-                      int c_dtype, int M, int N, int K, int ksplit, float *partial, cudaStream_t st) {
+                      int c_dtype, const ExpertRows &g, int E, int M, int N, int K, int ksplit, float *partial,
+                      cudaStream_t st) {
     using Lay = Layout<BN, MT, true>;
     CUtensorMap a_map, qw_map, sc_map;
     if (!make_map_2d(&a_map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a, K, M, (uint64_t)K * 2, BK, BM * MT,
                      CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map_2d(&qw_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_nk, (uint64_t)K / 2, N, (uint64_t)K / 2, BK / 2, BN,
-                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_map_2d(&sc_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, scale, N, K / 16, (uint64_t)N, BN, BK / 16,
-                     CU_TENSOR_MAP_SWIZZLE_NONE))
+        !make_map_3d(&qw_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_nk, (uint64_t)K / 2, N, E, (uint64_t)K / 2,
+                     (uint64_t)N * (K / 2), BK / 2, BN, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map_3d(&sc_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, scale, N, K / 16, E, (uint64_t)N, (uint64_t)(K / 16) * N,
+                     BN, BK / 16, CU_TENSOR_MAP_SWIZZLE_NONE))
         return -1;
-    auto kern = gptq_prefill_kernel<__nv_bfloat16, BN, MT, true>;
+    constexpr auto kern = gptq_prefill_kernel<__nv_bfloat16, BN, MT, true>;
     const size_t smem = Lay::TOTAL + 1024;
-    {
-        static std::mutex mu;
-        static bool set_dev[128] = {};
-        int dev = 0;
-        W4_CUDA_TRY(cudaGetDevice(&dev));
-        std::lock_guard<std::mutex> lk(mu);
-        if (dev < 128 && !set_dev[dev]) {
-            W4_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            set_dev[dev] = true;
-        }
-    }
+    if (const int rc = prepare<kern>(smem)) return rc;
     const int nk = K / BK;
     const int kb_per_split = (nk + ksplit - 1) / ksplit;
     ksplit = (nk + kb_per_split - 1) / kb_per_split;
-    dim3 grid((M + BM * MT - 1) / (BM * MT), N / BN, ksplit), block(kThreads);
+    dim3 grid((unsigned)g.blk0[g.n], (unsigned)((N + BN - 1) / BN), (unsigned)ksplit), block(kThreads);
     kern<<<grid, block, smem, st>>>(a_map, qw_map, sc_map, sc_map, 0, c, c_dtype, M, N, K, BK, 0, kb_per_split,
-                                    ksplit > 1 ? partial : nullptr, w_global);
+                                    ksplit > 1 ? partial : nullptr, w_global, g);
     W4_LAUNCH_CHECK();
     if (ksplit > 1) {
-        const long mn = (long)M * N;  // N % 128 == 0: whole float4 groups
+        const long mn = (long)M * N;  // N % 32 == 0: whole float4 groups
         splitk_reduce_kernel<<<(unsigned)((mn / 4 + 255) / 256), 256, 0, st>>>(partial, ksplit, mn, c, c_dtype);
         W4_LAUNCH_CHECK();
     }
@@ -521,40 +535,126 @@ static int launch_fp4(const uint16_t *a, const uint8_t *w_nk, const uint8_t *sca
 
 namespace pf {
 static bool handled(int N, int K, int gs, int c_dtype) {
-    return K % BK == 0 && gs % BK == 0 && N % 128 == 0 && c_dtype != W4_E4M3;
+    return N > 0 && K > 0 && K % BK == 0 && gs % BK == 0 && N % 32 == 0 && c_dtype != W4_E4M3;
 }
-static int m_tiles_per_cta(int M) { return M > BM ? 2 : 1; }  // two A tiles share each dequantised B tile
-static long tiles_of(int M, int N, bool wide) {
-    const int bm = BM * m_tiles_per_cta(M);
-    return (long)((M + bm - 1) / bm) * (N / (wide ? 256 : 128));
+
+// Tiling of one call: A tiles per CTA (two 128-row tiles share each dequantised B tile once an
+// expert has more than 128 rows), 256- or 128-wide column tiles, and the K split.
+struct Plan {
+    int mt, ks;
+    bool wide;
+    ExpertRows g;
+};
+
+// Tile width and K split from a cost model in microseconds: per wave of CTAs (one per SM), the
+// k-blocks of a CTA x the k-block time of the width (about 1 us at 256 columns; at 128 columns
+// 0.6 of that with one A tile per CTA, where the dequantising warps' fixed cost per k-block
+// dominates, and 0.8 with two, where the MMAs weigh more) plus 3 for a CTA's prologue, pipeline
+// fill and epilogue; a K split adds 1 plus its fp32 partials written and read back at an
+// effective 2.5 TB/s (the separate sum launch included); K is split only when the unsplit tiles fill at most half the SMs (at larger grids the
+// partials cost more than the model's estimate).  Measured against the earlier fill-the-wave rule: NVFP4 5120 x 5120 M = 16, 17 us (21);
+// GPTQ 5120 x 17408 M = 32, 35 us (45); 17408 x 5120 M = 256, 64 us (80); 7 experts of 17..40
+// rows, 2688 x 1856, 21 us (25); unchanged choices at 5120 x 5120 M = 128..8192 and 5120 x 27648
+// M = 2048.  K splits keep at least four k-blocks each, at most 8.
+// false: more experts than the table holds.
+static bool plan_for(const int *off, int n, int N, int K, Plan &p) {
+    int max_rows = 0;
+    for (int e = 0; e < n; ++e) max_rows = off[e + 1] - off[e] > max_rows ? off[e + 1] - off[e] : max_rows;
+    p.mt = max_rows > BM ? 2 : 1;
+    if (!expert_rows(p.g, off, n, BM * p.mt)) return false;
+    const long nsm = num_sms(), blocks = p.g.blk0[n], nk = K / BK;
+    const double partial_us_per_split = (double)off[n] * N * 8 / 2.5e6;  // fp32 written + read
+    long ks_max = nk / 4;
+    if (ks_max > 8) ks_max = 8;
+    if (ks_max < 1) ks_max = 1;
+    double best = 0;
+    p.wide = false;
+    p.ks = 1;
+    for (int w = 1; w >= 0; --w) {  // 256-wide first: it wins ties
+        if (w && N < 256) continue;
+        const long tiles = blocks * (w ? (N + 255) / 256 : (N + 127) / 128);
+        const long ks_top = 2 * tiles <= nsm ? ks_max : 1;  // split only grids that fill at most half the SMs
+        for (long ks = 1; ks <= ks_top; ++ks) {
+            const double waves = (double)((tiles * ks + nsm - 1) / nsm);
+            const double kb = (double)((nk + ks - 1) / ks);
+            const double t =
+                waves * (kb * (w ? 1.0 : (p.mt == 2 ? 0.8 : 0.6)) + 3.0) + (ks > 1 ? 1.0 + partial_us_per_split * ks : 0.0);
+            if (best == 0 || t < best - 1e-9) {
+                best = t;
+                p.wide = w == 1;
+                p.ks = (int)ks;
+            }
+        }
+    }
+    // tuning override W4_PREFILL="wide,ks" (wide 1: 256-column tiles, 0: 128; ks 1..8)
+    if (const char *e = std::getenv("W4_PREFILL")) {
+        int w = -1, k = 0;
+        if (std::sscanf(e, "%d,%d", &w, &k) == 2 && (w == 0 || (w == 1 && N >= 256)) && k >= 1 && k <= 8 &&
+            k <= K / BK) {
+            p.wide = w == 1;
+            p.ks = k;
+        }
+    }
+    return true;
 }
-// 256-wide tiles, unless they do not fill one wave and 128-wide ones need fewer
-// waves (a 128-wide tile takes about half as long): small M leaves SMs idle.
-static bool wide_tiles(int M, int N) {
-    if (N % 256) return false;
-    const long nsm = num_sms(), t256 = tiles_of(M, N, true);
-    if (t256 >= nsm) return true;
-    const long w256 = 2 * ((t256 + nsm - 1) / nsm), w128 = (2 * t256 + nsm - 1) / nsm;
-    return !(w128 < w256);
+
+static size_t split_bytes(const int *off, int n, int N, int K) {
+    Plan p;
+    if (!plan_for(off, n, N, K, p) || p.ks <= 1) return 0;
+    return (size_t)p.ks * off[n] * N * sizeof(float);
 }
-// K splits when the output tiles fill at most half the SMs: as many as still
-// fit one wave (one CTA per SM), at least four k-blocks per split, at most 8.
-static int ksplit_for(int M, int N, int K) {
-    const long nsm = num_sms();
-    const long tiles = tiles_of(M, N, wide_tiles(M, N));
-    if (2 * tiles > nsm) return 1;
-    long ks = nsm / tiles;
-    const long by_k = (K / BK) / 4;
-    if (ks > by_k) ks = by_k;
-    if (ks > 8) ks = 8;
-    return ks < 1 ? 1 : (int)ks;
+
+static int gptq_run(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
+                    const uint16_t *scales, const int *off, int n, int E, void *c, int c_dtype, int N, int K, int gs,
+                    int zero_offset, void *split_ws, size_t split_ws_bytes, cudaStream_t st) {
+    if (!handled(N, K, gs, c_dtype)) return -1;
+    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(qweight) |
+         reinterpret_cast<uintptr_t>(scales) | reinterpret_cast<uintptr_t>(qzeros)) & 15)
+        return -1;
+    Plan p;
+    if (!plan_for(off, n, N, K, p)) return -1;
+    const int M = off[n];
+    if (M == 0) return W4_OK;
+    int ks = p.ks;
+    if (ks > 1 && (!split_ws || split_ws_bytes < (size_t)ks * M * N * sizeof(float))) ks = 1;
+    float *partial = static_cast<float *>(split_ws);
+#define W4_PF_LAUNCH(TT, BNV, MTV) \
+    launch<TT, BNV, MTV>(a, qweight, qzeros, scales, c, c_dtype, p.g, E, M, N, K, gs, zero_offset, ks, partial, st)
+    if (a_dtype == W4_BF16) {
+        if (p.mt == 2) return p.wide ? W4_PF_LAUNCH(__nv_bfloat16, 256, 2) : W4_PF_LAUNCH(__nv_bfloat16, 128, 2);
+        return p.wide ? W4_PF_LAUNCH(__nv_bfloat16, 256, 1) : W4_PF_LAUNCH(__nv_bfloat16, 128, 1);
+    }
+    if (p.mt == 2) return p.wide ? W4_PF_LAUNCH(__half, 256, 2) : W4_PF_LAUNCH(__half, 128, 2);
+    return p.wide ? W4_PF_LAUNCH(__half, 256, 1) : W4_PF_LAUNCH(__half, 128, 1);
+#undef W4_PF_LAUNCH
+}
+
+static int fp4_run(const uint16_t *a, const uint8_t *w_nk, const uint8_t *scale, const float *w_global,
+                   const int *off, int n, int E, void *c, int c_dtype, int N, int K, void *split_ws,
+                   size_t split_ws_bytes, cudaStream_t st) {
+    if (!handled(N, K, BK, c_dtype)) return -1;
+    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(w_nk) | reinterpret_cast<uintptr_t>(scale)) &
+        15)
+        return -1;
+    Plan p;
+    if (!plan_for(off, n, N, K, p)) return -1;
+    const int M = off[n];
+    if (M == 0) return W4_OK;
+    int ks = p.ks;
+    if (ks > 1 && (!split_ws || split_ws_bytes < (size_t)ks * M * N * sizeof(float))) ks = 1;
+    float *partial = static_cast<float *>(split_ws);
+    if (p.mt == 2)
+        return p.wide ? launch_fp4<256, 2>(a, w_nk, scale, w_global, c, c_dtype, p.g, E, M, N, K, ks, partial, st)
+                      : launch_fp4<128, 2>(a, w_nk, scale, w_global, c, c_dtype, p.g, E, M, N, K, ks, partial, st);
+    return p.wide ? launch_fp4<256, 1>(a, w_nk, scale, w_global, c, c_dtype, p.g, E, M, N, K, ks, partial, st)
+                  : launch_fp4<128, 1>(a, w_nk, scale, w_global, c, c_dtype, p.g, E, M, N, K, ks, partial, st);
 }
 }  // namespace pf
 
 size_t gptq_prefill_split_bytes(int M, int N, int K, int gs, int c_dtype) {
     if (M < kPrefillMinM || !pf::handled(N, K, gs, c_dtype)) return 0;
-    const int ks = pf::ksplit_for(M, N, K);
-    return ks > 1 ? (size_t)ks * M * N * sizeof(float) : 0;
+    const int off[2] = {0, M};
+    return pf::split_bytes(off, 1, N, K);
 }
 
 // W4_OK / a W4 error, or -1 when this shape is not handled here (the caller
@@ -563,24 +663,21 @@ size_t gptq_prefill_split_bytes(int M, int N, int K, int gs, int c_dtype) {
 int gptq_prefill(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
                  void *c, int c_dtype, int M, int N, int K, int gs, int zero_offset, void *split_ws,
                  size_t split_ws_bytes, cudaStream_t st) {
-    if (!pf::handled(N, K, gs, c_dtype)) return -1;
-    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(qweight) |
-         reinterpret_cast<uintptr_t>(scales) | reinterpret_cast<uintptr_t>(qzeros)) & 15)
-        return -1;
-    const bool wide = pf::wide_tiles(M, N);
-    int ks = pf::ksplit_for(M, N, K);
-    if (ks > 1 && (!split_ws || split_ws_bytes < (size_t)ks * M * N * sizeof(float))) ks = 1;
-    float *partial = static_cast<float *>(split_ws);
-    const int mt = pf::m_tiles_per_cta(M);
-#define W4_PF_LAUNCH(TT, BNV, MTV) \
-    pf::launch<TT, BNV, MTV>(a, qweight, qzeros, scales, c, c_dtype, M, N, K, gs, zero_offset, ks, partial, st)
-    if (a_dtype == W4_BF16) {
-        if (mt == 2) return wide ? W4_PF_LAUNCH(__nv_bfloat16, 256, 2) : W4_PF_LAUNCH(__nv_bfloat16, 128, 2);
-        return wide ? W4_PF_LAUNCH(__nv_bfloat16, 256, 1) : W4_PF_LAUNCH(__nv_bfloat16, 128, 1);
-    }
-    if (mt == 2) return wide ? W4_PF_LAUNCH(__half, 256, 2) : W4_PF_LAUNCH(__half, 128, 2);
-    return wide ? W4_PF_LAUNCH(__half, 256, 1) : W4_PF_LAUNCH(__half, 128, 1);
-#undef W4_PF_LAUNCH
+    const int off[2] = {0, M};
+    return pf::gptq_run(a, a_dtype, qweight, qzeros, scales, off, 1, 1, c, c_dtype, N, K, gs, zero_offset, split_ws,
+                        split_ws_bytes, st);
+}
+
+size_t gptq_prefill_grouped_split_bytes(const int *off, int n, int N, int K, int gs, int c_dtype) {
+    if (!pf::handled(N, K, gs, c_dtype)) return 0;
+    return pf::split_bytes(off, n, N, K);
+}
+
+int gptq_prefill_grouped(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
+                         const uint16_t *scales, const int *off, int n, void *c, int c_dtype, int N, int K, int gs,
+                         int zero_offset, void *split_ws, size_t split_ws_bytes, cudaStream_t st) {
+    return pf::gptq_run(a, a_dtype, qweight, qzeros, scales, off, n, n, c, c_dtype, N, K, gs, zero_offset, split_ws,
+                        split_ws_bytes, st);
 }
 
 int splitk_reduce(const float *partial, int splits, long mn, void *c, int c_dtype, cudaStream_t st) {
@@ -591,8 +688,8 @@ int splitk_reduce(const float *partial, int splits, long mn, void *c, int c_dtyp
 
 size_t nvfp4_w4a16_prefill_split_bytes(int M, int N, int K, int c_dtype) {
     if (M < kFp4PrefillMinM || !pf::handled(N, K, pf::BK, c_dtype)) return 0;
-    const int ks = pf::ksplit_for(M, N, K);
-    return ks > 1 ? (size_t)ks * M * N * sizeof(float) : 0;
+    const int off[2] = {0, M};
+    return pf::split_bytes(off, 1, N, K);
 }
 
 // NVFP4 W4A16 on the tensor cores (M >= kFp4PrefillMinM): W4_OK / a W4 error, or -1
@@ -600,19 +697,20 @@ size_t nvfp4_w4a16_prefill_split_bytes(int M, int N, int K, int c_dtype) {
 int nvfp4_w4a16_prefill(const uint16_t *a, const uint8_t *w_nk, const uint8_t *scale, const float *w_global,
                         void *c, int c_dtype, int M, int N, int K, void *split_ws, size_t split_ws_bytes,
                         cudaStream_t st) {
-    if (M < kFp4PrefillMinM || !pf::handled(N, K, pf::BK, c_dtype)) return -1;
-    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(w_nk) | reinterpret_cast<uintptr_t>(scale)) &
-        15)
-        return -1;
-    const bool wide = pf::wide_tiles(M, N);
-    int ks = pf::ksplit_for(M, N, K);
-    if (ks > 1 && (!split_ws || split_ws_bytes < (size_t)ks * M * N * sizeof(float))) ks = 1;
-    float *partial = static_cast<float *>(split_ws);
-    if (pf::m_tiles_per_cta(M) == 2)
-        return wide ? pf::launch_fp4<256, 2>(a, w_nk, scale, w_global, c, c_dtype, M, N, K, ks, partial, st)
-                    : pf::launch_fp4<128, 2>(a, w_nk, scale, w_global, c, c_dtype, M, N, K, ks, partial, st);
-    return wide ? pf::launch_fp4<256, 1>(a, w_nk, scale, w_global, c, c_dtype, M, N, K, ks, partial, st)
-                : pf::launch_fp4<128, 1>(a, w_nk, scale, w_global, c, c_dtype, M, N, K, ks, partial, st);
+    if (M < kFp4PrefillMinM) return -1;
+    const int off[2] = {0, M};
+    return pf::fp4_run(a, w_nk, scale, w_global, off, 1, 1, c, c_dtype, N, K, split_ws, split_ws_bytes, st);
+}
+
+size_t nvfp4_w4a16_prefill_grouped_split_bytes(const int *off, int n, int N, int K, int c_dtype) {
+    if (!pf::handled(N, K, pf::BK, c_dtype)) return 0;
+    return pf::split_bytes(off, n, N, K);
+}
+
+int nvfp4_w4a16_prefill_grouped(const uint16_t *a, const uint8_t *w_nk, const uint8_t *scale, const float *w_global,
+                                const int *off, int n, void *c, int c_dtype, int N, int K, void *split_ws,
+                                size_t split_ws_bytes, cudaStream_t st) {
+    return pf::fp4_run(a, w_nk, scale, w_global, off, n, n, c, c_dtype, N, K, split_ws, split_ws_bytes, st);
 }
 
 int take_prefill_wait_status() {

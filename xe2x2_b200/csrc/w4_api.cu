@@ -235,13 +235,25 @@ static int check_offsets(const int32_t *off, int n, int *rows) {
     return W4_OK;
 }
 
+// Rows of the largest expert (offsets already checked).
+static int max_expert_rows(const int32_t *off, int n) {
+    int m = 0;
+    for (int e = 0; e < n; ++e) m = off[e + 1] - off[e] > m ? off[e + 1] - off[e] : m;
+    return m;
+}
+
 size_t w4_gptq_gemm_grouped_workspace_bytes(const int32_t *offsets, int num_experts, int N, int K, int group_size,
                                             int c_dtype) {
     int rows = 0;
     if (check_offsets(offsets, num_experts, &rows) || N <= 0 || K <= 0 || group_size <= 0) return 0;
     size_t ws = W4_WORKSPACE_SYNC_BYTES;
     if (c_dtype == W4_E4M3) ws += align256((size_t)rows * N * 4);
-    return ws + align256(w4::gptq_decode_grouped_split_bytes(offsets, num_experts, N, K, group_size));
+    const int odt = c_dtype == W4_E4M3 ? W4_F32 : c_dtype;
+    const size_t dec = w4::gptq_decode_grouped_split_bytes(offsets, num_experts, N, K, group_size);
+    const size_t pf = max_expert_rows(offsets, num_experts) >= w4::kGroupedPrefillMinRows
+                          ? w4::gptq_prefill_grouped_split_bytes(offsets, num_experts, N, K, group_size, odt)
+                          : 0;
+    return ws + align256(dec > pf ? dec : pf);
 }
 
 int w4_gptq_gemm_grouped(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
@@ -268,9 +280,15 @@ int w4_gptq_gemm_grouped(const void *a, int a_dtype, const int32_t *qweight, con
         out = ws;
         ws += align256((size_t)rows * N * 4);
     }
-    rc = w4::gptq_gemv_decode_grouped(a, a_dtype, qweight, qzeros, scales, offsets, num_experts, out,
-                                      c_dtype == W4_E4M3 ? W4_F32 : c_dtype, N, K, group_size, zero_offset, sync, ws,
-                                      workspace_bytes - (size_t)(ws - sync), st);
+    const int odt = c_dtype == W4_E4M3 ? W4_F32 : c_dtype;
+    const size_t have = workspace_bytes - (size_t)(ws - sync);
+    rc = -1;
+    if (max_expert_rows(offsets, num_experts) >= w4::kGroupedPrefillMinRows)
+        rc = w4::gptq_prefill_grouped(a, a_dtype, qweight, qzeros, scales, offsets, num_experts, out, odt, N, K,
+                                      group_size, zero_offset, ws, have, st);
+    if (rc == -1)
+        rc = w4::gptq_gemv_decode_grouped(a, a_dtype, qweight, qzeros, scales, offsets, num_experts, out, odt, N, K,
+                                          group_size, zero_offset, sync, ws, have, st);
     if (rc == -1) {
         w4::set_error("grouped GPTQ GEMM: shape not handled (N %% 32, K %% 8, group size 32, 64 or a multiple of "
                       "128, 16-byte aligned tensors)");
@@ -285,7 +303,12 @@ size_t w4_nvfp4_gemm_grouped_workspace_bytes(const int32_t *offsets, int num_exp
     if (check_offsets(offsets, num_experts, &rows) || N <= 0 || K <= 0) return 0;
     size_t ws = W4_WORKSPACE_SYNC_BYTES;
     if (c_dtype == W4_E4M3) ws += align256((size_t)rows * N * 4);
-    return ws + align256(w4::nvfp4_decode_grouped_split_bytes(offsets, num_experts, N, K));
+    const int odt = c_dtype == W4_E4M3 ? W4_F32 : c_dtype;
+    const size_t dec = w4::nvfp4_decode_grouped_split_bytes(offsets, num_experts, N, K);
+    const size_t pf = max_expert_rows(offsets, num_experts) >= w4::kGroupedPrefillMinRows
+                          ? w4::nvfp4_w4a16_prefill_grouped_split_bytes(offsets, num_experts, N, K, odt)
+                          : 0;
+    return ws + align256(dec > pf ? dec : pf);
 }
 
 int w4_nvfp4_gemm_grouped(const void *a, const uint8_t *w, const uint8_t *scale, const float *global_scale,
@@ -316,9 +339,15 @@ int w4_nvfp4_gemm_grouped(const void *a, const uint8_t *w, const uint8_t *scale,
         out = ws;
         ws += align256((size_t)rows * N * 4);
     }
-    rc = w4::nvfp4_gemv_decode_grouped(static_cast<const uint16_t *>(a), w, scale, W4_E4M3, global_scale, offsets,
-                                       num_experts, out, c_dtype == W4_E4M3 ? W4_F32 : c_dtype, N, K, sync, ws,
-                                       workspace_bytes - (size_t)(ws - sync), st);
+    const int odt = c_dtype == W4_E4M3 ? W4_F32 : c_dtype;
+    const size_t have = workspace_bytes - (size_t)(ws - sync);
+    rc = -1;
+    if (max_expert_rows(offsets, num_experts) >= w4::kGroupedPrefillMinRows)
+        rc = w4::nvfp4_w4a16_prefill_grouped(static_cast<const uint16_t *>(a), w, scale, global_scale, offsets,
+                                             num_experts, out, odt, N, K, ws, have, st);
+    if (rc == -1)
+        rc = w4::nvfp4_gemv_decode_grouped(static_cast<const uint16_t *>(a), w, scale, W4_E4M3, global_scale,
+                                           offsets, num_experts, out, odt, N, K, sync, ws, have, st);
     if (rc == -1) {
         w4::set_error("grouped NVFP4 GEMM: shape not handled by the decode kernel");
         return W4_ERR_UNSUPPORTED;

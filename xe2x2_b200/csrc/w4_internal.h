@@ -83,6 +83,20 @@ int nvfp4_w4a16_prefill(const uint16_t *a, const uint8_t *w_nk, const uint8_t *s
                         void *c, int c_dtype, int M, int N, int K, void *split_ws, size_t split_ws_bytes,
                         cudaStream_t st);
 size_t nvfp4_w4a16_prefill_split_bytes(int M, int N, int K, int c_dtype);
+// The same tensor-core GEMMs over E stacked expert matrices, rows off[e]..off[e+1] of a and c
+// for expert e (gptq_prefill.cu); -1 = not handled there
+int gptq_prefill_grouped(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
+                         const uint16_t *scales, const int *off, int n, void *c, int c_dtype, int N, int K, int gs,
+                         int zero_offset, void *split_ws, size_t split_ws_bytes, cudaStream_t st);
+size_t gptq_prefill_grouped_split_bytes(const int *off, int n, int N, int K, int gs, int c_dtype);
+int nvfp4_w4a16_prefill_grouped(const uint16_t *a, const uint8_t *w_nk, const uint8_t *scale, const float *w_global,
+                                const int *off, int n, void *c, int c_dtype, int N, int K, void *split_ws,
+                                size_t split_ws_bytes, cudaStream_t st);
+size_t nvfp4_w4a16_prefill_grouped_split_bytes(const int *off, int n, int N, int K, int c_dtype);
+// Grouped calls whose largest expert has more rows than this run the tensor-core GEMM (each
+// expert's weight tile dequantised once for up to 256 of its rows) instead of the decode kernel
+// (one pass over the weights per 16 rows)
+constexpr int kGroupedPrefillMinRows = 17;
 constexpr int kPrefillMinM = 17;  // token counts from here on run the tensor-core prefill GEMM
 // NVFP4 W4A16: the two-token-tile decode kernel (M = 9..16) is slower than the tensor-core
 // GEMM, which therefore starts at 9 tokens
