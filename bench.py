@@ -512,7 +512,7 @@ def run_decode(args) -> None:
     # the same way over as many buffers of one M = 1 launch's bytes: the practical ceiling of a
     # GEMM launch that reads its operands once (launch ramp and tail included)
     rb = alg_bytes(1) // 16 * 16
-    probe_bufs = [torch.zeros(rb, dtype=torch.uint8, device=dev) for _ in range(R)]
+    probe_bufs = [torch.randint(0, 256, (rb,), dtype=torch.uint8, device=dev) for _ in range(R)]
     sink = torch.zeros(1, dtype=torch.int32, device=dev)
     probe_us = time_graph(lambda r: L.call("w4_read_probe", ops._p(probe_bufs[r % R]), rb, ops._p(sink),
                                            ops._stream(dev)), max(30, 2 * R))
