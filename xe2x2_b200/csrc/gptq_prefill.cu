@@ -543,6 +543,7 @@ static bool handled(int N, int K, int gs, int c_dtype) {
 struct Plan {
     int mt, ks;
     bool wide;
+    double cost;  // the model's estimate (us)
     ExpertRows g;
 };
 
@@ -570,6 +571,7 @@ static bool plan_for(const int *off, int n, int N, int K, Plan &p) {
     double best = 0;
     p.wide = false;
     p.ks = 1;
+    p.cost = 0;
     for (int w = 1; w >= 0; --w) {  // 256-wide first: it wins ties
         if (w && N < 256) continue;
         const long tiles = blocks * (w ? (N + 255) / 256 : (N + 127) / 128);
@@ -583,6 +585,7 @@ static bool plan_for(const int *off, int n, int N, int K, Plan &p) {
                 best = t;
                 p.wide = w == 1;
                 p.ks = (int)ks;
+                p.cost = t;
             }
         }
     }
@@ -598,19 +601,65 @@ static bool plan_for(const int *off, int n, int N, int K, Plan &p) {
     return true;
 }
 
-static size_t split_bytes(const int *off, int n, int N, int K) {
+static size_t split_bytes_of(const int *off, int n, int N, int K) {
     Plan p;
     if (!plan_for(off, n, N, K, p) || p.ks <= 1) return 0;
     return (size_t)p.ks * off[n] * N * sizeof(float);
 }
 
+// A plain call whose tiles leave the last wave partly empty (5120^2 at M = 2048: 160 tiles of
+// 256 x 256 for 148 SMs) runs as two calls along M: the row blocks that fill whole waves
+// unsplit, the rest as a second call that the plan may split along K.  Returns the rows of the
+// first part when the model predicts the pair faster (2 us allowed for the second launch),
+// else 0.
+static int tail_rows(int M, int N, int K) {
+    if (std::getenv("W4_PREFILL")) return 0;  // a forced plan applies to the whole call
+    const int off[2] = {0, M};
+    Plan whole;
+    if (!plan_for(off, 1, N, K, whole)) return 0;
+    const long nsm = num_sms();
+    const long ntile = whole.wide ? (N + 255) / 256 : (N + 127) / 128;
+    const long tiles = (long)whole.g.blk0[1] * ntile;
+    const long full_waves = tiles / nsm;
+    if (full_waves == 0 || tiles % nsm == 0) return 0;
+    const int M1 = (int)(full_waves * nsm / ntile) * BM * whole.mt;
+    if (M1 <= 0 || M1 >= M) return 0;
+    const int off1[2] = {0, M1}, off2[2] = {0, M - M1};
+    Plan p1, p2;
+    if (!plan_for(off1, 1, N, K, p1) || !plan_for(off2, 1, N, K, p2)) return 0;
+    return p1.cost + p2.cost + 2.0 < whole.cost ? M1 : 0;
+}
+
+static size_t split_bytes(const int *off, int n, int N, int K) {
+    if (n == 1) {
+        if (const int M1 = tail_rows(off[1], N, K)) {
+            const int off1[2] = {0, M1}, off2[2] = {0, off[1] - M1};
+            const size_t b1 = split_bytes_of(off1, 1, N, K), b2 = split_bytes_of(off2, 1, N, K);
+            return b1 > b2 ? b1 : b2;
+        }
+    }
+    return split_bytes_of(off, n, N, K);
+}
+
 static int gptq_run(const void *a, int a_dtype, const int32_t *qweight, const int32_t *qzeros,
                     const uint16_t *scales, const int *off, int n, int E, void *c, int c_dtype, int N, int K, int gs,
-                    int zero_offset, void *split_ws, size_t split_ws_bytes, cudaStream_t st) {
+                    int zero_offset, void *split_ws, size_t split_ws_bytes, cudaStream_t st, bool tail = true) {
     if (!handled(N, K, gs, c_dtype)) return -1;
     if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(qweight) |
          reinterpret_cast<uintptr_t>(scales) | reinterpret_cast<uintptr_t>(qzeros)) & 15)
         return -1;
+    if (tail && n == 1) {
+        if (const int M1 = tail_rows(off[1], N, K)) {
+            const int off1[2] = {0, M1}, off2[2] = {0, off[1] - M1};
+            const size_t csz = c_dtype == W4_F32 ? 4 : 2;
+            int rc = gptq_run(a, a_dtype, qweight, qzeros, scales, off1, 1, 1, c, c_dtype, N, K, gs, zero_offset,
+                              split_ws, split_ws_bytes, st, false);
+            if (rc) return rc;
+            return gptq_run(static_cast<const uint16_t *>(a) + (size_t)M1 * K, a_dtype, qweight, qzeros, scales, off2,
+                            1, 1, static_cast<char *>(c) + (size_t)M1 * N * csz, c_dtype, N, K, gs, zero_offset,
+                            split_ws, split_ws_bytes, st, false);
+        }
+    }
     Plan p;
     if (!plan_for(off, n, N, K, p)) return -1;
     const int M = off[n];
@@ -631,11 +680,23 @@ static int gptq_run(const void *a, int a_dtype, const int32_t *qweight, const in
 
 static int fp4_run(const uint16_t *a, const uint8_t *w_nk, const uint8_t *scale, const float *w_global,
                    const int *off, int n, int E, void *c, int c_dtype, int N, int K, void *split_ws,
-                   size_t split_ws_bytes, cudaStream_t st) {
+                   size_t split_ws_bytes, cudaStream_t st, bool tail = true) {
     if (!handled(N, K, BK, c_dtype)) return -1;
     if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(w_nk) | reinterpret_cast<uintptr_t>(scale)) &
         15)
         return -1;
+    if (tail && n == 1) {
+        if (const int M1 = tail_rows(off[1], N, K)) {
+            const int off1[2] = {0, M1}, off2[2] = {0, off[1] - M1};
+            const size_t csz = c_dtype == W4_F32 ? 4 : 2;
+            int rc = fp4_run(a, w_nk, scale, w_global, off1, 1, 1, c, c_dtype, N, K, split_ws, split_ws_bytes, st,
+                             false);
+            if (rc) return rc;
+            return fp4_run(a + (size_t)M1 * K, w_nk, scale, w_global, off2, 1, 1,
+                           static_cast<char *>(c) + (size_t)M1 * N * csz, c_dtype, N, K, split_ws, split_ws_bytes, st,
+                           false);
+        }
+    }
     Plan p;
     if (!plan_for(off, n, N, K, p)) return -1;
     const int M = off[n];
