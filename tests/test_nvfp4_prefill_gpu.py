@@ -71,16 +71,19 @@ def test_nvfp4_act_rejects_unsupported(cuda):
     assert ei.value.status == L.W4_ERR_UNSUPPORTED
 
 
-@pytest.mark.parametrize("M", [128, 2048, 8192])
+@pytest.mark.parametrize("M", [128, 2048, 4096, 8192])
 def test_config3_prefill_sampled_rows(cuda, M):
     """BASELINE config 3 prefill shapes: K=N=5120, activations quantised to NVFP4 on the fly;
-    64 sampled rows x all N against the oracle."""
+    64 sampled rows x all N against the oracle, plus the rows either side of where a call with
+    a partly empty last round is split along M (M = 2048: 1792, M = 4096: 3712)."""
     K, N = 5120, 5120
     w, scale, gscale = synth.nvfp4_weights(K, N, seed=0, device=cuda)
     x = synth.activations(M, K, torch.bfloat16, seed=1, device=cuda)
     ag = _a_global(x)
     y = ops.nvfp4_gemm(x, w, scale, gscale, out_dtype=torch.float32, act_mode=L.W4_ACT_NVFP4, a_global=ag)
-    rows = torch.randperm(M, generator=torch.Generator().manual_seed(M))[:64].sort().values.to(cuda)
+    edges = torch.tensor([r for r in (0, 1791, 1792, 3711, 3712, M - 1) if r < M])
+    rows = torch.cat([torch.randperm(M, generator=torch.Generator().manual_seed(M))[:64], edges])
+    rows = torch.unique(rows).to(cuda)
     rf, _ = assert_gemm_close(np_(y[rows]), _oracle(x, w, scale, gscale, ag, rows))
     assert rf < 1e-5, rf
 
