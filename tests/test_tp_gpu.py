@@ -139,9 +139,11 @@ def _case_fused_row_parallel(rank, world):
                 u32 = lay(xs, out_dtype=torch.float32)
                 comm.wait()
                 # exact products either way; the fused and the un-fused GEMMs sum them in fp32 in
-                # different orders (the un-fused one per 128-k unit and over a K split)
-                assert _rel(f32, u32) < 1e-5, (K, N, M)
-                assert _rel(f32, full) < 1e-5
+                # different orders (the un-fused one per 128-k unit and over a K split), each with
+                # codes entering the MMA as 1024 + q: an fp32 sum about 128x the result's size,
+                # hence up to ~1e-5 from the exact product each (the contract allows 1e-2)
+                assert _rel(f32, u32) < 5e-5, (K, N, M)
+                assert _rel(f32, full) < 5e-5
                 assert _rel(b16, full) < 1e-2
                 assert _rel(q8.float() * rs[:, None], full) < 4e-2
                 got = [torch.empty_like(f32.cpu()) for _ in range(world)]
