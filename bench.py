@@ -178,6 +178,41 @@ def time_graph(fn, reps: int) -> float:
     return e0.elapsed_time(e1) * 1e3 / (5 * reps)
 
 
+def graph_kernels(graph) -> dict | None:
+    """Kernel nodes of a captured CUDA graph (torch ``CUDAGraph(keep_graph=True)``) by origin:
+    ``w4`` (this library's kernels: mangled names in namespace w4), ``nccl`` and ``other``.
+    None when the graph cannot be inspected (cuda-python missing or an unexpected driver)."""
+    try:
+        from cuda.bindings import driver as drv
+        g = drv.CUgraph(graph.raw_cuda_graph())
+        err, _, n = drv.cuGraphGetNodes(g, 0)
+        if err != drv.CUresult.CUDA_SUCCESS:
+            return None
+        err, nodes, n = drv.cuGraphGetNodes(g, n)
+        counts = {"w4": 0, "nccl": 0, "other": 0}
+        for nd in nodes[:n]:
+            err, t = drv.cuGraphNodeGetType(nd)
+            if err != drv.CUresult.CUDA_SUCCESS or t != drv.CUgraphNodeType.CU_GRAPH_NODE_TYPE_KERNEL:
+                continue
+            err, prm = drv.cuGraphKernelNodeGetParams(nd)
+            if err != drv.CUresult.CUDA_SUCCESS:
+                return None
+            name = b""
+            fn, kern = getattr(prm, "func", None), getattr(prm, "kern", None)
+            if fn is not None and int(fn):
+                err, name = drv.cuFuncGetName(fn)
+            elif kern is not None and int(kern):
+                err, name = drv.cuKernelGetName(kern)
+            if err != drv.CUresult.CUDA_SUCCESS or not name:
+                return None
+            name = name.decode() if isinstance(name, bytes) else str(name)
+            key = "w4" if "2w4" in name[:12] else ("nccl" if "nccl" in name[:24] else "other")
+            counts[key] += 1
+        return counts
+    except Exception:  # noqa: BLE001 - introspection is best effort; the caller reports None
+        return None
+
+
 def copies_for(nbytes: int, l2: int) -> int:
     """Weight copies that together exceed twice the L2 (every launch then reads HBM)."""
     return max(2, math.ceil(2 * l2 / max(nbytes, 1)) + 1)
@@ -463,10 +498,12 @@ def run_decode(args) -> None:
     cap = torch.cuda.Stream()
     cap.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(cap):
-        graph = torch.cuda.CUDAGraph()
+        graph = torch.cuda.CUDAGraph(keep_graph=True)  # kept: its kernel nodes are counted
         with torch.cuda.graph(graph, stream=cap):
             step()
     torch.cuda.current_stream().wait_stream(cap)
+    step_kernels = graph_kernels(graph)
+    graph.instantiate()
     torch.cuda.synchronize()
 
     def barrier():
@@ -621,7 +658,8 @@ def run_decode(args) -> None:
                          "kernel": "w4::dec::gptq_decode_kernel (M = 1, 4, 8), w4::gptq_gemv_kernel (M = 16)",
                          "peak_source": pk["source"] + " hbm_gbs (copy)",
                          "per_m": per_m, "read_ceiling": read_ceiling},
-            "gpu_launches": gemms_per_step * args.steps,
+            "gpu_launches": gemms_per_step * args.steps if step_kernels is None else step_kernels["w4"] * args.steps,
+            "graph_kernels_per_step": step_kernels,
             "decode_fallbacks": fallbacks,
             "clocks": clk,
         }
@@ -735,12 +773,14 @@ def run_tp(args) -> None:
     cap = torch.cuda.Stream()
     cap.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(cap):
-        graph = torch.cuda.CUDAGraph()
+        graph = torch.cuda.CUDAGraph(keep_graph=True)  # kept: its kernel nodes are counted
         with torch.cuda.graph(graph, stream=cap):
             step()
     torch.cuda.current_stream().wait_stream(cap)
+    step_kernels = graph_kernels(graph)
+    graph.instantiate()
     barrier()
-    trace("graph captured")
+    trace(f"graph captured: kernels per step {step_kernels}")
     for _ in range(args.warmup):
         graph.replay()
     if comm is not None:
@@ -760,6 +800,39 @@ def run_tp(args) -> None:
     clk = clocks.stop()
     ms = max_over_ranks(e0.elapsed_time(e1))
     trace(f"timed region: {ms:.3f} ms")
+
+    # ---------------- end to end: every step's activations in from pinned host memory, every
+    # projection's output back to pinned host memory, around the same rotation (one graph)
+    h_xs = {M: {k: v.cpu().pin_memory() for k, v in xs[M].items()} for M in TP_MS}
+    h_outs = {M: {k: torch.empty(v.shape, dtype=v.dtype).pin_memory() for k, v in outs[M].items()} for M in TP_MS}
+
+    def e2e_step():
+        for M in TP_MS:
+            for k in xs[M]:
+                xs[M][k].copy_(h_xs[M][k], non_blocking=True)
+        step()
+        for M in TP_MS:
+            for k in outs[M]:
+                h_outs[M][k].copy_(outs[M][k], non_blocking=True)
+
+    h2d = sum(t.numel() * t.element_size() for M in TP_MS for t in h_xs[M].values())
+    d2h = sum(t.numel() * t.element_size() for M in TP_MS for t in h_outs[M].values())
+    with torch.cuda.stream(cap):
+        g_e2e = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_e2e, stream=cap):
+            e2e_step()
+    torch.cuda.current_stream().wait_stream(cap)
+    for _ in range(args.warmup):
+        g_e2e.replay()
+    barrier()
+    e0.record(st)
+    for _ in range(args.steps):
+        g_e2e.replay()
+    e1.record(st)
+    barrier()
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1))
+    del g_e2e  # holds collective work: gone before the communicator is
+    trace(f"e2e region: {ms_e2e:.3f} ms")
 
     # per-M layer time and all-reduce time alone (graphs of one M / of the bare collectives)
     per_m = {}
@@ -818,6 +891,7 @@ def run_tp(args) -> None:
 
     step_bytes_tp = R * sum(sets[0].bytes(M) for M in TP_MS)
     value = step_bytes_tp * args.steps / (ms / 1e3) / 1e9
+    e2e_value = step_bytes_tp * args.steps / (ms_e2e / 1e3) / 1e9
     pk = peaks()
     fallbacks = lib.w4_decode_fallback_count() - fb0
     if rank == 0:
@@ -834,7 +908,14 @@ def run_tp(args) -> None:
             "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": round(pk["hbm"] * world, 1),
                          "unit": "GB/s", "frac": round(value / (pk["hbm"] * world), 4), "traffic": None,
                          "peak_source": f"{world} x {pk['source']} hbm_gbs", "per_m": per_m},
-            "gpu_launches": None, "decode_fallbacks": fallbacks, "clocks": clk,
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h,
+                    "path": "tp.TPLayerSet.step (w4_tp_linear per projection shard); every step copies its "
+                            "activations in from pinned host memory and every projection's output back, "
+                            "in one CUDA graph per step", "ms_per_step": round(ms_e2e / args.steps, 5)},
+            "gpu_launches": None if step_kernels is None else step_kernels["w4"] * args.steps,
+            "graph_kernels_per_step": step_kernels,
+            "decode_fallbacks": fallbacks, "clocks": clk,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
