@@ -180,8 +180,9 @@ def time_graph(fn, reps: int) -> float:
 
 def graph_kernels(graph) -> dict | None:
     """Kernel nodes of a captured CUDA graph (torch ``CUDAGraph(keep_graph=True)``) by origin:
-    ``w4`` (this library's kernels: mangled names in namespace w4), ``nccl`` and ``other``.
-    None when the graph cannot be inspected (cuda-python missing or an unexpected driver)."""
+    ``w4`` (this library's kernels: mangled names in namespace w4), ``nccl`` and ``other``, with
+    the names of the ``other`` ones.  None when the graph cannot be inspected (cuda-python missing
+    or an unexpected driver)."""
     try:
         from cuda.bindings import driver as drv
         g = drv.CUgraph(graph.raw_cuda_graph())
@@ -190,6 +191,7 @@ def graph_kernels(graph) -> dict | None:
             return None
         err, nodes, n = drv.cuGraphGetNodes(g, n)
         counts = {"w4": 0, "nccl": 0, "other": 0}
+        others = set()
         for nd in nodes[:n]:
             err, t = drv.cuGraphNodeGetType(nd)
             if err != drv.CUresult.CUDA_SUCCESS or t != drv.CUgraphNodeType.CU_GRAPH_NODE_TYPE_KERNEL:
@@ -208,6 +210,10 @@ def graph_kernels(graph) -> dict | None:
             name = name.decode() if isinstance(name, bytes) else str(name)
             key = "w4" if "2w4" in name[:12] else ("nccl" if "nccl" in name[:24] else "other")
             counts[key] += 1
+            if key == "other":
+                others.add(name[:120])
+        if others:
+            counts["other_names"] = sorted(others)
         return counts
     except Exception:  # noqa: BLE001 - introspection is best effort; the caller reports None
         return None

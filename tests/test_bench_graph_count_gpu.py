@@ -20,6 +20,8 @@ def test_graph_kernels_counts_one_decode_gemm(cuda):
     st.wait_stream(torch.cuda.current_stream(cuda))
     g = torch.cuda.CUDAGraph(keep_graph=True)
     with torch.cuda.stream(st):
+        ops.gptq_gemm(a, qw, qz, sc, gs, 1, out=out)  # this stream's workspace exists before capture
+        torch.cuda.synchronize()
         with torch.cuda.graph(g, stream=st):
             ops.gptq_gemm(a, qw, qz, sc, gs, 1, out=out)
     torch.cuda.current_stream(cuda).wait_stream(st)
