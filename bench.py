@@ -771,12 +771,17 @@ def run_tp(args) -> None:
         return float(t.item())
 
     trace(f"{R} layer sets built")
-    step()
+    # eager warm-up on the capture stream: the per-stream workspaces (zero-filled when first
+    # allocated) exist before capture, so no fill kernel lands in the step graph
+    cap = torch.cuda.Stream()
+    cap.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cap):
+        step()
+    torch.cuda.current_stream().wait_stream(cap)
     if comm is not None:
         comm.wait()
     barrier()
     trace("eager warm-up done")
-    cap = torch.cuda.Stream()
     cap.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(cap):
         graph = torch.cuda.CUDAGraph(keep_graph=True)  # kept: its kernel nodes are counted
