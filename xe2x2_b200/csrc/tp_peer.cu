@@ -18,7 +18,10 @@
 // still reading, because each call waits for every peer's push of that call.
 // The counters live in device memory, so captured CUDA graphs replay correctly.
 // No copy here is a TMA or bulk load, and nothing uses multicast.
-// The same buffer also carries the epilogue all-reduce of the fused
+// Messages up to 64 KB (decode-sized outputs) take a second form that needs
+// neither the fence nor the flags: every 4-byte word travels with the call
+// number in one 8-byte store and readers wait on the words themselves (see
+// ll_off).  The same buffer also carries the epilogue all-reduce of the fused
 // row-parallel decode GEMM (separate slots, flags and sequence; see fdata_off).
 #include <chrono>
 #include <thread>
@@ -48,7 +51,18 @@ constexpr int kFusedMaxCtas = 1024;
 static size_t fdata_off(int nranks) { return (ctr_off(nranks) + kTpMaxBlocks * sizeof(uint32_t) + 255) & ~size_t(255); }
 static size_t fflags_off(int nranks) { return fdata_off(nranks) + 2 * (size_t)nranks * kFusedSlotBytes; }
 static size_t fctrl_off(int nranks) { return fflags_off(nranks) + 2 * (size_t)kFusedMaxCtas * 8 * sizeof(uint32_t); }
-static size_t sym_bytes(int nranks) { return fctrl_off(nranks) + 256; }
+
+// A third region carries small messages (up to kLLMaxBytes) with the data and the call number
+// side by side: every 4-byte word of a partial travels as one 8-byte store {word, v}, and a
+// reader takes a word once its v matches, so no fence or separate flag is needed (an aligned
+// 8-byte store is observed whole).  Layout: slots [2 parities][nranks][kLLSlotBytes], then
+// this rank's call sequence and finished-block count.
+constexpr size_t kLLMaxBytes = size_t(64) << 10;
+constexpr size_t kLLSlotBytes = 2 * kLLMaxBytes;  // 8 bytes per 4-byte word
+constexpr int kLLWordsPerBlock = 2048;
+static size_t ll_off(int nranks) { return (fctrl_off(nranks) + 256 + 255) & ~size_t(255); }
+static size_t llctr_off(int nranks) { return ll_off(nranks) + 2 * (size_t)nranks * kLLSlotBytes; }
+static size_t sym_bytes(int nranks) { return llctr_off(nranks) + kTpMaxBlocks * sizeof(uint32_t) + 256; }
 
 struct PeerPtrs {
     char *p[kTpMaxRanks];
@@ -148,6 +162,89 @@ oneshot_allreduce_kernel(PeerPtrs pp, int rank, int nranks, T *__restrict__ data
     }
     __syncthreads();
     if (threadIdx.x == 0) *ctr = v;
+}
+
+// ---- the small-message form: data and call number in one 8-byte store ----
+__device__ __forceinline__ void st_ll(char *p, uint32_t d, uint32_t f) {
+    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(d), "r"(f) : "memory");
+}
+__device__ __forceinline__ uint2 ld_ll(const char *p) {
+    uint2 r;
+    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p) : "memory");
+    return r;
+}
+
+// A 4-byte word of T values, summed in fp32 and rounded back as the one-shot kernel does.
+template <typename T> struct Word {
+    static constexpr int E = 4 / sizeof(T);
+    static __device__ void add(float (&acc)[E], uint32_t w) {
+        const T *e = reinterpret_cast<const T *>(&w);
+#pragma unroll
+        for (int i = 0; i < E; ++i) acc[i] += Acc<T>::to(e[i]);
+    }
+    static __device__ uint32_t pack(const float (&acc)[E]) {
+        uint32_t w;
+        T *e = reinterpret_cast<T *>(&w);
+#pragma unroll
+        for (int i = 0; i < E; ++i) e[i] = Acc<T>::from(acc[i]);
+        return w;
+    }
+};
+
+// One call number per call, the same in every block: v = seq + 1 (parity v & 1), where seq
+// (ctl[0]) advances once the last block of the call is done (ctl[1] counts finished blocks), so
+// a word of an older call always carries an older number, whichever block moved it (the
+// word-to-block partition changes with the message size).  Block b owns words
+// [b * per_block, ...): each thread stores {word, v} of its words into slot [parity][rank] of
+// every rank, then sums slot [parity][0 .. nranks-1] of the same words in rank order as each
+// reads v (bounded by the time limit; after one expiry a thread stops waiting).  A thread
+// reads back only the words it wrote itself in its own slot.  Reuse of a parity is safe as in
+// the one-shot kernel: a rank is at most one call ahead of a peer still reading.
+template <typename T>
+__global__ void __launch_bounds__(kTpThreads)
+ll_allreduce_kernel(PeerPtrs pp, int rank, int nranks, T *__restrict__ data, long nwords, long per_block,
+                    size_t loff, size_t coff) {
+    const int b = blockIdx.x;
+    const long w0 = b * per_block, w1 = min(nwords, w0 + per_block);
+    uint32_t *ctl = reinterpret_cast<uint32_t *>(pp.p[rank] + coff);  // {call sequence, blocks done}
+    __shared__ uint32_t v_s;
+    if (threadIdx.x == 0) v_s = *reinterpret_cast<volatile uint32_t *>(ctl) + 1;
+    __syncthreads();
+    const uint32_t v = v_s;
+    const int par = v & 1;
+    uint32_t *words = reinterpret_cast<uint32_t *>(data);
+    for (long w = w0 + threadIdx.x; w < w1; w += kTpThreads) {
+        const uint32_t x = words[w];
+        for (int p = 0; p < nranks; ++p)
+            st_ll(pp.p[p] + loff + (size_t)(par * nranks + rank) * kLLSlotBytes + (size_t)w * 8, x, v);
+    }
+    bool waiting = true;
+    for (long w = w0 + threadIdx.x; w < w1; w += kTpThreads) {
+        float acc[Word<T>::E];
+#pragma unroll
+        for (int i = 0; i < Word<T>::E; ++i) acc[i] = 0.f;
+        for (int p = 0; p < nranks; ++p) {
+            const char *slot = pp.p[rank] + loff + (size_t)(par * nranks + p) * kLLSlotBytes + (size_t)w * 8;
+            uint2 r = ld_ll(slot);
+            if (r.y != v && waiting) {
+                const unsigned long long t0 = tp_ns();
+                while ((r = ld_ll(slot)).y != v) {
+                    if (tp_ns() - t0 > kTpWaitNs) {
+                        atomicExch(&g_tp_timeout, 1u);
+                        waiting = false;
+                        break;
+                    }
+                }
+            }
+            Word<T>::add(acc, r.x);
+        }
+        words[w] = Word<T>::pack(acc);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(&ctl[1], 1u) == gridDim.x - 1) {  // every block has read seq
+        ctl[1] = 0;
+        ctl[0] = v;
+    }
 }
 
 static int wait_stream_bounded(cudaStream_t st, int timeout_ms) {
@@ -281,6 +378,25 @@ int tp_peer_allreduce(w4_tp_comm *c, void *buf, size_t count, int dtype, cudaStr
     if (!c->p2p) return -1;
     const size_t es = dtype == W4_F32 ? 4 : 2;
     if (count * es > kTpSlotBytes || (count * es) % 16 || (reinterpret_cast<uintptr_t>(buf) & 15)) return -1;
+    PeerPtrs pp;
+    for (int p = 0; p < kTpMaxRanks; ++p) pp.p[p] = static_cast<char *>(c->peer[p]);
+    if (count * es <= kLLMaxBytes) {  // data and call number side by side: no fence, no flags
+        const long nwords = (long)(count * es / 4);
+        const long lblocks = (nwords + kLLWordsPerBlock - 1) / kLLWordsPerBlock;
+        const long lper = (nwords + lblocks - 1) / lblocks;
+        const size_t lo = ll_off(c->nranks), lc = llctr_off(c->nranks);
+        if (dtype == W4_BF16)
+            ll_allreduce_kernel<__nv_bfloat16><<<(unsigned)lblocks, kTpThreads, 0, st>>>(
+                pp, c->rank, c->nranks, static_cast<__nv_bfloat16 *>(buf), nwords, lper, lo, lc);
+        else if (dtype == W4_F16)
+            ll_allreduce_kernel<__half><<<(unsigned)lblocks, kTpThreads, 0, st>>>(
+                pp, c->rank, c->nranks, static_cast<__half *>(buf), nwords, lper, lo, lc);
+        else
+            ll_allreduce_kernel<float><<<(unsigned)lblocks, kTpThreads, 0, st>>>(
+                pp, c->rank, c->nranks, static_cast<float *>(buf), nwords, lper, lo, lc);
+        W4_LAUNCH_CHECK();
+        return W4_OK;
+    }
     const long n = (long)count;
     const long v = 16 / (long)es;
     long blocks = (n + 4095) / 4096;
@@ -289,8 +405,6 @@ int tp_peer_allreduce(w4_tp_comm *c, void *buf, size_t count, int dtype, cudaStr
     long per = (n + blocks - 1) / blocks;
     per = (per + v - 1) / v * v;  // whole 16-byte vectors per block
     blocks = (n + per - 1) / per;
-    PeerPtrs pp;
-    for (int p = 0; p < kTpMaxRanks; ++p) pp.p[p] = static_cast<char *>(c->peer[p]);
     const size_t fo = flags_off(c->nranks), co = ctr_off(c->nranks);
     if (dtype == W4_BF16)
         oneshot_allreduce_kernel<__nv_bfloat16><<<(unsigned)blocks, kTpThreads, 0, st>>>(
