@@ -924,8 +924,10 @@ def run_tp(args) -> None:
                     "path": "tp.TPLayerSet.step (w4_tp_linear per projection shard); every step copies its "
                             "activations in from pinned host memory and every projection's output back, "
                             "in one CUDA graph per step", "ms_per_step": round(ms_e2e / args.steps, 5)},
-            "gpu_launches": None if step_kernels is None else step_kernels["w4"] * args.steps,
-            "graph_kernels_per_step": step_kernels,
+            # counted from the step graph; if it cannot be inspected, the lower bound of one libw4
+            # kernel per GEMM call (12 per rotation)
+            "gpu_launches": (12 * R if step_kernels is None else step_kernels["w4"]) * args.steps,
+            "graph_kernels_per_step": step_kernels if step_kernels is not None else "not inspected: lower bound",
             "decode_fallbacks": fallbacks, "clocks": clk,
         }
         print(json.dumps(line), flush=True)
