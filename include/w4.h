@@ -99,7 +99,9 @@ int w4_check_device_status(void);
  *                              and reads nothing until that kernel completed.
  *   W4_OVERLAP_STATIC_WEIGHTS  as above, and it also starts streaming the
  *                              weight operands (qweight, scales, zeros / NVFP4
- *                              codes and block scales) before then.  Only for
+ *                              codes and block scales) before then, on calls
+ *                              where that measured faster (at most 16 MB of
+ *                              codes and four token rows per block).  Only for
  *                              callers whose weights are never written by the
  *                              kernel that precedes the GEMM on the stream
  *                              (inference on loaded checkpoints). */

@@ -540,7 +540,12 @@ static int launch_fp4d_t(const Fp4Call &q, Fp4Choice ch, cudaStream_t st) {
             if (dev >= 0 && dev < 128) set_dev[dev] = true;
         }
     }
-    const int pre = launch_overlap() == W4_OVERLAP_STATIC_WEIGHTS;
+    // static weights: the first ring fill is requested before the previous kernel completes, for
+    // at most four token rows on layers of at most 16 MB of codes (measured faster there: 5120^2
+    // M=1; slower on wider layers, where the early copies compete with the draining kernel's,
+    // and at 8 rows)
+    const int pre = launch_overlap() == W4_OVERLAP_STATIC_WEIGHTS && q.rows_alloc <= 4 &&
+                    (long long)N * K / 2 * q.E <= (16LL << 20);
     dim3 grid(mblocks, N / BN, ks), block(32 * (CW + 1));
     W4_CUDA_TRY(launch_decode(kern, grid, block, smem, st, 1u, w_map, sc_map, q.a, q.global_scale, q.c, q.c_dtype, q.M,
                               N, K, nst, max_st, S, pre, q.rows_alloc, q.grp, q.part, q.cnt, q.rowmax));
