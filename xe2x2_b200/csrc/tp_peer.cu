@@ -340,7 +340,7 @@ int tp_peer_setup(w4_tp_comm *c) {
             ok = false;
         }
     }
-    // Every rank must agree on using the peer path: all-reduce the verdicts.
+    // Every rank must agree on using the peer path: all-reduce the decisions.
     int *flag = nullptr;
     W4_CUDA_TRY(cudaMalloc(&flag, sizeof(int)));
     const int mine_ok = ok ? 1 : 0;
@@ -348,7 +348,7 @@ int tp_peer_setup(w4_tp_comm *c) {
     W4_CUDA_TRY(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
     r = api.all_reduce(flag, flag, 1, ncclInt32, ncclMin, c->comm, st);
     if (r != ncclSuccess && r != ncclInProgress) {
-        set_error("ncclAllReduce of peer verdicts: %s", api.error_string(r));
+        set_error("ncclAllReduce of the peer-path decisions: %s", api.error_string(r));
         rc = W4_ERR_NCCL;
     } else {
         rc = settle(api, c);
