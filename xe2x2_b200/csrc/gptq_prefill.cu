@@ -748,7 +748,7 @@ int splitk_reduce(const float *partial, int splits, long mn, void *c, int c_dtyp
 }
 
 size_t nvfp4_w4a16_prefill_split_bytes(int M, int N, int K, int c_dtype) {
-    if (M < kFp4PrefillMinM || !pf::handled(N, K, pf::BK, c_dtype)) return 0;
+    if (prefer_fp4_decode(M, N, K) || !pf::handled(N, K, pf::BK, c_dtype)) return 0;
     const int off[2] = {0, M};
     return pf::split_bytes(off, 1, N, K);
 }
@@ -758,7 +758,7 @@ size_t nvfp4_w4a16_prefill_split_bytes(int M, int N, int K, int c_dtype) {
 int nvfp4_w4a16_prefill(const uint16_t *a, const uint8_t *w_nk, const uint8_t *scale, const float *w_global,
                         void *c, int c_dtype, int M, int N, int K, void *split_ws, size_t split_ws_bytes,
                         cudaStream_t st) {
-    if (M < kFp4PrefillMinM) return -1;
+    if (prefer_fp4_decode(M, N, K)) return -1;  // the caller runs the decode kernel
     const int off[2] = {0, M};
     return pf::fp4_run(a, w_nk, scale, w_global, off, 1, 1, c, c_dtype, N, K, split_ws, split_ws_bytes, st);
 }

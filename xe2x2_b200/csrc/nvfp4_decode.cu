@@ -480,6 +480,20 @@ Fp4Choice fp4_choose(int mblocks, int N, int K) {
     return c;
 }
 
+}  // namespace
+
+// NVFP4 W4A16 with 9..16 tokens: the decode kernel (two token tiles) instead of the tensor-core
+// GEMM on layers up to 32 Mi weights (5120 x 5120 at M = 9 / 12 / 16: 11.9 / 12.9 / 14.8 us
+// against 16.9 / 16.9 / 17.1) and at 9 tokens on layers with K <= 8192 (17408 x 5120: 22.8
+// against 36.9 us); wider or deeper layers at more tokens keep the tensor cores.
+bool prefer_fp4_decode(int M, int N, int K) {
+    if (M < 1 || M > 16) return false;
+    if (M < kFp4PrefillMinM) return true;
+    return (long long)N * K <= 32LL * 1024 * 1024 || (M <= 9 && K <= 8192);
+}
+
+namespace {
+
 // One decode GEMM call: E stacked weight matrices, grp.n expert row groups (1 for a plain GEMM).
 struct Fp4Call {
     const uint16_t *a;

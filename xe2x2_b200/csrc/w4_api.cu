@@ -466,8 +466,8 @@ int w4_nvfp4_gemm(const void *a, const uint8_t *w, int layout, const void *scale
         if (rc || c_dtype != W4_E4M3) return rc;
         return w4::rowscale_fp8(out, W4_F32, static_cast<uint8_t *>(c), row_scale, M, N, st);
     }
-    // W4A16: the tensor-core GEMM from kFp4PrefillMinM tokens on (E4M3 block scales),
-    // else the decode kernels
+    // W4A16: the decode kernels up to 16 tokens where prefer_fp4_decode says so, else the
+    // tensor-core GEMM (E4M3 block scales)
     char *wsb = wsbase;
     void *out = c;
     int odt = c_dtype;
@@ -478,7 +478,7 @@ int w4_nvfp4_gemm(const void *a, const uint8_t *w, int layout, const void *scale
     }
     rc = -1;
     const size_t have = workspace_bytes - (size_t)(wsb - static_cast<char *>(workspace));
-    if (c_dtype == W4_E4M3 && M < w4::kFp4PrefillMinM && N % 8 == 0 && aligned(c, 8)) {
+    if (c_dtype == W4_E4M3 && w4::prefer_fp4_decode(M, N, K) && N % 8 == 0 && aligned(c, 8)) {
         // decode: the GEMM folds the row maxima of its f32 product into the sync area, so the
         // cast reads the product once
         unsigned int *sw = static_cast<unsigned int *>(workspace);

@@ -101,6 +101,9 @@ constexpr int kPrefillMinM = 17;  // token counts from here on run the tensor-co
 // NVFP4 W4A16: the two-token-tile decode kernel (M = 9..16) is slower than the tensor-core
 // GEMM, which therefore starts at 9 tokens
 constexpr int kFp4PrefillMinM = 9;
+// NVFP4 W4A16 calls of up to 16 tokens that run the decode kernel rather than the tensor-core
+// GEMM (nvfp4_decode.cu)
+bool prefer_fp4_decode(int M, int N, int K);
 int gptq_s4a(const uint8_t *a, const uint8_t *b, const float *a_scale, const uint16_t *s,
              uint16_t *c, int rows, int cols, int dk, cudaStream_t st);
 
