@@ -18,7 +18,7 @@
 // still reading, because each call waits for every peer's push of that call.
 // The counters live in device memory, so captured CUDA graphs replay correctly.
 // No copy here is a TMA or bulk load, and nothing uses multicast.
-// Messages up to 64 KB (decode-sized outputs) take a second form that needs
+// Messages up to 512 KB (decode-sized outputs) take a second form that needs
 // neither the fence nor the flags: every 4-byte word travels with the call
 // number in one 8-byte store and readers wait on the words themselves (see
 // ll_off).  The same buffer also carries the epilogue all-reduce of the fused
@@ -57,7 +57,7 @@ static size_t fctrl_off(int nranks) { return fflags_off(nranks) + 2 * (size_t)kF
 // reader takes a word once its v matches, so no fence or separate flag is needed (an aligned
 // 8-byte store is observed whole).  Layout: slots [2 parities][nranks][kLLSlotBytes], then
 // this rank's call sequence and finished-block count.
-constexpr size_t kLLMaxBytes = size_t(64) << 10;
+constexpr size_t kLLMaxBytes = size_t(512) << 10;
 constexpr size_t kLLSlotBytes = 2 * kLLMaxBytes;  // 8 bytes per 4-byte word
 constexpr int kLLWordsPerBlock = 2048;
 static size_t ll_off(int nranks) { return (fctrl_off(nranks) + 256 + 255) & ~size_t(255); }
